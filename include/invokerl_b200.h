@@ -1,0 +1,200 @@
+/*
+ * invokerl_b200 — C ABI of the B200 (sm_100a) kernels behind invokerl's training hot path.
+ *
+ * The hot path is invokerl's per-token log-prob computation (invokerl/policy.py:60-196) and
+ * the advantage/loss hooks of its algorithms (invokerl/algorithms/{base,grpo,dapo,ppo,simpo}.py).
+ * The reference is pure Python over PyTorch; the Python package `invokerl_b200` binds these
+ * entry points through ctypes and keeps the reference's Python interface.  Every entry point
+ * below names the reference code it replaces.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers, sizes and a `cudaStream_t` passed as `void* stream`; every launch is
+ *     ordered on that stream and nothing synchronises the host unless the comment says so.
+ *   - The library allocates no device memory: outputs and workspaces belong to the caller.  A
+ *     `*_workspace_bytes` function gives the workspace size where one is needed.
+ *   - Return value: IKRL_OK (0) or an IKRL_ERR_* code; `ikrl_last_error()` then holds a message
+ *     (thread-local).  No C++ exception crosses this boundary.
+ *   - Row-major tensors.  Masks are bool tensors read as bytes (0 / non-zero).
+ */
+#ifndef INVOKERL_B200_H_
+#define INVOKERL_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define IKRL_API __attribute__((visibility("default")))
+#else
+#define IKRL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  IKRL_OK = 0,
+  IKRL_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative or inconsistent size */
+  IKRL_ERR_ALIGNMENT = 2,        /* pointer or stride misses the alignment a kernel needs */
+  IKRL_ERR_UNSUPPORTED = 3,      /* dtype / shape combination the kernels do not cover */
+  IKRL_ERR_WORKSPACE = 4,        /* workspace missing or smaller than *_workspace_bytes() */
+  IKRL_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed (message has the name) */
+  IKRL_ERR_DEVICE = 6            /* a kernel recorded a device-side fault (bounded wait expired) */
+};
+
+enum { IKRL_DTYPE_F32 = 0, IKRL_DTYPE_BF16 = 1 };
+
+/* KL estimators of invokerl/algorithms/grpo.py:117-123. */
+enum { IKRL_KL_SCHULMAN = 0, IKRL_KL_SIMPLE = 1, IKRL_KL_NONE = 2 };
+
+/* Loss families that share the clipped-ratio kernel. */
+enum {
+  IKRL_LOSS_GRPO = 0, /* grpo.py:84-143 and dapo.py:90-150: L = sum((pl + beta*kl)*m)/n */
+  IKRL_LOSS_PPO = 1   /* ppo.py:108-184: L = pl_mean + vf_coef*vf + entropy term + kl term */
+};
+
+/* Number of doubles in the per-call sum vector (`sums`) of the clipped-ratio loss. */
+#define IKRL_LOSS_NSUMS 16
+/* Number of floats in the metrics vector of the clipped-ratio loss. */
+#define IKRL_LOSS_NMETRICS 12
+/* Number of floats in the metrics vector of SimPO. */
+#define IKRL_SIMPO_NMETRICS 8
+
+/* ---- library ---------------------------------------------------------------------------- */
+
+/* Last error message of the calling thread ("" when none). */
+IKRL_API const char* ikrl_last_error(void);
+/* ABI version; bumps whenever a signature below changes. */
+IKRL_API int ikrl_abi_version(void);
+
+/* ---- K3: advantages ------------------------------------------------------------------------ */
+
+/* Count of non-zero mask bytes -> *count_out (int64, device).  Feeds num_tokens =
+ * mask.sum().clamp(min=1) of grpo.py:127, dapo.py:105, ppo.py:121; with rows sharded over ranks
+ * the caller all-reduces this count before the loss.  Sets *count_out (no accumulation). */
+IKRL_API int ikrl_mask_count(const uint8_t* mask, int64_t n, int64_t* count_out, void* stream);
+
+/* Default credit assignment of invokerl/algorithms/base.py:86-110:
+ * adv[b,t] = rewards[b] * mask[b,t]. */
+IKRL_API int ikrl_broadcast_advantages(const float* rewards, const uint8_t* response_mask, int32_t B,
+                              int32_t T, float* adv_out, void* stream);
+
+/* Group-normalised sequence advantages, invokerl/algorithms/grpo.py:72-80 and
+ * dapo.py:55-88.  Groups are G contiguous rows (rewards.view(-1, G)); std is unbiased and
+ * clamped to >= 1e-8 (G == 1 gives NaN, as torch.std does).
+ *   filter_zero_var != 0: DAPO dynamic sampling, adv *= (std > 1e-8)          (dapo.py:69-74)
+ *   truncated != NULL  : adv = overlong_penalty where truncated[b]            (dapo.py:82-86)
+ * adv_out[b,t] = adv[b] * mask[b,t].  Optional row_adv_out[B] receives adv[b]. */
+IKRL_API int ikrl_group_advantages(const float* rewards, const uint8_t* response_mask,
+                          const uint8_t* truncated, int32_t B, int32_t T, int32_t G,
+                          int32_t filter_zero_var, float overlong_penalty, float* adv_out,
+                          float* row_adv_out, void* stream);
+
+/* Token-level group normalisation of grpo.py:62-70: per (group, position) mean and unbiased
+ * std over the G rows of token_rewards, adv = (tr - mean) / max(std, 1e-8) * mask. */
+IKRL_API int ikrl_token_group_advantages(const float* token_rewards, const uint8_t* response_mask,
+                                int32_t B, int32_t T, int32_t G, float* adv_out, void* stream);
+
+/* Masked mean and unbiased std of x over mask (ppo.py:123-127 whitening) -> out[0]=mean,
+ * out[1]=std, out[2]=count (float).  count < 2 leaves whitening off (out[3] = 0, else 1). */
+IKRL_API size_t ikrl_masked_moments_workspace_bytes(int64_t n);
+IKRL_API int ikrl_masked_moments(const float* x, const uint8_t* mask, int64_t n, float* out4, void* ws,
+                        size_t ws_bytes, void* stream);
+
+/* PPO generalised advantage estimation, invokerl/algorithms/ppo.py:80-106: one reverse scan per
+ * row.  rewards_bt != NULL uses token rewards; otherwise the sequence reward rewards_b[b] is
+ * placed at the last response token of row b.  values[b,t] are the value predictions.
+ * adv_out[b,t] = gae[b,t] * mask[b,t]. */
+IKRL_API int ikrl_gae_advantages(const float* rewards_b, const float* rewards_bt, const float* values,
+                        const uint8_t* response_mask, int32_t B, int32_t T, float gamma,
+                        float lam, float* adv_out, void* stream);
+
+/* ---- K3: clipped-ratio loss (GRPO / DAPO / PPO) ------------------------------------------- */
+
+typedef struct {
+  int32_t family;        /* IKRL_LOSS_GRPO or IKRL_LOSS_PPO */
+  float ratio_lo;        /* clamp lower bound: 1 - clip_eps (GRPO/PPO) or 1 - clip_eps_low */
+  float ratio_hi;        /* clamp upper bound: 1 + clip_eps (GRPO/PPO) or 1 + clip_eps_high */
+  float clip_metric_eps; /* clip_frac counts |ratio - 1| > clip_metric_eps */
+  float beta;            /* KL coefficient (0 disables the KL term and its gradient) */
+  int32_t kl_type;       /* IKRL_KL_* */
+  float entropy_coef;    /* PPO entropy bonus coefficient */
+  float vf_coef;         /* PPO value-loss coefficient */
+  float vf_clip_eps;     /* PPO value clipping */
+} ikrl_loss_params;
+
+/* Workspace of ikrl_clip_loss_fwd for n = B*T tokens. */
+IKRL_API size_t ikrl_clip_loss_workspace_bytes(int64_t n_tokens);
+
+/* One pass over the tokens of grpo.py:103-128 / dapo.py:108-128 / ppo.py:123-164.
+ * Inputs [B,T]: new_lp (fp32 or bf16, `lp_dtype`), old_lp, adv (fp32), mask (bytes);
+ * ref_lp (fp32, may be NULL when beta == 0); rewards [B] (for the "reward" metric and, with
+ * G > 0, the zero-variance group count of dapo.py:132-135).
+ * ntok: global token count (int64, device; max(ntok,1) is the normaliser n).
+ * whiten: NULL or the 4 floats of ikrl_masked_moments (PPO advantage whitening).
+ * values / old_values: NULL or [B,T] fp32 (PPO value loss, ppo.py:147-156).
+ * Outputs: dlp_out [B,T] (dtype of new_lp; NULL skips it) = d loss / d new_lp for an upstream
+ * gradient of 1;
+ * dvalues_out: NULL or [B,T] fp32 gradient of the value loss;
+ * sums_out[IKRL_LOSS_NSUMS] (double, device): the sums of this call's rows, reduced in a fixed
+ * order (bitwise reproducible): 0 pl*m, 1 kl*m, 2 clipped*m, 3 0.5*log_ratio^2*m,
+ * 4 sum of adv over masked tokens, 5 m, 6 lp*m, 7 value-loss max*m, 8 (pl+beta*kl)*m,
+ * 9 sum(rewards), 10 B, 11 zero-variance groups, 12 groups, 13-15 zero.  With rows sharded over
+ * ranks the caller all-reduces sums_out (SUM) before ikrl_clip_loss_finalize. */
+IKRL_API int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp,
+                                const float* ref_lp, const float* adv, const uint8_t* mask,
+                                const float* rewards, int32_t B, int32_t T, int32_t G,
+                                const int64_t* ntok, const float* whiten, const float* values,
+                                const float* old_values, const ikrl_loss_params* params,
+                                void* dlp_out, float* dvalues_out, double* sums_out, void* ws,
+                                size_t ws_bytes, void* stream);
+
+/* Turns sums into the loss value (loss_out[0]) and the metrics of grpo.py:131-141 /
+ * dapo.py:137-148 / ppo.py:170-182: metrics_out[IKRL_LOSS_NMETRICS] = loss, reward, kl,
+ * policy_loss, clip_frac, approx_kl, advantages_mean, entropy, vf_loss, num_tokens,
+ * zero_var_groups, num_groups.  One block of one launch; no host synchronisation. */
+IKRL_API int ikrl_clip_loss_finalize(const double* sums, const int64_t* ntok,
+                                     const ikrl_loss_params* params, float* loss_out,
+                                     float* metrics_out, void* stream);
+
+/* In-place g *= *scale (device scalar); returns at once on the device when *scale == 1.
+ * The backward of every loss above: d(upstream * loss)/d lp. */
+IKRL_API int ikrl_scale_grad(void* g, int32_t dtype, int64_t n, const float* scale, void* stream);
+
+/* ---- K3: SimPO (invokerl/algorithms/simpo.py:48-90) -------------------------------------- */
+
+/* Per-row masked mean of lp, pairwise -logsigmoid(beta*(chosen - rejected) - gamma), mean.
+ * loss_out[0]; metrics_out[IKRL_SIMPO_NMETRICS]: loss, reward, chosen_reward, rejected_reward,
+ * reward_accuracy, margin, avg_log_prob, num_pairs.  row_coef_out[B] = d loss / d lp[b,t] for
+ * masked tokens of row b (upstream 1).  B must be even.  rewards may be NULL ("reward" = 0). */
+IKRL_API size_t ikrl_simpo_workspace_bytes(int32_t B);
+IKRL_API int ikrl_simpo_fwd(const void* lp, int32_t lp_dtype, const uint8_t* mask, const float* rewards,
+                   int32_t B, int32_t T, float beta, float gamma, int32_t chosen_first,
+                   float* loss_out, float* metrics_out, float* row_coef_out, void* ws,
+                   size_t ws_bytes, void* stream);
+
+/* dlp[b,t] = row_coef[b] * mask[b,t] * (*scale). */
+IKRL_API int ikrl_simpo_bwd(const float* row_coef, const uint8_t* mask, int32_t B, int32_t T,
+                   const float* scale, void* dlp_out, int32_t dlp_dtype, void* stream);
+
+/* ---- K2: logits -> log-prob (unfused path) ------------------------------------------------ */
+
+/* Replaces -F.cross_entropy(logits, targets, reduction="none") of invokerl/policy.py:100-104
+ * and :151-155 (and the chunk of :187-191).  logits bf16 [N, ld] (row stride ld >= V, in
+ * elements), ids int64 [N] in [0, V).
+ * logp[N] fp32 = logits[r, ids[r]] - logsumexp(logits[r, :V]); lse[N] fp32 (saved for the
+ * backward); tgt_logit (nullable) = the gathered raw logit, bit-exact. */
+IKRL_API int ikrl_logits_logprob_fwd(const void* logits, int64_t ld, const int64_t* ids, int64_t N,
+                            int32_t V, float* logp, float* lse, float* tgt_logit, void* stream);
+
+/* Backward of the above: dlogits[r, v] = dlogp[r] * ([v == ids[r]] - exp(logits[r,v] - lse[r]))
+ * in bf16, row stride ld_out.  Rows with dlogp == 0 are written as zeros without reading. */
+IKRL_API int ikrl_logits_logprob_bwd(const void* logits, int64_t ld, const int64_t* ids, const float* lse,
+                            const float* dlogp, int64_t N, int32_t V, void* dlogits,
+                            int64_t ld_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INVOKERL_B200_H_ */

@@ -1,0 +1,747 @@
+// K3: the advantage and loss hooks of invokerl's algorithms as fused, memory-bound kernels.
+//
+//   group advantages      invokerl/algorithms/grpo.py:46-80, dapo.py:55-88, base.py:86-110
+//   clipped-ratio loss    invokerl/algorithms/grpo.py:84-143, dapo.py:90-150, ppo.py:108-184
+//   PPO whitening / GAE   invokerl/algorithms/ppo.py:65-106, :123-127
+//   SimPO                 invokerl/algorithms/simpo.py:44-90
+//
+// The reference runs each of these as 6-30 separate ATen launches plus one blocking .item()
+// per metric.  Here the per-token work of a loss is one pass over the tokens that also writes
+// d loss / d new_lp, and the metrics come out of a fixed-order (reproducible) reduction in the
+// same launch; the host reads them with a single copy.
+#include "common.cuh"
+
+namespace ikrl {
+namespace {
+
+constexpr int kLossThreads = 256;
+constexpr int kLossMaxBlocks = kNumSMs * 8;
+constexpr int kTokenSums = 9;  // sums[0..8] are per-token; [9..15] batch-level
+
+__host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// torch.min(a, b) forward value (NaN-propagating) and its backward weights (ties split 1/2).
+__device__ __forceinline__ void torch_min2(float a, float b, float& v, float& wa, float& wb) {
+  if (a < b) { v = a; wa = 1.f; wb = 0.f; }
+  else if (b < a) { v = b; wa = 0.f; wb = 1.f; }
+  else if (a == b) { v = a; wa = 0.5f; wb = 0.5f; }
+  else { v = __int_as_float(0x7fc00000); wa = 1.f; wb = 1.f; }
+}
+__device__ __forceinline__ void torch_max2(float a, float b, float& v, float& wa, float& wb) {
+  if (a > b) { v = a; wa = 1.f; wb = 0.f; }
+  else if (b > a) { v = b; wa = 0.f; wb = 1.f; }
+  else if (a == b) { v = a; wa = 0.5f; wb = 0.5f; }
+  else { v = __int_as_float(0x7fc00000); wa = 1.f; wb = 1.f; }
+}
+// torch.clamp(x, lo, hi) value (NaN stays NaN) and whether its gradient passes (closed range).
+__device__ __forceinline__ float torch_clamp(float x, float lo, float hi) {
+  return x != x ? x : fminf(fmaxf(x, lo), hi);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Advantages
+// ---------------------------------------------------------------------------------------------
+
+// mean and unbiased std of G values (double accumulation; G == 1 -> NaN like torch.std).
+__device__ inline void group_stats(const float* r, int G, double& mean, double& std_) {
+  double s = 0.0;
+  for (int j = 0; j < G; ++j) s += r[j];
+  mean = s / G;
+  double q = 0.0;
+  for (int j = 0; j < G; ++j) { double d = r[j] - mean; q += d * d; }
+  std_ = G > 1 ? sqrt(q / (G - 1)) : __longlong_as_double(0x7ff8000000000000ll);
+}
+
+__global__ void group_adv_kernel(const float* __restrict__ rewards, const uint8_t* __restrict__ mask,
+                                 const uint8_t* __restrict__ truncated, int B, int T, int G,
+                                 int filter_zero_var, float overlong_penalty, float* __restrict__ adv,
+                                 float* __restrict__ row_adv) {
+  const int b = blockIdx.x;
+  __shared__ float s_adv;
+  if (threadIdx.x == 0) {
+    const int g0 = (b / G) * G;
+    double mean, sd;
+    group_stats(rewards + g0, G, mean, sd);
+    const float meanf = (float)mean, sdf = (float)sd;
+    float a;
+    if (filter_zero_var) {
+      const float valid = (sdf > 1e-8f) ? 1.f : 0.f;
+      a = ((rewards[b] - meanf) / clamp_min_nan(sdf, 1e-8f)) * valid;
+    } else {
+      a = (rewards[b] - meanf) / clamp_min_nan(sdf, 1e-8f);
+    }
+    if (truncated != nullptr && truncated[b]) a = overlong_penalty;
+    s_adv = a;
+    if (row_adv) row_adv[b] = a;
+  }
+  __syncthreads();
+  const float a = s_adv;
+  const uint8_t* mrow = mask + (int64_t)b * T;
+  float* arow = adv + (int64_t)b * T;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) arow[t] = a * (mrow[t] ? 1.f : 0.f);
+}
+
+__global__ void broadcast_adv_kernel(const float* __restrict__ rewards, const uint8_t* __restrict__ mask,
+                                     int B, int T, float* __restrict__ adv) {
+  const int b = blockIdx.x;
+  const float a = rewards[b];
+  const uint8_t* mrow = mask + (int64_t)b * T;
+  float* arow = adv + (int64_t)b * T;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) arow[t] = a * (mrow[t] ? 1.f : 0.f);
+}
+
+// One thread per (group, position): normalise the G token rewards of that column.
+__global__ void token_group_adv_kernel(const float* __restrict__ tr, const uint8_t* __restrict__ mask,
+                                       int B, int T, int G, float* __restrict__ adv) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t ngroups = B / G;
+  if (i >= ngroups * T) return;
+  const int64_t g = i / T, t = i % T;
+  const float* base = tr + g * G * (int64_t)T + t;
+  double s = 0.0;
+  for (int j = 0; j < G; ++j) s += base[(int64_t)j * T];
+  const double mean = s / G;
+  double q = 0.0;
+  for (int j = 0; j < G; ++j) { double d = base[(int64_t)j * T] - mean; q += d * d; }
+  const float sdf = G > 1 ? (float)sqrt(q / (G - 1)) : __int_as_float(0x7fc00000);
+  const float meanf = (float)mean, den = clamp_min_nan(sdf, 1e-8f);
+  for (int j = 0; j < G; ++j) {
+    const int64_t o = (g * G + j) * (int64_t)T + t;
+    adv[o] = ((tr[o] - meanf) / den) * (mask[o] ? 1.f : 0.f);
+  }
+}
+
+__global__ void mask_count_kernel(const uint8_t* __restrict__ mask, int64_t n,
+                                  unsigned long long* __restrict__ out) {
+  unsigned long long c = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t n16 = ((reinterpret_cast<uintptr_t>(mask) & 15) == 0) ? n / 16 : 0;
+  const uint4* m4 = reinterpret_cast<const uint4*>(mask);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) {
+    uint4 v = __ldg(m4 + i);
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      // count non-zero bytes
+      uint32_t x = w[k];
+      x = (x | (x >> 1) | (x >> 2) | (x >> 3) | (x >> 4) | (x >> 5) | (x >> 6) | (x >> 7)) & 0x01010101u;
+      c += __popc(x);
+    }
+  }
+  for (int64_t i = n16 * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    c += mask[i] ? 1 : 0;
+  c = warp_sum(c);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(out, c);
+}
+
+// ---- PPO whitening moments (two passes, fixed order) --------------------------------------
+
+__global__ void moments_pass_kernel(const float* __restrict__ x, const uint8_t* __restrict__ mask,
+                                    int64_t n, int pass, float* __restrict__ out4,
+                                    double* __restrict__ partials, unsigned* __restrict__ ticket) {
+  __shared__ double scratch[2 * 32];
+  __shared__ bool am_last;
+  double v[2] = {0.0, 0.0};
+  const double mean = pass == 1 ? (double)out4[0] : 0.0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    if (mask[i]) {
+      if (pass == 0) { v[0] += x[i]; v[1] += 1.0; }
+      else { double d = (double)x[i] - mean; v[0] += d * d; }
+    }
+  }
+  block_sum<double, 2>(v, scratch);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x * 2 + 0] = v[0];
+    partials[blockIdx.x * 2 + 1] = v[1];
+    __threadfence();
+    am_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (am_last && threadIdx.x == 0) {
+    __threadfence();
+    double a = 0.0, c = 0.0;
+    for (unsigned b = 0; b < gridDim.x; ++b) { a += __ldcg(partials + 2 * b); c += __ldcg(partials + 2 * b + 1); }
+    if (pass == 0) {
+      out4[2] = (float)c;
+      out4[0] = c > 0 ? (float)(a / c) : __int_as_float(0x7fc00000);
+      out4[3] = c > 1 ? 1.f : 0.f;
+    } else {
+      const double cnt = out4[2];
+      out4[1] = cnt > 1 ? (float)sqrt(a / (cnt - 1)) : __int_as_float(0x7fc00000);
+    }
+    *ticket = 0;
+  }
+}
+
+// ---- PPO GAE reverse scan ------------------------------------------------------------------
+// x_t = delta_t + c_t * x_{t+1} with c_t = gamma*lambda*mask_t and x_T = 0 (ppo.py:96-104).
+// One block per row; each thread owns a contiguous chunk, composes its chunk into one affine
+// map, a block scan from the right combines the chunks, and a second sweep writes the values.
+constexpr int kGaeThreads = 256;
+
+__global__ void gae_kernel(const float* __restrict__ rewards_b, const float* __restrict__ rewards_bt,
+                           const float* __restrict__ values, const uint8_t* __restrict__ mask, int T,
+                           float gamma, float lam, float* __restrict__ adv) {
+  const int b = blockIdx.x;
+  const uint8_t* mrow = mask + (int64_t)b * T;
+  const float* vrow = values + (int64_t)b * T;
+  float* arow = adv + (int64_t)b * T;
+  __shared__ int s_last;
+  __shared__ float s_A[kGaeThreads], s_B[kGaeThreads];
+  // Last response token of the row (sequence reward placement, ppo.py:91-94).
+  if (threadIdx.x == 0) s_last = -1;
+  __syncthreads();
+  if (rewards_bt == nullptr) {
+    int last = -1;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) if (mrow[t]) last = max(last, t);
+    atomicMax(&s_last, last);
+  }
+  __syncthreads();
+  const int last = s_last;
+  const float gl = gamma * lam;
+  const int chunk = (T + blockDim.x - 1) / blockDim.x;
+  const int t0 = threadIdx.x * chunk, t1 = min(T, t0 + chunk);
+  auto reward_at = [&](int t) -> float {
+    if (rewards_bt) return rewards_bt[(int64_t)b * T + t];
+    return t == last ? rewards_b[b] : 0.f;
+  };
+  // Compose the chunk: x_{t0} = Bc + Ac * x_{t1}.
+  float Ac = 1.f, Bc = 0.f;
+  for (int t = t1 - 1; t >= t0; --t) {
+    const float nv = (t == T - 1) ? 0.f : vrow[t + 1];
+    const float delta = reward_at(t) + gamma * nv - vrow[t];
+    const float c = gl * (mrow[t] ? 1.f : 0.f);
+    Bc = delta + c * Bc;
+    Ac = c * Ac;
+  }
+  s_A[threadIdx.x] = Ac;
+  s_B[threadIdx.x] = Bc;
+  __syncthreads();
+  // Serial combine of the per-thread maps from the right (256 steps, one thread).
+  __shared__ float s_in[kGaeThreads];
+  if (threadIdx.x == 0) {
+    float x = 0.f;
+    for (int k = blockDim.x - 1; k >= 0; --k) {
+      s_in[k] = x;  // value x_{t1} entering chunk k
+      x = s_B[k] + s_A[k] * x;
+    }
+  }
+  __syncthreads();
+  float x = s_in[threadIdx.x];
+  for (int t = t1 - 1; t >= t0; --t) {
+    const float nv = (t == T - 1) ? 0.f : vrow[t + 1];
+    const float delta = reward_at(t) + gamma * nv - vrow[t];
+    const float m = mrow[t] ? 1.f : 0.f;
+    x = delta + gl * x * m;
+    arow[t] = x * m;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Clipped-ratio loss: one pass, d loss / d lp written in the same pass.
+// ---------------------------------------------------------------------------------------------
+
+struct LossArgs {
+  const void* new_lp;
+  const float* old_lp;
+  const float* ref_lp;
+  const float* adv;
+  const uint8_t* mask;
+  const int64_t* ntok;
+  const float* whiten;
+  const float* values;
+  const float* old_values;
+  const float* rewards;
+  int B, G;
+  void* dlp;
+  float* dvalues;
+  double* partials;
+  unsigned* ticket;
+  double* sums;
+  int64_t n;
+  ikrl_loss_params p;
+};
+
+template <bool BF16>
+__device__ __forceinline__ float load_lp(const void* p, int64_t i) {
+  if constexpr (BF16) return bf16_to_f32(reinterpret_cast<const uint16_t*>(p)[i]);
+  else return reinterpret_cast<const float*>(p)[i];
+}
+template <bool BF16>
+__device__ __forceinline__ void store_lp(void* p, int64_t i, float v) {
+  if constexpr (BF16) reinterpret_cast<uint16_t*>(p)[i] = f32_to_bf16_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// Per-token body shared by the scalar and vector paths.  acc[] are the masked sums:
+//  0 pl*m  1 kl*m  2 clipped*m  3 0.5*lr^2*m  4 adv (masked select)  5 m  6 lp*m  7 vmax*m
+//  8 token_loss*m (GRPO)
+template <int FAMILY>
+__device__ __forceinline__ float token_step(const LossArgs& a, float lp, float old, float ref,
+                                            float adv, uint8_t mk, float inv_n, float wmean,
+                                            float wstd, bool whiten_on, float vv, float ov,
+                                            float& dval, float (&acc)[kTokenSums]) {
+  const ikrl_loss_params& p = a.p;
+  const float m = mk ? 1.f : 0.f;
+  if (whiten_on) adv = ((adv - wmean) / (wstd + 1e-8f)) * m;
+  const float lr = lp - old;
+  const float rho = expf(lr);
+  const float s1 = rho * adv;
+  const float rc = torch_clamp(rho, p.ratio_lo, p.ratio_hi);
+  const float s2 = rc * adv;
+  float mn, w1, w2;
+  torch_min2(s1, s2, mn, w1, w2);
+  const float pl = -mn;
+  const float inb = (rho >= p.ratio_lo && rho <= p.ratio_hi) ? 1.f : 0.f;
+  // d pl / d lp  (grad_rho = w1*A + w2*A*inb; exp backward multiplies by rho)
+  const float dpl = -((w1 * adv + w2 * (adv * inb)) * rho);
+
+  float kl = 0.f, dkl = 0.f;
+  const bool has_kl = (a.ref_lp != nullptr) && (p.kl_type != IKRL_KL_NONE) &&
+                      (FAMILY == IKRL_LOSS_GRPO || p.beta > 0.f);
+  if (has_kl) {
+    const float lrr = ref - lp;
+    if (p.kl_type == IKRL_KL_SCHULMAN) {
+      const float e = expf(lrr);
+      kl = e - lrr - 1.f;
+      dkl = 1.f - e;
+    } else {
+      kl = -lrr;
+      dkl = 1.f;
+    }
+  }
+  const float g = m * inv_n;  // d (sum(x*m)/n) / d x
+  float dlp;
+  acc[0] += pl * m;
+  acc[1] += kl * m;
+  acc[2] += (fabsf(rho - 1.f) > p.clip_metric_eps ? 1.f : 0.f) * m;
+  acc[3] += (0.5f * (lr * lr)) * m;
+  if (mk) acc[4] += adv;
+  acc[5] += m;
+  acc[6] += lp * m;
+  if constexpr (FAMILY == IKRL_LOSS_GRPO) {
+    const float tl = pl + p.beta * kl;
+    acc[8] += tl * m;
+    dlp = g * dpl + (g * p.beta) * dkl;
+  } else {
+    dlp = g * dpl + p.entropy_coef * g;
+    if (has_kl) dlp += (p.beta * g) * dkl;
+    if (a.values != nullptr) {
+      const float ret = adv + ov;
+      const float dv = vv - ov;
+      const float vclip = ov + torch_clamp(dv, -p.vf_clip_eps, p.vf_clip_eps);
+      const float e1 = vv - ret, e2 = vclip - ret;
+      const float l1 = e1 * e1, l2 = e2 * e2;
+      float vmax, u1, u2;
+      torch_max2(l1, l2, vmax, u1, u2);
+      acc[7] += vmax * m;
+      const float vinb = (dv >= -p.vf_clip_eps && dv <= p.vf_clip_eps) ? 1.f : 0.f;
+      const float gv = p.vf_coef * 0.5f * g;
+      dval = gv * (u1 * 2.f * e1 + u2 * 2.f * e2 * vinb);
+    }
+  }
+  return dlp;
+}
+
+template <int FAMILY, bool BF16>
+__global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
+  __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
+  __shared__ bool am_last;
+  float acc[kTokenSums];
+#pragma unroll
+  for (int i = 0; i < kTokenSums; ++i) acc[i] = 0.f;
+
+  const float inv_n = 1.f / fmaxf((float)(*a.ntok), 1.f);
+  const bool whiten_on = a.whiten != nullptr && a.whiten[3] != 0.f;
+  const float wmean = whiten_on ? a.whiten[0] : 0.f, wstd = whiten_on ? a.whiten[1] : 0.f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    const float lp = load_lp<BF16>(a.new_lp, i);
+    const float old = __ldg(a.old_lp + i);
+    const float ref = a.ref_lp ? __ldg(a.ref_lp + i) : 0.f;
+    const float adv = __ldg(a.adv + i);
+    const uint8_t mk = __ldg(a.mask + i);
+    const float vv = a.values ? __ldg(a.values + i) : 0.f;
+    const float ov = a.values ? __ldg(a.old_values + i) : 0.f;
+    float dval = 0.f;
+    const float d = token_step<FAMILY>(a, lp, old, ref, adv, mk, inv_n, wmean, wstd, whiten_on,
+                                       vv, ov, dval, acc);
+    if (a.dlp) store_lp<BF16>(a.dlp, i, d);
+    if (a.dvalues) a.dvalues[i] = dval;
+  }
+
+  double v[kTokenSums];
+#pragma unroll
+  for (int i = 0; i < kTokenSums; ++i) v[i] = (double)acc[i];
+  block_sum<double, kTokenSums>(v, scratch);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < kTokenSums; ++i) a.partials[(int64_t)blockIdx.x * IKRL_LOSS_NSUMS + i] = v[i];
+    __threadfence();
+    am_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (am_last) {
+    __threadfence();
+    if (threadIdx.x < kTokenSums) {
+      double s = 0.0;
+      for (unsigned b = 0; b < gridDim.x; ++b) s += __ldcg(a.partials + (int64_t)b * IKRL_LOSS_NSUMS + threadIdx.x);
+      a.sums[threadIdx.x] = s;
+    }
+    // Batch-level terms: rewards.mean() and the zero-variance group count (dapo.py:132-135).
+    double r[2] = {0.0, 0.0};
+    for (int b = threadIdx.x; b < a.B; b += blockDim.x) r[0] += a.rewards[b];
+    if (a.G > 0) {
+      for (int g = threadIdx.x; g < a.B / a.G; g += blockDim.x) {
+        double mean, sd;
+        group_stats(a.rewards + g * a.G, a.G, mean, sd);
+        if ((float)sd < 1e-8f) r[1] += 1.0;
+      }
+    }
+    block_sum<double, 2>(r, scratch);
+    if (threadIdx.x == 0) {
+      a.sums[9] = r[0];
+      a.sums[10] = (double)a.B;
+      a.sums[11] = r[1];
+      a.sums[12] = a.G > 0 ? (double)(a.B / a.G) : 0.0;
+      a.sums[13] = a.sums[14] = a.sums[15] = 0.0;
+      *a.ticket = 0;
+    }
+  }
+}
+
+__global__ void clip_loss_finalize_kernel(const double* __restrict__ s, const int64_t* __restrict__ ntok,
+                                          ikrl_loss_params p, float* __restrict__ loss_out,
+                                          float* __restrict__ metrics) {
+  if (threadIdx.x != 0) return;
+  const double n = fmax((double)(float)(*ntok), 1.0);
+  const float nf = (float)n;
+  double loss;
+  const double pl = s[0] / n, kl = s[1] / n, entropy = -s[6] / n;
+  if (p.family == IKRL_LOSS_GRPO) {
+    loss = (float)(s[8]) / nf;
+  } else {
+    const float plm = (float)s[0] / nf;
+    const float vf = 0.5f * (float)s[7] / nf;
+    const float ent = -((float)s[6]) / nf;
+    float l = plm + p.vf_coef * vf + (-p.entropy_coef * ent);
+    if (p.beta > 0.f) l += p.beta * ((float)s[1] / nf);
+    loss = l;
+  }
+  loss_out[0] = (float)loss;
+  metrics[0] = (float)loss;
+  metrics[1] = s[10] > 0 ? (float)(s[9] / s[10]) : __int_as_float(0x7fc00000);
+  metrics[2] = (float)kl;
+  metrics[3] = (float)pl;
+  metrics[4] = (float)(s[2] / n);
+  metrics[5] = (float)(s[3] / n);
+  metrics[6] = s[5] > 0 ? (float)(s[4] / s[5]) : 0.f;
+  metrics[7] = (float)entropy;
+  metrics[8] = (float)(0.5 * s[7] / n);
+  metrics[9] = (float)n;
+  metrics[10] = (float)s[11];
+  metrics[11] = (float)s[12];
+}
+
+template <bool BF16>
+__global__ void scale_grad_kernel(void* g, int64_t n, const float* __restrict__ scale) {
+  const float s = *scale;
+  if (s == 1.f) return;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    if constexpr (BF16) {
+      uint16_t* p = reinterpret_cast<uint16_t*>(g);
+      p[i] = f32_to_bf16_rn(bf16_to_f32(p[i]) * s);
+    } else {
+      float* p = reinterpret_cast<float*>(g);
+      p[i] = p[i] * s;
+    }
+  }
+}
+
+// ---- SimPO -----------------------------------------------------------------------------------
+
+template <bool BF16>
+__global__ void simpo_rows_kernel(const void* lp, const uint8_t* __restrict__ mask, int T,
+                                  float* __restrict__ avg, float* __restrict__ len) {
+  __shared__ float scratch[2 * 32];
+  const int b = blockIdx.x;
+  float v[2] = {0.f, 0.f};
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const int64_t i = (int64_t)b * T + t;
+    const float m = mask[i] ? 1.f : 0.f;
+    v[0] += load_lp<BF16>(lp, i) * m;
+    v[1] += m;
+  }
+  block_sum<float, 2>(v, scratch);
+  if (threadIdx.x == 0) {
+    const float l = fmaxf(v[1], 1.f);
+    len[b] = l;
+    avg[b] = v[0] / l;
+  }
+}
+
+__device__ __forceinline__ float log_sigmoid(float x) {
+  // log(sigmoid(x)) = min(x, 0) - log1p(exp(-|x|))
+  return fminf(x, 0.f) - log1pf(expf(-fabsf(x)));
+}
+
+__global__ void simpo_pairs_kernel(const float* __restrict__ avg, const float* __restrict__ len,
+                                   const float* __restrict__ rewards, int B, float beta, float gamma,
+                                   int chosen_first, float* __restrict__ loss_out,
+                                   float* __restrict__ metrics, float* __restrict__ row_coef) {
+  __shared__ double scratch[6 * 32];
+  const int P = B / 2;
+  double v[6] = {0, 0, 0, 0, 0, 0};
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const int ic = chosen_first ? 2 * i : 2 * i + 1;
+    const int ir = chosen_first ? 2 * i + 1 : 2 * i;
+    const float c = avg[ic], r = avg[ir];
+    const float margin = beta * (c - r) - gamma;
+    v[0] += -log_sigmoid(margin);
+    v[1] += c;
+    v[2] += r;
+    v[3] += (c > r) ? 1.0 : 0.0;
+    v[4] += margin;
+    // d(-logsigmoid(m))/dm = sigmoid(m) - 1, mean over P pairs
+    const float dm = (1.f / (1.f + expf(-margin)) - 1.f) / (float)P;
+    row_coef[ic] = beta * dm / len[ic];
+    row_coef[ir] = -beta * dm / len[ir];
+  }
+  for (int b = threadIdx.x; b < B; b += blockDim.x) v[5] += avg[b];
+  block_sum<double, 6>(v, scratch);
+  if (threadIdx.x == 0) {
+    double r = 0.0;
+    for (int b = 0; b < B; ++b) r += rewards ? rewards[b] : 0.0;
+    const float loss = (float)(v[0] / P);
+    loss_out[0] = loss;
+    metrics[0] = loss;
+    metrics[1] = rewards ? (float)(r / B) : 0.f;
+    metrics[2] = (float)(v[1] / P);
+    metrics[3] = (float)(v[2] / P);
+    metrics[4] = (float)(v[3] / P);
+    metrics[5] = (float)(v[4] / P);
+    metrics[6] = (float)(v[5] / B);
+    metrics[7] = (float)P;
+  }
+}
+
+template <bool BF16>
+__global__ void simpo_bwd_kernel(const float* __restrict__ row_coef, const uint8_t* __restrict__ mask,
+                                 int T, const float* __restrict__ scale, void* dlp) {
+  const int b = blockIdx.x;
+  const float c = row_coef[b] * *scale;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const int64_t i = (int64_t)b * T + t;
+    store_lp<BF16>(dlp, i, c * (mask[i] ? 1.f : 0.f));
+  }
+}
+
+int loss_grid(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, kLossThreads), kLossMaxBlocks)); }
+
+}  // namespace
+}  // namespace ikrl
+
+using namespace ikrl;
+
+extern "C" {
+
+int ikrl_mask_count(const uint8_t* mask, int64_t n, int64_t* count_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(count_out != nullptr && n >= 0 && (n == 0 || mask != nullptr), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_mask_count: bad arguments (n=%lld)", (long long)n);
+  cudaStream_t s = as_stream(stream);
+  IKRL_CUDA(cudaMemsetAsync(count_out, 0, sizeof(int64_t), s));
+  if (n == 0) return IKRL_OK;
+  const int grid = (int)std::min<int64_t>(kNumSMs * 4, cdiv(cdiv(n, 16), 256));
+  mask_count_kernel<<<std::max(grid, 1), 256, 0, s>>>(mask, n, reinterpret_cast<unsigned long long*>(count_out));
+  return check_launch("mask_count_kernel");
+}
+
+int ikrl_broadcast_advantages(const float* rewards, const uint8_t* response_mask, int32_t B, int32_t T,
+                              float* adv_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B >= 0 && T >= 0 && (B == 0 || (rewards && response_mask && adv_out)), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_broadcast_advantages: bad arguments");
+  if ((int64_t)B * T == 0) return IKRL_OK;
+  broadcast_adv_kernel<<<B, 256, 0, as_stream(stream)>>>(rewards, response_mask, B, T, adv_out);
+  return check_launch("broadcast_adv_kernel");
+}
+
+int ikrl_group_advantages(const float* rewards, const uint8_t* response_mask, const uint8_t* truncated,
+                          int32_t B, int32_t T, int32_t G, int32_t filter_zero_var, float overlong_penalty,
+                          float* adv_out, float* row_adv_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B >= 0 && T >= 0 && G >= 1, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_group_advantages: bad sizes B=%d T=%d G=%d", B, T, G);
+  IKRL_REQUIRE(B % G == 0, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_group_advantages: B=%d is not a multiple of group_size G=%d", B, G);
+  if (B == 0) return IKRL_OK;
+  IKRL_REQUIRE(rewards && response_mask && adv_out, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_group_advantages: null pointer");
+  group_adv_kernel<<<B, 256, 0, as_stream(stream)>>>(rewards, response_mask, truncated, B, T, G,
+                                                    filter_zero_var, overlong_penalty, adv_out, row_adv_out);
+  return check_launch("group_adv_kernel");
+}
+
+int ikrl_token_group_advantages(const float* token_rewards, const uint8_t* response_mask, int32_t B,
+                                int32_t T, int32_t G, float* adv_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B >= 0 && T >= 0 && G >= 1 && B % G == 0, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_token_group_advantages: bad sizes B=%d T=%d G=%d", B, T, G);
+  const int64_t work = (int64_t)(B / G) * T;
+  if (work == 0) return IKRL_OK;
+  IKRL_REQUIRE(token_rewards && response_mask && adv_out, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_token_group_advantages: null pointer");
+  token_group_adv_kernel<<<(unsigned)cdiv(work, 256), 256, 0, as_stream(stream)>>>(token_rewards, response_mask,
+                                                                                   B, T, G, adv_out);
+  return check_launch("token_group_adv_kernel");
+}
+
+size_t ikrl_masked_moments_workspace_bytes(int64_t n) {
+  (void)n;
+  return 256 + (size_t)kNumSMs * 2 * 2 * sizeof(double);
+}
+
+int ikrl_masked_moments(const float* x, const uint8_t* mask, int64_t n, float* out4, void* ws, size_t ws_bytes,
+                        void* stream) {
+  clear_error();
+  IKRL_REQUIRE(n >= 0 && out4 && (n == 0 || (x && mask)), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_masked_moments: bad arguments");
+  IKRL_REQUIRE(ws != nullptr && ws_bytes >= ikrl_masked_moments_workspace_bytes(n), IKRL_ERR_WORKSPACE,
+               "ikrl_masked_moments: workspace too small (%zu < %zu)", ws_bytes,
+               ikrl_masked_moments_workspace_bytes(n));
+  cudaStream_t s = as_stream(stream);
+  unsigned* ticket = reinterpret_cast<unsigned*>(ws);
+  double* partials = reinterpret_cast<double*>(reinterpret_cast<char*>(ws) + 256);
+  IKRL_CUDA(cudaMemsetAsync(ticket, 0, sizeof(unsigned), s));
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(kNumSMs * 2, cdiv(n, 256)));
+  moments_pass_kernel<<<grid, 256, 0, s>>>(x, mask, n, 0, out4, partials, ticket);
+  int rc = check_launch("moments_pass_kernel");
+  if (rc) return rc;
+  moments_pass_kernel<<<grid, 256, 0, s>>>(x, mask, n, 1, out4, partials, ticket);
+  return check_launch("moments_pass_kernel");
+}
+
+int ikrl_gae_advantages(const float* rewards_b, const float* rewards_bt, const float* values,
+                        const uint8_t* response_mask, int32_t B, int32_t T, float gamma, float lam,
+                        float* adv_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B >= 0 && T >= 0, IKRL_ERR_INVALID_ARGUMENT, "ikrl_gae_advantages: bad sizes");
+  if ((int64_t)B * T == 0) return IKRL_OK;
+  IKRL_REQUIRE(values && response_mask && adv_out && (rewards_b || rewards_bt), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_gae_advantages: null pointer");
+  gae_kernel<<<B, kGaeThreads, 0, as_stream(stream)>>>(rewards_b, rewards_bt, values, response_mask, T, gamma,
+                                                      lam, adv_out);
+  return check_launch("gae_kernel");
+}
+
+size_t ikrl_clip_loss_workspace_bytes(int64_t n_tokens) {
+  return 256 + (size_t)loss_grid(n_tokens) * IKRL_LOSS_NSUMS * sizeof(double);
+}
+
+int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp, const float* ref_lp,
+                       const float* adv, const uint8_t* mask, const float* rewards, int32_t B, int32_t T,
+                       int32_t G, const int64_t* ntok,
+                       const float* whiten, const float* values, const float* old_values,
+                       const ikrl_loss_params* params, void* dlp_out, float* dvalues_out, double* sums_out,
+                       void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  const int64_t n = (int64_t)B * T;
+  IKRL_REQUIRE(B >= 0 && T >= 0 && params && ntok && sums_out && (B == 0 || rewards), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_clip_loss_fwd: bad arguments");
+  IKRL_REQUIRE(G <= 0 || B % G == 0, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_clip_loss_fwd: B=%d not a multiple of group_size G=%d", B, G);
+  IKRL_REQUIRE(n == 0 || (new_lp && old_lp && adv && mask), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_clip_loss_fwd: null tensor pointer");
+  IKRL_REQUIRE(lp_dtype == IKRL_DTYPE_F32 || lp_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
+               "ikrl_clip_loss_fwd: lp_dtype %d unsupported", lp_dtype);
+  IKRL_REQUIRE(params->family == IKRL_LOSS_GRPO || params->family == IKRL_LOSS_PPO, IKRL_ERR_UNSUPPORTED,
+               "ikrl_clip_loss_fwd: loss family %d unsupported", params->family);
+  IKRL_REQUIRE((values == nullptr) == (old_values == nullptr), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_clip_loss_fwd: values and old_values must both be given or both be NULL");
+  IKRL_REQUIRE(ws != nullptr && ws_bytes >= ikrl_clip_loss_workspace_bytes(n), IKRL_ERR_WORKSPACE,
+               "ikrl_clip_loss_fwd: workspace too small (%zu < %zu)", ws_bytes, ikrl_clip_loss_workspace_bytes(n));
+  cudaStream_t s = as_stream(stream);
+  LossArgs a;
+  a.new_lp = new_lp; a.old_lp = old_lp; a.ref_lp = ref_lp; a.adv = adv; a.mask = mask; a.ntok = ntok;
+  a.rewards = rewards; a.B = B; a.G = G;
+  a.whiten = whiten; a.values = values; a.old_values = old_values; a.dlp = dlp_out; a.dvalues = dvalues_out;
+  a.ticket = reinterpret_cast<unsigned*>(ws);
+  a.partials = reinterpret_cast<double*>(reinterpret_cast<char*>(ws) + 256);
+  a.sums = sums_out; a.n = n; a.p = *params;
+  IKRL_CUDA(cudaMemsetAsync(a.ticket, 0, sizeof(unsigned), s));
+  const int grid = loss_grid(n);
+  const bool bf = lp_dtype == IKRL_DTYPE_BF16;
+  if (params->family == IKRL_LOSS_GRPO) {
+    if (bf) clip_loss_kernel<IKRL_LOSS_GRPO, true><<<grid, kLossThreads, 0, s>>>(a);
+    else clip_loss_kernel<IKRL_LOSS_GRPO, false><<<grid, kLossThreads, 0, s>>>(a);
+  } else {
+    if (bf) clip_loss_kernel<IKRL_LOSS_PPO, true><<<grid, kLossThreads, 0, s>>>(a);
+    else clip_loss_kernel<IKRL_LOSS_PPO, false><<<grid, kLossThreads, 0, s>>>(a);
+  }
+  return check_launch("clip_loss_kernel");
+}
+
+int ikrl_clip_loss_finalize(const double* sums, const int64_t* ntok, const ikrl_loss_params* params,
+                            float* loss_out, float* metrics_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(sums && ntok && params && loss_out && metrics_out, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_clip_loss_finalize: bad arguments");
+  clip_loss_finalize_kernel<<<1, 32, 0, as_stream(stream)>>>(sums, ntok, *params, loss_out, metrics_out);
+  return check_launch("clip_loss_finalize_kernel");
+}
+
+int ikrl_scale_grad(void* g, int32_t dtype, int64_t n, const float* scale, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(n >= 0 && scale && (n == 0 || g), IKRL_ERR_INVALID_ARGUMENT, "ikrl_scale_grad: bad arguments");
+  IKRL_REQUIRE(dtype == IKRL_DTYPE_F32 || dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
+               "ikrl_scale_grad: dtype %d unsupported", dtype);
+  if (n == 0) return IKRL_OK;
+  const int grid = (int)std::min<int64_t>(kNumSMs * 8, cdiv(n, 256));
+  if (dtype == IKRL_DTYPE_BF16) scale_grad_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(g, n, scale);
+  else scale_grad_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(g, n, scale);
+  return check_launch("scale_grad_kernel");
+}
+
+size_t ikrl_simpo_workspace_bytes(int32_t B) { return (size_t)(B > 0 ? B : 0) * 2 * sizeof(float) + 256; }
+
+int ikrl_simpo_fwd(const void* lp, int32_t lp_dtype, const uint8_t* mask, const float* rewards, int32_t B,
+                   int32_t T, float beta, float gamma, int32_t chosen_first, float* loss_out, float* metrics_out,
+                   float* row_coef_out, void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B > 0 && T >= 0 && B % 2 == 0, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_simpo_fwd: B=%d must be positive and even (chosen/rejected pairs)", B);
+  IKRL_REQUIRE(lp && mask && loss_out && metrics_out && row_coef_out, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_simpo_fwd: null pointer");
+  IKRL_REQUIRE(lp_dtype == IKRL_DTYPE_F32 || lp_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
+               "ikrl_simpo_fwd: lp_dtype %d unsupported", lp_dtype);
+  IKRL_REQUIRE(ws && ws_bytes >= ikrl_simpo_workspace_bytes(B), IKRL_ERR_WORKSPACE,
+               "ikrl_simpo_fwd: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  float* avg = reinterpret_cast<float*>(ws);
+  float* len = avg + B;
+  if (lp_dtype == IKRL_DTYPE_BF16) simpo_rows_kernel<true><<<B, 256, 0, s>>>(lp, mask, T, avg, len);
+  else simpo_rows_kernel<false><<<B, 256, 0, s>>>(lp, mask, T, avg, len);
+  int rc = check_launch("simpo_rows_kernel");
+  if (rc) return rc;
+  simpo_pairs_kernel<<<1, 256, 0, s>>>(avg, len, rewards, B, beta, gamma, chosen_first, loss_out, metrics_out,
+                                       row_coef_out);
+  return check_launch("simpo_pairs_kernel");
+}
+
+int ikrl_simpo_bwd(const float* row_coef, const uint8_t* mask, int32_t B, int32_t T, const float* scale,
+                   void* dlp_out, int32_t dlp_dtype, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B >= 0 && T >= 0 && scale && (B == 0 || (row_coef && mask && dlp_out)), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_simpo_bwd: bad arguments");
+  IKRL_REQUIRE(dlp_dtype == IKRL_DTYPE_F32 || dlp_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
+               "ikrl_simpo_bwd: dtype %d unsupported", dlp_dtype);
+  if ((int64_t)B * T == 0) return IKRL_OK;
+  if (dlp_dtype == IKRL_DTYPE_BF16) simpo_bwd_kernel<true><<<B, 256, 0, as_stream(stream)>>>(row_coef, mask, T, scale, dlp_out);
+  else simpo_bwd_kernel<false><<<B, 256, 0, as_stream(stream)>>>(row_coef, mask, T, scale, dlp_out);
+  return check_launch("simpo_bwd_kernel");
+}
+
+}  // extern "C"

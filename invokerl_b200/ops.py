@@ -1,0 +1,344 @@
+"""PyTorch-facing ops over the C ABI: plain functions for the advantage kernels and
+``torch.autograd.Function`` s for the losses and the log-prob kernels.
+
+Every op checks that its tensors are on a CUDA device and calls the native library on the
+current stream; nothing here computes on the CPU or falls back to ATen for the hot-path math.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from ._native import call, f32, i32, i64, ptr, sz
+
+# ---------------------------------------------------------------------------------------------
+# Advantages (invokerl/algorithms/base.py:86-110, grpo.py:46-80, dapo.py:55-88, ppo.py:65-106)
+# ---------------------------------------------------------------------------------------------
+
+
+def mask_count(mask: torch.Tensor) -> torch.Tensor:
+    """Number of True entries of `mask` as an int64 device tensor of shape [1] (no host sync)."""
+    dev = N.require_cuda(mask)
+    m = N.as_mask(mask)
+    out = torch.empty(1, dtype=torch.int64, device=dev)
+    call("ikrl_mask_count", ptr(m), i64(m.numel()), ptr(out), N.stream_of(dev))
+    return out
+
+
+def broadcast_advantages(rewards: torch.Tensor, response_mask: torch.Tensor) -> torch.Tensor:
+    """rewards[b] * mask[b,t] (base.py:108-110)."""
+    dev = N.require_cuda(rewards, response_mask)
+    B, T = response_mask.shape
+    r = rewards.contiguous().float()
+    m = N.as_mask(response_mask)
+    out = torch.empty(B, T, dtype=torch.float32, device=dev)
+    call("ikrl_broadcast_advantages", ptr(r), ptr(m), i32(B), i32(T), ptr(out), N.stream_of(dev))
+    return out
+
+
+def group_advantages(
+    rewards: torch.Tensor,
+    response_mask: torch.Tensor,
+    group_size: int,
+    filter_zero_var: bool = False,
+    truncated: torch.Tensor | None = None,
+    overlong_penalty: float = 0.0,
+    row_adv: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Group-normalised advantages broadcast over the response mask (grpo.py:72-80;
+    with filter_zero_var / truncated: dapo.py:61-88)."""
+    dev = N.require_cuda(rewards, response_mask, truncated)
+    B, T = response_mask.shape
+    if rewards.numel() != B:
+        raise ValueError(f"rewards has {rewards.numel()} entries, expected B={B}")
+    r = rewards.contiguous().float()
+    m = N.as_mask(response_mask)
+    tr = None if truncated is None else N.as_mask(truncated)
+    out = torch.empty(B, T, dtype=torch.float32, device=dev)
+    call(
+        "ikrl_group_advantages", ptr(r), ptr(m), ptr(tr), i32(B), i32(T), i32(group_size),
+        i32(1 if filter_zero_var else 0), f32(overlong_penalty), ptr(out), ptr(row_adv),
+        N.stream_of(dev),
+    )
+    return out
+
+
+def token_group_advantages(token_rewards: torch.Tensor, response_mask: torch.Tensor, group_size: int) -> torch.Tensor:
+    """Per-(group, position) normalisation of token rewards (grpo.py:62-70)."""
+    dev = N.require_cuda(token_rewards, response_mask)
+    B, T = response_mask.shape
+    tr = token_rewards.contiguous().float()
+    m = N.as_mask(response_mask)
+    out = torch.empty(B, T, dtype=torch.float32, device=dev)
+    call("ikrl_token_group_advantages", ptr(tr), ptr(m), i32(B), i32(T), i32(group_size), ptr(out),
+         N.stream_of(dev))
+    return out
+
+
+def gae_advantages(
+    rewards: torch.Tensor | None,
+    token_rewards: torch.Tensor | None,
+    values: torch.Tensor,
+    response_mask: torch.Tensor,
+    gamma: float,
+    lam: float,
+) -> torch.Tensor:
+    """PPO GAE reverse scan (ppo.py:80-106), one block per row."""
+    dev = N.require_cuda(values, response_mask, rewards, token_rewards)
+    B, T = response_mask.shape
+    v = values.contiguous().float()
+    m = N.as_mask(response_mask)
+    rb = None if rewards is None else rewards.contiguous().float()
+    rt = None if token_rewards is None else token_rewards.contiguous().float()
+    out = torch.empty(B, T, dtype=torch.float32, device=dev)
+    call("ikrl_gae_advantages", ptr(rb), ptr(rt), ptr(v), ptr(m), i32(B), i32(T), f32(gamma), f32(lam),
+         ptr(out), N.stream_of(dev))
+    return out
+
+
+def masked_moments(x: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+    """[mean, unbiased std, count, enabled] of x over mask (ppo.py:123-127)."""
+    dev = N.require_cuda(x, mask)
+    xx = x.contiguous().float()
+    m = N.as_mask(mask)
+    n = xx.numel()
+    out = torch.empty(4, dtype=torch.float32, device=dev)
+    nbytes = int(N.lib().ikrl_masked_moments_workspace_bytes(n))
+    ws = N.workspace(dev, nbytes)
+    call("ikrl_masked_moments", ptr(xx), ptr(m), i64(n), ptr(out), ptr(ws), sz(ws.numel()), N.stream_of(dev))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# Clipped-ratio loss (grpo.py:84-143, dapo.py:90-150, ppo.py:108-184)
+# ---------------------------------------------------------------------------------------------
+
+
+def make_loss_params(
+    family: int,
+    ratio_lo: float,
+    ratio_hi: float,
+    clip_metric_eps: float,
+    beta: float,
+    kl_type: str | int = "schulman",
+    entropy_coef: float = 0.0,
+    vf_coef: float = 0.0,
+    vf_clip_eps: float = 0.0,
+) -> N.LossParams:
+    if isinstance(kl_type, str):
+        kl = N.IKRL_KL_SCHULMAN if kl_type == "schulman" else N.IKRL_KL_SIMPLE
+    else:
+        kl = int(kl_type)
+    return N.LossParams(family, ratio_lo, ratio_hi, clip_metric_eps, beta, kl, entropy_coef, vf_coef,
+                        vf_clip_eps)
+
+
+def _clip_loss_launch(new_lp, old_lp, ref_lp, adv, mask_u8, rewards, G, ntok, whiten, values, old_values,
+                      params, want_dlp, want_dvalues):
+    dev = new_lp.device
+    B, T = new_lp.shape
+    dlp = torch.empty_like(new_lp) if want_dlp else None
+    dvalues = torch.empty(B, T, dtype=torch.float32, device=dev) if want_dvalues else None
+    sums = torch.empty(N.LOSS_NSUMS, dtype=torch.float64, device=dev)
+    nbytes = int(N.lib().ikrl_clip_loss_workspace_bytes(B * T))
+    ws = N.workspace(dev, nbytes)
+    call(
+        "ikrl_clip_loss_fwd", ptr(new_lp), i32(N.dtype_code(new_lp)), ptr(old_lp), ptr(ref_lp), ptr(adv),
+        ptr(mask_u8), ptr(rewards), i32(B), i32(T), i32(G), ptr(ntok), ptr(whiten), ptr(values),
+        ptr(old_values), params, ptr(dlp), ptr(dvalues), ptr(sums), ptr(ws), sz(ws.numel()),
+        N.stream_of(dev),
+    )
+    return dlp, dvalues, sums
+
+
+def clip_loss_finalize(sums: torch.Tensor, ntok: torch.Tensor, params: N.LossParams):
+    dev = sums.device
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    metrics = torch.empty(N.LOSS_NMETRICS, dtype=torch.float32, device=dev)
+    call("ikrl_clip_loss_finalize", ptr(sums), ptr(ntok), params, ptr(loss), ptr(metrics), N.stream_of(dev))
+    return loss, metrics
+
+
+def _scale(g_tensor: torch.Tensor, upstream: torch.Tensor) -> None:
+    s = upstream.detach().reshape(1).to(torch.float32).contiguous()
+    call("ikrl_scale_grad", ptr(g_tensor), i32(N.dtype_code(g_tensor)), i64(g_tensor.numel()), ptr(s),
+         N.stream_of(g_tensor.device))
+
+
+class ClipRatioLoss(torch.autograd.Function):
+    """Loss value of one rank's rows; d loss / d new_lp is written by the forward pass and scaled
+    by the upstream gradient in backward (skipped on the device when the upstream is 1)."""
+
+    @staticmethod
+    def forward(ctx, new_lp, values, old_lp, ref_lp, adv, mask_u8, rewards, G, ntok, whiten, old_values,
+                params):
+        want_dlp = new_lp.requires_grad
+        want_dv = values is not None and values.requires_grad
+        dlp, dvalues, sums = _clip_loss_launch(
+            new_lp.detach(), old_lp, ref_lp, adv, mask_u8, rewards, G, ntok, whiten,
+            None if values is None else values.detach(), old_values, params, want_dlp, want_dv,
+        )
+        loss, _ = clip_loss_finalize(sums, ntok, params)
+        ctx.dlp = dlp
+        ctx.dvalues = dvalues
+        ctx.n_bwd = 0
+        ctx.replay = (new_lp.detach(), None if values is None else values.detach(), old_lp, ref_lp, adv, mask_u8,
+                      rewards, G, ntok, whiten, old_values, params, want_dlp, want_dv)
+        ctx.mark_non_differentiable(sums)
+        return loss, sums
+
+    @staticmethod
+    def backward(ctx, g_loss, g_sums):
+        if g_loss is None:
+            return (None,) * 12
+        dlp, dvalues = ctx.dlp, ctx.dvalues
+        if ctx.n_bwd > 0:  # retain_graph: the saved gradient was scaled in place; recompute it
+            (nl, vals, old, ref, adv, m, r, G, ntok, wh, ov, params, wd, wv) = ctx.replay
+            dlp, dvalues, _ = _clip_loss_launch(nl, old, ref, adv, m, r, G, ntok, wh, vals, ov, params, wd, wv)
+        ctx.n_bwd += 1
+        if dlp is not None:
+            _scale(dlp, g_loss)
+        if dvalues is not None:
+            _scale(dvalues, g_loss)
+        return (dlp, dvalues) + (None,) * 10
+
+
+def clip_ratio_loss(
+    new_lp: torch.Tensor,
+    old_lp: torch.Tensor,
+    ref_lp: torch.Tensor | None,
+    adv: torch.Tensor,
+    response_mask: torch.Tensor,
+    rewards: torch.Tensor,
+    group_size: int,
+    params: N.LossParams,
+    ntok: torch.Tensor | None = None,
+    whiten: torch.Tensor | None = None,
+    values: torch.Tensor | None = None,
+    old_values: torch.Tensor | None = None,
+):
+    """Returns (loss tensor, sums tensor, ntok).  ntok defaults to this call's mask count."""
+    dev = N.require_cuda(new_lp, old_lp, ref_lp, adv, response_mask, rewards, values, old_values)
+    if new_lp.dim() != 2:
+        raise ValueError(f"new_log_probs must be [B, T], got {tuple(new_lp.shape)}")
+    B, T = new_lp.shape
+    for name, t in (("old_log_probs", old_lp), ("ref_log_probs", ref_lp), ("advantages", adv),
+                    ("response_mask", response_mask), ("values", values), ("old_values", old_values)):
+        if t is not None and tuple(t.shape) != (B, T):
+            raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {(B, T)}")
+    m = N.as_mask(response_mask)
+    if ntok is None:
+        ntok = mask_count(m)
+    lp = new_lp if new_lp.dtype in (torch.float32, torch.bfloat16) else new_lp.float()
+    loss, sums = ClipRatioLoss.apply(
+        lp.contiguous(), None if values is None else values.contiguous().float(),
+        old_lp.contiguous().float(), None if ref_lp is None else ref_lp.contiguous().float(),
+        adv.contiguous().float(), m, rewards.contiguous().float(), int(group_size), ntok, whiten,
+        None if old_values is None else old_values.contiguous().float(), params,
+    )
+    return loss, sums, ntok
+
+
+# ---------------------------------------------------------------------------------------------
+# SimPO (simpo.py:48-90)
+# ---------------------------------------------------------------------------------------------
+
+
+class SimPOLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, lp, mask_u8, rewards, beta, gamma, chosen_first):
+        dev = lp.device
+        B, T = lp.shape
+        loss = torch.empty((), dtype=torch.float32, device=dev)
+        metrics = torch.empty(N.SIMPO_NMETRICS, dtype=torch.float32, device=dev)
+        coef = torch.empty(B, dtype=torch.float32, device=dev)
+        ws = N.workspace(dev, int(N.lib().ikrl_simpo_workspace_bytes(B)))
+        call("ikrl_simpo_fwd", ptr(lp), i32(N.dtype_code(lp)), ptr(mask_u8), ptr(rewards), i32(B), i32(T),
+             f32(beta), f32(gamma), i32(1 if chosen_first else 0), ptr(loss), ptr(metrics), ptr(coef), ptr(ws),
+             sz(ws.numel()), N.stream_of(dev))
+        ctx.save_for_backward(coef, mask_u8)
+        ctx.lp_dtype = lp.dtype
+        ctx.shape = (B, T)
+        ctx.mark_non_differentiable(metrics)
+        return loss, metrics
+
+    @staticmethod
+    def backward(ctx, g_loss, g_metrics):
+        if g_loss is None:
+            return (None,) * 6
+        coef, m = ctx.saved_tensors
+        B, T = ctx.shape
+        dlp = torch.empty(B, T, dtype=ctx.lp_dtype, device=coef.device)
+        s = g_loss.detach().reshape(1).float().contiguous()
+        call("ikrl_simpo_bwd", ptr(coef), ptr(m), i32(B), i32(T), ptr(s), ptr(dlp),
+             i32(N.dtype_code(dlp)), N.stream_of(coef.device))
+        return dlp, None, None, None, None, None
+
+
+def simpo_loss(lp, response_mask, rewards, beta, gamma, chosen_first):
+    N.require_cuda(lp, response_mask, rewards)
+    B, T = lp.shape
+    if B % 2:
+        raise ValueError(f"SimPO needs an even batch of chosen/rejected pairs, got B={B}")
+    x = lp if lp.dtype in (torch.float32, torch.bfloat16) else lp.float()
+    return SimPOLoss.apply(x.contiguous(), N.as_mask(response_mask),
+                           None if rewards is None else rewards.contiguous().float(), float(beta), float(gamma),
+                           bool(chosen_first))
+
+
+# ---------------------------------------------------------------------------------------------
+# K2: logits -> log-prob (policy.py:100-104, :151-155, :187-191)
+# ---------------------------------------------------------------------------------------------
+
+
+class LogitsLogProb(torch.autograd.Function):
+    """log p(target) from materialised bf16 logits [N, V] (row stride may exceed V)."""
+
+    @staticmethod
+    def forward(ctx, logits, ids):
+        dev = logits.device
+        Nr, V = logits.shape
+        ld = logits.stride(0)
+        logp = torch.empty(Nr, dtype=torch.float32, device=dev)
+        lse = torch.empty(Nr, dtype=torch.float32, device=dev)
+        call("ikrl_logits_logprob_fwd", ptr(logits), i64(ld), ptr(ids), i64(Nr), i32(V), ptr(logp), ptr(lse), None,
+             N.stream_of(dev))
+        ctx.save_for_backward(logits, ids, lse)
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, ids, lse = ctx.saved_tensors
+        Nr, V = logits.shape
+        g = g.contiguous().float()
+        dlogits = torch.empty(Nr, V, dtype=torch.bfloat16, device=logits.device)
+        call("ikrl_logits_logprob_bwd", ptr(logits), i64(logits.stride(0)), ptr(ids), ptr(lse), ptr(g), i64(Nr),
+             i32(V), ptr(dlogits), i64(dlogits.stride(0)), N.stream_of(logits.device))
+        return dlogits, None
+
+
+def logits_logprob(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """-F.cross_entropy(logits, targets, reduction="none") over the last dim, as fp32."""
+    N.require_cuda(logits, targets)
+    if logits.dtype != torch.bfloat16:
+        raise TypeError(f"logits_logprob expects bf16 logits, got {logits.dtype}")
+    shape = targets.shape
+    V = logits.shape[-1]
+    x = logits.reshape(-1, V)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    ids = targets.reshape(-1).to(torch.int64).contiguous()
+    return LogitsLogProb.apply(x, ids).reshape(shape)
+
+
+def logits_logprob_raw(logits: torch.Tensor, ids: torch.Tensor, with_target: bool = False):
+    """Forward only: (logp, lse[, gathered target logit]) — used by tests for the bit-exact gather."""
+    dev = N.require_cuda(logits, ids)
+    Nr, V = logits.shape
+    logp = torch.empty(Nr, dtype=torch.float32, device=dev)
+    lse = torch.empty(Nr, dtype=torch.float32, device=dev)
+    tgt = torch.empty(Nr, dtype=torch.float32, device=dev) if with_target else None
+    call("ikrl_logits_logprob_fwd", ptr(logits), i64(logits.stride(0)), ptr(ids), i64(Nr), i32(V), ptr(logp),
+         ptr(lse), ptr(tgt), N.stream_of(dev))
+    return (logp, lse, tgt) if with_target else (logp, lse)

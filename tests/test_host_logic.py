@@ -1,0 +1,110 @@
+"""Host-side logic that needs no GPU: group sharding, loss parameters, synthetic inputs."""
+
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from invokerl_b200 import _native as N
+from invokerl_b200 import ops
+from invokerl_b200.algorithms import DAPO, GRPO, PPO
+from invokerl_b200.distributed import group_shard_bounds, shard_batch
+from invokerl_b200.synthetic import rollout_batch
+
+
+@pytest.mark.parametrize("B,G,world", [(16, 4, 1), (16, 4, 2), (16, 4, 3), (128, 8, 8), (8, 8, 4), (12, 2, 5)])
+def test_group_shards_cover_whole_groups(B, G, world):
+    seen = []
+    for r in range(world):
+        s, e = group_shard_bounds(B, G, r, world)
+        assert s % G == 0 and e % G == 0 and s <= e
+        seen.extend(range(s, e))
+    assert seen == list(range(B))
+
+
+def test_shard_bounds_reject_partial_groups():
+    with pytest.raises(ValueError):
+        group_shard_bounds(10, 4, 0, 2)
+
+
+def test_shard_batch_slices_every_row_field():
+    b = rollout_batch(4, 4, 64, prompt_len=(4, 16), completion_len=(4, 32), seed=0)
+    b.extras["truncated"] = torch.arange(16) % 3 == 0
+    s = shard_batch(b, 1, 2)
+    assert s.token_ids.shape == (8, 64)
+    assert torch.equal(s.rewards, b.rewards[8:16])
+    assert torch.equal(s.extras["truncated"], b.extras["truncated"][8:16])
+    assert s.extras["new_log_probs"].shape == (8, 64)
+
+
+def test_loss_params_follow_each_algorithm():
+    p = GRPO(clip_eps=0.3, beta=0.1, kl_type="simple")._params()
+    assert p.family == N.IKRL_LOSS_GRPO and abs(p.ratio_lo - 0.7) < 1e-7 and abs(p.ratio_hi - 1.3) < 1e-7
+    assert p.kl_type == N.IKRL_KL_SIMPLE and abs(p.beta - 0.1) < 1e-7
+    d = DAPO()._params()
+    assert abs(d.ratio_lo - 0.8) < 1e-7 and abs(d.ratio_hi - 1.28) < 1e-6 and abs(d.clip_metric_eps - 0.2) < 1e-7
+    q = PPO()._params()
+    assert q.family == N.IKRL_LOSS_PPO and q.kl_type == N.IKRL_KL_NONE and abs(q.entropy_coef - 0.01) < 1e-7
+    assert ops.make_loss_params(0, 0.8, 1.2, 0.2, 0.0).kl_type == N.IKRL_KL_SCHULMAN
+
+
+def test_synthetic_batch_layout():
+    b = rollout_batch(4, 4, 512, seed=3)
+    assert b.token_ids.shape == (16, 512) and b.group_size == 4
+    assert not (b.prompt_mask & b.response_mask).any()
+    c = b.response_mask.sum(1)
+    assert int(c.min()) >= 32 and int(c.max()) <= 256
+    assert set(b.rewards.tolist()) <= {0.0, 1.0}
+    assert float(b.extras["new_log_probs"].max()) <= 0.0
+
+
+# ---- row sharding over gloo ranks: sharded loss shares and gradients equal the global ones ----
+
+
+def _sharded_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        b = rollout_batch(4, 4, 128, prompt_len=(8, 40), completion_len=(8, 80), seed=21)
+        local = shard_batch(b, rank, world)
+        adv = oracle.group_advantages(local.rewards, local.response_mask, local.group_size)
+        n = local.response_mask.sum().to(torch.int64).reshape(1)
+        dist.all_reduce(n)  # the one collective before the loss
+        lp = local.extras["new_log_probs"].clone().requires_grad_(True)
+        m = local.response_mask.float()
+        ratio = torch.exp(lp - local.old_log_probs)
+        pl = -torch.minimum(ratio * adv, torch.clamp(ratio, 0.8, 1.2) * adv)
+        d = local.ref_log_probs - lp
+        share = ((pl + 0.04 * (torch.exp(d) - d - 1)) * m).sum() / n.clamp(min=1).float()
+        share.backward()
+        tot = share.detach().clone()
+        dist.all_reduce(tot)
+        grads = [torch.zeros(4 * 4 // world * 1, 128) for _ in range(world)]
+        dist.all_gather(grads, lp.grad.contiguous())
+        if rank == 0:
+            q.put((float(tot), torch.cat(grads)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_loss_matches_global_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    tot, grad = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    b = rollout_batch(4, 4, 128, prompt_len=(8, 40), completion_len=(8, 80), seed=21)
+    adv = oracle.group_advantages(b.rewards, b.response_mask, 4)
+    loss, _, g = oracle.clip_ratio_loss(b.extras["new_log_probs"], b.old_log_probs, b.ref_log_probs, adv,
+                                        b.response_mask, b.rewards)
+    assert abs(tot - float(loss)) <= 1e-5 * abs(float(loss)) + 1e-7
+    torch.testing.assert_close(grad, g, rtol=1e-5, atol=1e-8)

@@ -1,0 +1,69 @@
+"""The C-ABI library builds, loads without a GPU, and exports every declared symbol."""
+
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols() -> list[str]:
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        names += re.findall(r"IKRL_API\s+[\w\s\*]+?\b(ikrl_\w+)\s*\(", h.read_text())
+    return sorted(set(names))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from invokerl_b200.csrc.build import build
+
+    build()
+    from invokerl_b200 import _native
+
+    return _native.lib()
+
+
+def test_header_declares_symbols():
+    names = declared_symbols()
+    assert len(names) >= 18
+    assert "ikrl_clip_loss_fwd" in names and "ikrl_logits_logprob_fwd" in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_every_declared_symbol_has_a_python_signature(lib):
+    from invokerl_b200 import _native
+
+    missing = [n for n in declared_symbols() if n not in _native.exported_names()]
+    assert not missing, missing
+
+
+def test_abi_version_and_error_string(lib):
+    assert lib.ikrl_abi_version() >= 1
+    assert lib.ikrl_last_error() == b""
+
+
+def test_argument_errors_need_no_gpu(lib):
+    """Validation happens on the host before any CUDA call and sets the error string."""
+    from invokerl_b200 import _native as N
+
+    with pytest.raises(N.IkrlError, match="group_size"):
+        N.call("ikrl_group_advantages", None, None, None, N.i32(6), N.i32(4), N.i32(4), N.i32(0),
+               N.f32(0), None, None, None)
+    with pytest.raises(N.IkrlError, match="workspace"):
+        N.call("ikrl_masked_moments", N.c_void_p(16), N.c_void_p(16), N.i64(10), N.c_void_p(16), None,
+               N.sz(0), None)
+
+
+def test_cpu_tensors_are_rejected():
+    import torch
+
+    from invokerl_b200 import ops
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.mask_count(torch.ones(4, dtype=torch.bool))
