@@ -66,6 +66,8 @@ enum {
 IKRL_API const char* ikrl_last_error(void);
 /* ABI version; bumps whenever a signature below changes. */
 IKRL_API int ikrl_abi_version(void);
+/* Number of kernels this library has launched in this process (host-side counter). */
+IKRL_API unsigned long long ikrl_launch_count(void);
 
 /* ---- K3: advantages ------------------------------------------------------------------------ */
 
@@ -192,6 +194,36 @@ IKRL_API int ikrl_logits_logprob_fwd(const void* logits, int64_t ld, const int64
 IKRL_API int ikrl_logits_logprob_bwd(const void* logits, int64_t ld, const int64_t* ids, const float* lse,
                             const float* dlogp, int64_t N, int32_t V, void* dlogits,
                             int64_t ld_out, void* stream);
+
+/* ---- K1: fused LM-head log-prob (tcgen05 / TMEM / TMA) --------------------------------------- */
+
+/* Replaces the LM head + cross-entropy of invokerl/policy.py:124-191 (`_chunked_lm_head_ce`,
+ * `_chunk_ce_fn`): hidden bf16 [N, H] (row stride H), weight bf16 [V, H] (row stride H),
+ * ids int64 [N] in [0, V) (-100 = ignored row, log p = -0.0).  logp[N] fp32 =
+ * (h W^T)[r, ids[r]] - logsumexp_v (h W^T)[r, v]; lse[N] fp32 (nullable) is saved for the
+ * backward.  The [N, V] logits never exist in memory.  H must be a multiple of 8; pointers
+ * 16-byte aligned; the workspace 256-byte aligned. */
+IKRL_API size_t ikrl_lmhead_fwd_workspace_bytes(int64_t N, int32_t H, int32_t V);
+IKRL_API int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_t* ids,
+                                     int64_t N, int32_t H, int32_t V, float* logp, float* lse,
+                                     void* ws, size_t ws_bytes, void* stream);
+
+/* Backward of the above for upstream dlogp[N] fp32: dhidden bf16 [N, H] (nullable) and dweight
+ * [V, H] (nullable; IKRL_DTYPE_BF16 or IKRL_DTYPE_F32, the latter optionally accumulated into).
+ * Rows are processed in chunks of `chunk_rows` (<= 0: all rows at once); the workspace holds one
+ * chunk of bf16 dlogits [chunk, round_up(V, 64)] plus, for a bf16 dweight over several chunks,
+ * an fp32 [V, H] accumulator. */
+IKRL_API size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows,
+                                                int32_t dweight_dtype, int32_t accumulate_dweight);
+IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids,
+                                     const float* lse, const float* dlogp, int64_t N, int32_t H,
+                                     int32_t V, int64_t chunk_rows, void* dhidden, void* dweight,
+                                     int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
+                                     size_t ws_bytes, void* stream);
+
+/* Device status word of the last K1 call that used workspace `ws` (synchronises `stream`):
+ * IKRL_OK, or IKRL_ERR_DEVICE with *status_out = the recorded code (a bounded wait expired). */
+IKRL_API int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream);
 
 #ifdef __cplusplus
 }

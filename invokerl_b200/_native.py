@@ -65,6 +65,7 @@ _P = c_void_p
 _SIGNATURES: dict[str, tuple] = {
     "ikrl_last_error": (ctypes.c_char_p, []),
     "ikrl_abi_version": (ctypes.c_int, []),
+    "ikrl_launch_count": (ctypes.c_ulonglong, []),
     "ikrl_mask_count": (ctypes.c_int, [_P, c_int64, _P, _P]),
     "ikrl_broadcast_advantages": (ctypes.c_int, [_P, _P, c_int32, c_int32, _P, _P]),
     "ikrl_group_advantages": (
@@ -101,6 +102,17 @@ _SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_P, c_int64, _P, _P, _P, c_int64, c_int32, _P, c_int64, _P],
     ),
+    "ikrl_lmhead_fwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
+    "ikrl_lmhead_logprob_fwd": (
+        ctypes.c_int,
+        [_P, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P, c_size_t, _P],
+    ),
+    "ikrl_lmhead_bwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32, c_int64, c_int32, c_int32]),
+    "ikrl_lmhead_logprob_bwd": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _P, c_int64, c_int32, c_int32, c_int64, _P, _P, c_int32, c_int32, _P, c_size_t, _P],
+    ),
+    "ikrl_lmhead_status": (ctypes.c_int, [_P, POINTER(c_int32), _P]),
 }
 
 _lock = threading.Lock()
@@ -246,4 +258,8 @@ __all__ = [
     "workspace",
     "c_double",
     "c_uint8",
+    "c_int32",
+    "byref",
 ]
+
+byref = ctypes.byref

@@ -1,0 +1,653 @@
+// K1: fused LM-head log-prob on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces invokerl/policy.py:124-191 (`_chunked_lm_head_ce` / `_chunk_ce_fn`: F.linear then
+// -F.cross_entropy, chunk by chunk under torch.utils.checkpoint) and its autograd.
+//
+// Forward: logits tiles S = h W^T are produced in TMEM, 128 rows x 256 vocab columns at a time,
+// and consumed in place by an epilogue that keeps an online (max, sum-exp) per row and picks out
+// the target logit; the [N, V] logits never reach HBM.  Partial row statistics of each vocab
+// split are merged by a small combine kernel: log p = S[target] - logsumexp(S).
+//
+// Backward: for each chunk of rows, the same GEMM recomputes S and its epilogue writes
+// dS = g * (onehot - exp(S - lse)) in bf16 to a chunk workspace; two more tcgen05 GEMMs form
+// dH = dS W (A K-major, B MN-major) and dW += dS^T h (both MN-major), the latter accumulated in
+// fp32.  Only one chunk of dS exists at a time.
+//
+// Kernel shape (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 4-stage ring of {A 128x64, B 256x64} bf16 tiles, 128B swizzle
+//   warp 1      TMEM allocator + MMA issuer: tcgen05.mma M=128 N=256 K=16, f32 accumulators,
+//               two accumulators (2 x 256 TMEM columns) so the epilogue of tile j overlaps the
+//               MMAs of tile j+1
+//   warps 2-5   epilogue: tcgen05.ld, one TMEM lane (= one output row) per thread
+// Every mbarrier wait is bounded (sm100::kWaitTimeoutNs); on expiry the CTA records an error,
+// drains its in-flight copies and MMAs, frees TMEM and exits.
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <mutex>
+
+namespace ikrl {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr uint32_t kTileA = BM * BK * 2;  // 16 KB
+constexpr uint32_t kTileB = BN * BK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kTileA + kTileB;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr uint32_t kMnAtomBytes = 64 * BK * 2;  // one 64-wide MN slab of an MN-major tile: 8 KB
+
+enum Epi : int { EPI_LSE = 0, EPI_DLOGITS = 1, EPI_STORE_BF16 = 2, EPI_F32 = 3 };
+enum F32Mode : int { F32_STORE = 0, F32_ADD = 1, F32_ADD_TO_BF16 = 2 };
+
+struct GemmParams {
+  int M, N, K;            // C[M, N] = A[M, K] * B[N, K]^T
+  int n_tiles;            // ceil(N / BN)
+  int tiles_per_split;    // consecutive N tiles of one CTA
+  int splits;             // number of N ranges (gridDim.x when split-major)
+  int split_major;        // 1: blockIdx.x = split, blockIdx.y = row block; 0: the reverse
+  const int64_t* ids;     // [M] target ids (LSE / DLOGITS)
+  const float* lse;       // [M] (DLOGITS)
+  const float* g;         // [M] upstream d loss / d logp (DLOGITS)
+  float* part_m;          // [splits][M] running max, log2 units (LSE)
+  float* part_s;          // [splits][M] sum of 2^(x - max) (LSE)
+  float* part_t;          // [M] raw target logit, written by the split owning the target (LSE)
+  uint16_t* out_bf16;     // DLOGITS: dS; STORE_BF16: output; F32 mode 2: bf16 output
+  int64_t ld_bf16;
+  float* out_f32;         // F32: accumulator
+  int64_t ld_f32;
+  int f32_mode;
+  int* err;               // device error word
+};
+
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitTimeoutNs / 4) {
+      atomicCAS(err, 0, kErrTimeoutDrain);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    lmhead_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages], acc_full[2], acc_empty[2], drain_bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+
+  const int split = p.split_major ? blockIdx.x : blockIdx.y;
+  const int m_blk = p.split_major ? blockIdx.y : blockIdx.x;
+  const int m0 = m_blk * BM;
+  const int t_begin = split * p.tiles_per_split;
+  const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+  const int ntiles = t_end - t_begin;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), kEpiWarps);
+    }
+    mbar_init(smem_u32(&drain_bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    fence_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_holder;
+  volatile int* abort_v = &abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && ntiles > 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_phase[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) issued_phase[s] = -1;
+      bool ok = true;
+      for (int t = t_begin; t < t_end && ok; ++t) {
+        const int n0 = t * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          const uint32_t a_dst = smem_base + stage * kStageBytes;
+          const uint32_t b_dst = a_dst + kTileA;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, fb, k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c) tma_load_2d(a_dst + c * kMnAtomBytes, &tmA, fb, m0 + 64 * c, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, fb, k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * kMnAtomBytes, &tmB, fb, n0 + 64 * c, k0);
+          }
+          issued_phase[stage] = (int)phase;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (ok) {
+        // Tail: wait until the MMA warp has released every stage, so no arrive is pending.
+        for (int s = 0; s < kStages; ++s) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) break;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      } else {
+        // Abort: let every issued copy land before shared memory is released.
+        for (int s = 0; s < kStages; ++s)
+          if (issued_phase[s] >= 0) mbar_wait_drain(smem_u32(&full_bar[s]), (uint32_t)issued_phase[s], p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && ntiles > 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int acc = j & 1;
+        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_base + stage * kStageBytes;
+          const uint32_t b_addr = a_addr + kTileA;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
+                                     : smem_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, kMnAtomBytes, 1024)
+                                     : smem_desc(b_addr + k * 32, 16, 1024);
+            mma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) mma_commit(smem_u32(&acc_full[acc]));
+      }
+      if (!ok) {
+        // Abort: wait for the MMAs already issued before TMEM and shared memory go away.
+        mma_commit(smem_u32(&drain_bar));
+        mbar_wait_drain(smem_u32(&drain_bar), 0, p.err);
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int r = q * 32 + lane;
+    const int grow = m0 + r;
+    const bool row_ok = grow < p.M;
+    int64_t tgt = -1;
+    float lse2 = 0.f, gval = 0.f;
+    if constexpr (EPI == EPI_LSE || EPI == EPI_DLOGITS) {
+      if (row_ok) tgt = p.ids[grow];
+    }
+    if constexpr (EPI == EPI_DLOGITS) {
+      if (row_ok) {
+        lse2 = p.lse[grow] * kLog2e;
+        gval = p.g[grow];
+        if (tgt == -100) gval = 0.f;  // ignore_index rows have zero gradient
+      }
+    }
+    float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
+    for (int j = 0; j < ntiles; ++j) {
+      const int acc = j & 1;
+      const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+      if (!mbar_wait(smem_u32(&acc_full[acc]), acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int n0 = (t_begin + j) * BN;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const int col0 = n0 + c;
+        if (col0 >= p.N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tbase + (uint32_t)c, v);
+        tmem_wait_ld();
+        const int nvalid = min(32, p.N - col0);
+        if constexpr (EPI == EPI_LSE) {
+          float cm = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < nvalid) cm = fmaxf(cm, v[i]);
+          cm *= kLog2e;
+          if (cm > run_m) {
+            run_s *= fast_exp2(run_m - cm);
+            run_m = cm;
+          }
+          float cs = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
+          run_s += cs;
+          const int64_t rel = tgt - col0;
+          if (rel >= 0 && rel < nvalid) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i == (int)rel) tval = v[i];
+          }
+        } else if constexpr (EPI == EPI_DLOGITS) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float p0 = fast_exp2(fmaf(v[i], kLog2e, -lse2));
+            const float p1 = fast_exp2(fmaf(v[i + 1], kLog2e, -lse2));
+            const float d0 = gval * (((int64_t)(col0 + i) == tgt ? 1.f : 0.f) - p0);
+            const float d1 = gval * (((int64_t)(col0 + i + 1) == tgt ? 1.f : 0.f) - p1);
+            w[i >> 1] = pack_bf16x2(d0, d1);
+          }
+          if (row_ok) {
+            uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          }
+        } else if constexpr (EPI == EPI_STORE_BF16) {
+          if (row_ok) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) w[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
+            uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          }
+        } else {  // EPI_F32
+          if (row_ok) {
+            float* dst = p.out_f32 + (int64_t)grow * p.ld_f32 + col0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              if (4 * k >= nvalid) break;
+              float4 x = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+              if (p.f32_mode != F32_STORE) {
+                const float4 o = *reinterpret_cast<const float4*>(dst + 4 * k);
+                x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+              }
+              if (p.f32_mode == F32_ADD_TO_BF16) {
+                uint16_t* d16 = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0 + 4 * k;
+                *reinterpret_cast<uint2*>(d16) = make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
+              } else {
+                *reinterpret_cast<float4*>(dst + 4 * k) = x;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+    }
+    if constexpr (EPI == EPI_LSE) {
+      if (row_ok && !*abort_v) {
+        p.part_m[(int64_t)split * p.M + grow] = run_m;
+        p.part_s[(int64_t)split * p.M + grow] = run_s;
+        if (tgt >= (int64_t)t_begin * BN && tgt < (int64_t)t_end * BN && tgt < p.N) p.part_t[grow] = tval;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Merge the per-split (max, sum) pairs of each row: lse = ln2 * (M + log2 sum_s s_s 2^(m_s - M)).
+__global__ void lse_combine_kernel(const float* __restrict__ part_m, const float* __restrict__ part_s,
+                                   const float* __restrict__ part_t, const int64_t* __restrict__ ids, int M,
+                                   int V, int splits, float* __restrict__ logp, float* __restrict__ lse_out,
+                                   const int* __restrict__ err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= M) return;
+  const bool bad = *err != 0;
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, part_m[(int64_t)s * M + r]);
+  float sum = 0.f;
+  for (int s = 0; s < splits; ++s) sum += part_s[(int64_t)s * M + r] * fast_exp2(part_m[(int64_t)s * M + r] - mx);
+  const float lse = (mx + log2f(sum)) * kLn2;
+  const int64_t t = ids[r];
+  float lp;
+  if (bad) lp = __int_as_float(0x7fc00000);
+  else if (t == -100) lp = -0.f;
+  else if (t < 0 || t >= V) lp = __int_as_float(0x7fc00000);
+  else lp = part_t[r] - lse;
+  logp[r] = lp;
+  if (lse_out) lse_out[r] = bad ? __int_as_float(0x7fc00000) : lse;
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [outer, inner] with row stride `ld` elements and a
+// box of {64 inner, box_outer} elements, 128-byte swizzle, zero fill out of bounds.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_outer,
+              const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  IKRL_REQUIRE(fn != nullptr, IKRL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  IKRL_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, IKRL_ERR_ALIGNMENT,
+               "%s: base address must be 16-byte aligned", what);
+  IKRL_REQUIRE((ld * 2) % 16 == 0, IKRL_ERR_ALIGNMENT, "%s: row stride %llu elements is not a multiple of 8", what,
+               (unsigned long long)ld);
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {64, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  IKRL_REQUIRE(r == CUDA_SUCCESS, IKRL_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return IKRL_OK;
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int m_tiles, cudaStream_t s) {
+  auto kern = lmhead_gemm_kernel<EPI, A_MN, B_MN>;
+  IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+  IKRL_REQUIRE(m_tiles <= 65535 || p.split_major == 0, IKRL_ERR_UNSUPPORTED, "too many row blocks (%d)", m_tiles);
+  const dim3 grid = p.split_major ? dim3(p.splits, m_tiles) : dim3(m_tiles, p.splits);
+  kern<<<grid, kThreads, kSmemBytes, s>>>(a, b, p);
+  return check_launch("lmhead_gemm_kernel");
+}
+
+int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Vocab splits for the row-sweeping GEMMs: enough that the row blocks resident at once keep their
+// A tiles in L2 (about 24 MB of hidden rows), and enough CTAs to fill the GPU.
+int choose_splits(int64_t m_tiles, int n_tiles, int H) {
+  const int64_t resident_rows_budget = (24ll << 20) / (2ll * H);   // rows whose A tiles fit ~24 MB
+  const int64_t blocks_resident = std::max<int64_t>(1, resident_rows_budget / BM);
+  int64_t s = cdiv64(kNumSMs, std::min<int64_t>(blocks_resident, m_tiles));
+  s = std::max<int64_t>(s, cdiv64(2 * kNumSMs, m_tiles));
+  s = std::min<int64_t>(s, n_tiles);
+  return (int)std::max<int64_t>(1, s);
+}
+
+struct FwdLayout {
+  size_t err_off, pm_off, ps_off, pt_off, total;
+  int splits, tps;
+};
+
+FwdLayout fwd_layout(int64_t N, int H, int V) {
+  FwdLayout L;
+  const int64_t m_tiles = cdiv64(N, BM);
+  const int n_tiles = (int)cdiv64(V, BN);
+  int s = choose_splits(m_tiles, n_tiles, H);
+  L.tps = (int)cdiv64(n_tiles, s);
+  L.splits = (int)cdiv64(n_tiles, L.tps);
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  L.err_off = 0;
+  L.pm_off = 256;
+  L.ps_off = al(L.pm_off + (size_t)L.splits * N * 4);
+  L.pt_off = al(L.ps_off + (size_t)L.splits * N * 4);
+  L.total = al(L.pt_off + (size_t)N * 4);
+  return L;
+}
+
+struct BwdLayout {
+  size_t err_off, ds_off, dw_off, total;
+  int64_t chunk, lds;
+  bool need_dw32;
+};
+
+BwdLayout bwd_layout(int64_t N, int H, int V, int64_t chunk_rows, int dweight_dtype, int accumulate) {
+  BwdLayout L;
+  int64_t c = chunk_rows > 0 ? chunk_rows : N;
+  c = std::min<int64_t>(c, N);
+  if (c < N) c = std::max<int64_t>(BM, (c / BM) * BM);
+  L.chunk = std::max<int64_t>(c, 1);
+  L.lds = cdiv64(V, 64) * 64;
+  const int64_t nchunks = cdiv64(N, L.chunk);
+  L.need_dw32 = (dweight_dtype == IKRL_DTYPE_BF16) && (nchunks > 1 || accumulate);
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  L.err_off = 0;
+  L.ds_off = 256;
+  L.dw_off = al(L.ds_off + (size_t)L.chunk * L.lds * 2);
+  L.total = L.dw_off + (L.need_dw32 ? al((size_t)V * H * 4) : 0);
+  return L;
+}
+
+int check_common(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int H, int V,
+                 const char* what) {
+  IKRL_REQUIRE(N >= 0 && H > 0 && V > 0, IKRL_ERR_INVALID_ARGUMENT, "%s: bad sizes N=%lld H=%d V=%d", what,
+               (long long)N, H, V);
+  IKRL_REQUIRE(H % 8 == 0, IKRL_ERR_ALIGNMENT, "%s: hidden size H=%d must be a multiple of 8 (16-byte rows)", what, H);
+  IKRL_REQUIRE(N == 0 || (hidden && weight && ids), IKRL_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  IKRL_REQUIRE(N <= (int64_t)65535 * BM, IKRL_ERR_UNSUPPORTED, "%s: N=%lld rows exceeds one launch; chunk the call",
+               what, (long long)N);
+  return IKRL_OK;
+}
+
+}  // namespace
+}  // namespace ikrl
+
+using namespace ikrl;
+
+extern "C" {
+
+size_t ikrl_lmhead_fwd_workspace_bytes(int64_t N, int32_t H, int32_t V) {
+  if (N <= 0 || H <= 0 || V <= 0) return 256;
+  return fwd_layout(N, H, V).total;
+}
+
+int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
+                            int32_t V, float* logp, float* lse, void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  int rc = check_common(hidden, weight, ids, N, H, V, "ikrl_lmhead_logprob_fwd");
+  if (rc) return rc;
+  if (N == 0) return IKRL_OK;
+  IKRL_REQUIRE(logp != nullptr, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_logprob_fwd: logp is NULL");
+  const FwdLayout L = fwd_layout(N, H, V);
+  IKRL_REQUIRE(ws != nullptr && ws_bytes >= L.total, IKRL_ERR_WORKSPACE,
+               "ikrl_lmhead_logprob_fwd: workspace %zu < %zu bytes", ws_bytes, L.total);
+  IKRL_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, IKRL_ERR_ALIGNMENT,
+               "ikrl_lmhead_logprob_fwd: workspace must be 256-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  char* w = reinterpret_cast<char*>(ws);
+  int* err = reinterpret_cast<int*>(w + L.err_off);
+  IKRL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, hidden, H, N, H, BM, "hidden"))) return rc;
+  if ((rc = make_tmap(&tb, weight, H, V, H, BN, "weight"))) return rc;
+  GemmParams p{};
+  p.M = (int)N; p.N = V; p.K = H;
+  p.n_tiles = (int)cdiv64(V, BN);
+  p.tiles_per_split = L.tps;
+  p.splits = L.splits;
+  p.split_major = 1;
+  p.ids = ids;
+  p.part_m = reinterpret_cast<float*>(w + L.pm_off);
+  p.part_s = reinterpret_cast<float*>(w + L.ps_off);
+  p.part_t = reinterpret_cast<float*>(w + L.pt_off);
+  p.err = err;
+  const int m_tiles = (int)cdiv64(N, BM);
+  if ((rc = launch_gemm<EPI_LSE, false, false>(ta, tb, p, m_tiles, s))) return rc;
+  lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V, L.splits,
+                                                              logp, lse, err);
+  return check_launch("lse_combine_kernel");
+}
+
+size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows, int32_t dweight_dtype,
+                                       int32_t accumulate_dweight) {
+  if (N <= 0 || H <= 0 || V <= 0) return 256;
+  return bwd_layout(N, H, V, chunk_rows, dweight_dtype, accumulate_dweight).total;
+}
+
+int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids, const float* lse,
+                            const float* dlogp, int64_t N, int32_t H, int32_t V, int64_t chunk_rows, void* dhidden,
+                            void* dweight, int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
+                            size_t ws_bytes, void* stream) {
+  clear_error();
+  int rc = check_common(hidden, weight, ids, N, H, V, "ikrl_lmhead_logprob_bwd");
+  if (rc) return rc;
+  IKRL_REQUIRE(dweight_dtype == IKRL_DTYPE_F32 || dweight_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
+               "ikrl_lmhead_logprob_bwd: dweight dtype %d unsupported", dweight_dtype);
+  IKRL_REQUIRE(!(accumulate_dweight && dweight_dtype == IKRL_DTYPE_BF16), IKRL_ERR_UNSUPPORTED,
+               "ikrl_lmhead_logprob_bwd: accumulating into a bf16 dweight is not supported; use fp32");
+  if (N == 0) return IKRL_OK;
+  IKRL_REQUIRE(lse && dlogp && (dhidden || dweight), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_lmhead_logprob_bwd: null pointer");
+  const BwdLayout L = bwd_layout(N, H, V, chunk_rows, dweight_dtype, accumulate_dweight);
+  IKRL_REQUIRE(ws != nullptr && ws_bytes >= L.total, IKRL_ERR_WORKSPACE,
+               "ikrl_lmhead_logprob_bwd: workspace %zu < %zu bytes", ws_bytes, L.total);
+  IKRL_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, IKRL_ERR_ALIGNMENT,
+               "ikrl_lmhead_logprob_bwd: workspace must be 256-byte aligned");
+  IKRL_REQUIRE(dweight == nullptr || (reinterpret_cast<uintptr_t>(dweight) & 15) == 0, IKRL_ERR_ALIGNMENT,
+               "ikrl_lmhead_logprob_bwd: dweight must be 16-byte aligned");
+  IKRL_REQUIRE(dhidden == nullptr || (reinterpret_cast<uintptr_t>(dhidden) & 15) == 0, IKRL_ERR_ALIGNMENT,
+               "ikrl_lmhead_logprob_bwd: dhidden must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  char* w = reinterpret_cast<char*>(ws);
+  int* err = reinterpret_cast<int*>(w + L.err_off);
+  uint16_t* dS = reinterpret_cast<uint16_t*>(w + L.ds_off);
+  float* dw32 = L.need_dw32 ? reinterpret_cast<float*>(w + L.dw_off) : nullptr;
+  IKRL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+  const uint16_t* h16 = reinterpret_cast<const uint16_t*>(hidden);
+  const int n_vt = (int)cdiv64(V, BN);
+  const int n_ht = (int)cdiv64(H, BN);
+  const int64_t nchunks = cdiv64(N, L.chunk);
+
+  CUtensorMap t_w_k, t_w_mn;
+  if ((rc = make_tmap(&t_w_k, weight, H, V, H, BN, "weight"))) return rc;
+  if ((rc = make_tmap(&t_w_mn, weight, H, V, H, 64, "weight^T"))) return rc;
+
+  for (int64_t ci = 0; ci < nchunks; ++ci) {
+    const int64_t c0 = ci * L.chunk;
+    const int64_t rows = std::min<int64_t>(L.chunk, N - c0);
+    const int m_tiles = (int)cdiv64(rows, BM);
+    const uint16_t* hc = h16 + c0 * H;
+    // 1) dS = g * (onehot - softmax(h W^T)) for this chunk
+    {
+      CUtensorMap ta;
+      if ((rc = make_tmap(&ta, hc, H, rows, H, BM, "hidden chunk"))) return rc;
+      GemmParams p{};
+      p.M = (int)rows; p.N = V; p.K = H;
+      p.n_tiles = n_vt;
+      const int sp = choose_splits(m_tiles, n_vt, H);
+      p.tiles_per_split = (int)cdiv64(n_vt, sp);
+      p.splits = (int)cdiv64(n_vt, p.tiles_per_split);
+      p.split_major = 1;
+      p.ids = ids + c0; p.lse = lse + c0; p.g = dlogp + c0;
+      p.out_bf16 = dS; p.ld_bf16 = L.lds;
+      p.err = err;
+      if ((rc = launch_gemm<EPI_DLOGITS, false, false>(ta, t_w_k, p, m_tiles, s))) return rc;
+    }
+    // 2) dH[chunk] = dS W
+    if (dhidden) {
+      CUtensorMap ta;
+      if ((rc = make_tmap(&ta, dS, V, rows, L.lds, BM, "dS"))) return rc;
+      GemmParams p{};
+      p.M = (int)rows; p.N = H; p.K = V;
+      p.n_tiles = n_ht; p.tiles_per_split = 1; p.splits = n_ht; p.split_major = 1;
+      p.out_bf16 = reinterpret_cast<uint16_t*>(dhidden) + c0 * H; p.ld_bf16 = H;
+      p.err = err;
+      if ((rc = launch_gemm<EPI_STORE_BF16, false, true>(ta, t_w_mn, p, m_tiles, s))) return rc;
+    }
+    // 3) dW (+)= dS^T h[chunk]
+    if (dweight) {
+      CUtensorMap ta, tb;
+      if ((rc = make_tmap(&ta, dS, V, rows, L.lds, 64, "dS^T"))) return rc;
+      if ((rc = make_tmap(&tb, hc, H, rows, H, 64, "hidden chunk^T"))) return rc;
+      GemmParams p{};
+      p.M = V; p.N = H; p.K = (int)rows;
+      p.n_tiles = n_ht; p.tiles_per_split = 1; p.splits = n_ht; p.split_major = 1;
+      p.err = err;
+      const int v_tiles = (int)cdiv64(V, BM);
+      const bool last = ci == nchunks - 1;
+      if (dweight_dtype == IKRL_DTYPE_BF16 && !L.need_dw32) {
+        p.out_bf16 = reinterpret_cast<uint16_t*>(dweight); p.ld_bf16 = H;
+        if ((rc = launch_gemm<EPI_STORE_BF16, true, true>(ta, tb, p, v_tiles, s))) return rc;
+      } else {
+        if (dweight_dtype == IKRL_DTYPE_F32) {
+          p.out_f32 = reinterpret_cast<float*>(dweight);
+          p.f32_mode = (ci == 0 && !accumulate_dweight) ? F32_STORE : F32_ADD;
+        } else {
+          p.out_f32 = dw32;
+          p.out_bf16 = reinterpret_cast<uint16_t*>(dweight); p.ld_bf16 = H;
+          p.f32_mode = last ? F32_ADD_TO_BF16 : (ci == 0 ? F32_STORE : F32_ADD);
+        }
+        p.ld_f32 = H;
+        if ((rc = launch_gemm<EPI_F32, true, true>(ta, tb, p, v_tiles, s))) return rc;
+      }
+    }
+  }
+  return IKRL_OK;
+}
+
+int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(ws && status_out, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_status: null pointer");
+  cudaStream_t s = as_stream(stream);
+  int v = 0;
+  IKRL_CUDA(cudaMemcpyAsync(&v, ws, sizeof(int), cudaMemcpyDeviceToHost, s));
+  IKRL_CUDA(cudaStreamSynchronize(s));
+  *status_out = v;
+  if (v != 0) {
+    set_error("device error 0x%x recorded by a tensor-core kernel (bounded wait expired)", v);
+    return IKRL_ERR_DEVICE;
+  }
+  return IKRL_OK;
+}
+
+}  // extern "C"

@@ -52,12 +52,35 @@ __device__ inline void group_stats(const float* r, int G, double& mean, double& 
   std_ = G > 1 ? sqrt(q / (G - 1)) : __longlong_as_double(0x7ff8000000000000ll);
 }
 
+// out[t] = a * mask[t] over one row; 16 tokens per step when the row is 16-byte aligned.
+__device__ __forceinline__ void broadcast_row(float a, const uint8_t* __restrict__ mrow, float* __restrict__ arow,
+                                              int T) {
+  int t0 = 0;
+  if (((reinterpret_cast<uintptr_t>(mrow) & 15) == 0) && ((reinterpret_cast<uintptr_t>(arow) & 15) == 0)) {
+    const int n16 = T >> 4;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+      const uint4 m = __ldg(reinterpret_cast<const uint4*>(mrow) + i);
+      const uint32_t w[4] = {m.x, m.y, m.z, m.w};
+      float4* o = reinterpret_cast<float4*>(arow) + 4 * i;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o[k] = make_float4(a * ((w[k] & 0xffu) ? 1.f : 0.f), a * ((w[k] & 0xff00u) ? 1.f : 0.f),
+                           a * ((w[k] & 0xff0000u) ? 1.f : 0.f), a * ((w[k] & 0xff000000u) ? 1.f : 0.f));
+      }
+    }
+    t0 = n16 << 4;
+  }
+  for (int t = t0 + threadIdx.x; t < T; t += blockDim.x) arow[t] = a * (mrow[t] ? 1.f : 0.f);
+}
+
 __global__ void group_adv_kernel(const float* __restrict__ rewards, const uint8_t* __restrict__ mask,
                                  const uint8_t* __restrict__ truncated, int B, int T, int G,
                                  int filter_zero_var, float overlong_penalty, float* __restrict__ adv,
                                  float* __restrict__ row_adv) {
   const int b = blockIdx.x;
   __shared__ float s_adv;
+  // Touch this row's mask early so its loads overlap the group statistics below.
+  if (threadIdx.x * 16 < T) asm volatile("prefetch.global.L2 [%0];" ::"l"(mask + (int64_t)b * T + threadIdx.x * 16));
   if (threadIdx.x == 0) {
     const int g0 = (b / G) * G;
     double mean, sd;
@@ -75,19 +98,13 @@ __global__ void group_adv_kernel(const float* __restrict__ rewards, const uint8_
     if (row_adv) row_adv[b] = a;
   }
   __syncthreads();
-  const float a = s_adv;
-  const uint8_t* mrow = mask + (int64_t)b * T;
-  float* arow = adv + (int64_t)b * T;
-  for (int t = threadIdx.x; t < T; t += blockDim.x) arow[t] = a * (mrow[t] ? 1.f : 0.f);
+  broadcast_row(s_adv, mask + (int64_t)b * T, adv + (int64_t)b * T, T);
 }
 
 __global__ void broadcast_adv_kernel(const float* __restrict__ rewards, const uint8_t* __restrict__ mask,
                                      int B, int T, float* __restrict__ adv) {
   const int b = blockIdx.x;
-  const float a = rewards[b];
-  const uint8_t* mrow = mask + (int64_t)b * T;
-  float* arow = adv + (int64_t)b * T;
-  for (int t = threadIdx.x; t < T; t += blockDim.x) arow[t] = a * (mrow[t] ? 1.f : 0.f);
+  broadcast_row(rewards[b], mask + (int64_t)b * T, adv + (int64_t)b * T, T);
 }
 
 // One thread per (group, position): normalise the G token rewards of that column.
@@ -344,7 +361,31 @@ __device__ __forceinline__ float token_step(const LossArgs& a, float lp, float o
   return dlp;
 }
 
-template <int FAMILY, bool BF16>
+template <bool BF16>
+__device__ __forceinline__ void load_lp4(const void* p, int64_t q, float (&x)[4]) {
+  if constexpr (BF16) {
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(p) + q);
+    x[0] = bf16lo(w.x); x[1] = bf16hi(w.x); x[2] = bf16lo(w.y); x[3] = bf16hi(w.y);
+  } else {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p) + q);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  }
+}
+template <bool BF16>
+__device__ __forceinline__ void store_lp4(void* p, int64_t q, const float (&x)[4]) {
+  if constexpr (BF16) {
+    reinterpret_cast<uint2*>(p)[q] = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+  } else {
+    reinterpret_cast<float4*>(p)[q] = make_float4(x[0], x[1], x[2], x[3]);
+  }
+}
+__device__ __forceinline__ void ld4(const float* p, int64_t q, float (&x)[4]) {
+  const float4 v = __ldg(reinterpret_cast<const float4*>(p) + q);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+
+// VEC: four tokens per thread per step with 16-byte loads (n % 4 == 0, aligned pointers).
+template <int FAMILY, bool BF16, bool VEC>
 __global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
   __shared__ bool am_last;
@@ -356,19 +397,41 @@ __global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
   const bool whiten_on = a.whiten != nullptr && a.whiten[3] != 0.f;
   const float wmean = whiten_on ? a.whiten[0] : 0.f, wstd = whiten_on ? a.whiten[1] : 0.f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
-    const float lp = load_lp<BF16>(a.new_lp, i);
-    const float old = __ldg(a.old_lp + i);
-    const float ref = a.ref_lp ? __ldg(a.ref_lp + i) : 0.f;
-    const float adv = __ldg(a.adv + i);
-    const uint8_t mk = __ldg(a.mask + i);
-    const float vv = a.values ? __ldg(a.values + i) : 0.f;
-    const float ov = a.values ? __ldg(a.old_values + i) : 0.f;
-    float dval = 0.f;
-    const float d = token_step<FAMILY>(a, lp, old, ref, adv, mk, inv_n, wmean, wstd, whiten_on,
-                                       vv, ov, dval, acc);
-    if (a.dlp) store_lp<BF16>(a.dlp, i, d);
-    if (a.dvalues) a.dvalues[i] = dval;
+  if constexpr (VEC) {
+    const int64_t nq = a.n >> 2;
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += stride) {
+      float lp[4], old[4], ref[4] = {0.f, 0.f, 0.f, 0.f}, adv[4], vv[4] = {0.f, 0.f, 0.f, 0.f},
+            ov[4] = {0.f, 0.f, 0.f, 0.f}, d[4], dv[4] = {0.f, 0.f, 0.f, 0.f};
+      load_lp4<BF16>(a.new_lp, q, lp);
+      ld4(a.old_lp, q, old);
+      if (a.ref_lp) ld4(a.ref_lp, q, ref);
+      ld4(a.adv, q, adv);
+      const uint32_t mw = __ldg(reinterpret_cast<const uint32_t*>(a.mask) + q);
+      if (a.values) { ld4(a.values, q, vv); ld4(a.old_values, q, ov); }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint8_t mk = (uint8_t)((mw >> (8 * j)) & 0xffu);
+        d[j] = token_step<FAMILY>(a, lp[j], old[j], ref[j], adv[j], mk, inv_n, wmean, wstd, whiten_on, vv[j],
+                                  ov[j], dv[j], acc);
+      }
+      if (a.dlp) store_lp4<BF16>(a.dlp, q, d);
+      if (a.dvalues) reinterpret_cast<float4*>(a.dvalues)[q] = make_float4(dv[0], dv[1], dv[2], dv[3]);
+    }
+  } else {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+      const float lp = load_lp<BF16>(a.new_lp, i);
+      const float old = __ldg(a.old_lp + i);
+      const float ref = a.ref_lp ? __ldg(a.ref_lp + i) : 0.f;
+      const float adv = __ldg(a.adv + i);
+      const uint8_t mk = __ldg(a.mask + i);
+      const float vv = a.values ? __ldg(a.values + i) : 0.f;
+      const float ov = a.values ? __ldg(a.old_values + i) : 0.f;
+      float dval = 0.f;
+      const float d = token_step<FAMILY>(a, lp, old, ref, adv, mk, inv_n, wmean, wstd, whiten_on,
+                                         vv, ov, dval, acc);
+      if (a.dlp) store_lp<BF16>(a.dlp, i, d);
+      if (a.dvalues) a.dvalues[i] = dval;
+    }
   }
 
   double v[kTokenSums];
@@ -384,10 +447,19 @@ __global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
   __syncthreads();
   if (am_last) {
     __threadfence();
-    if (threadIdx.x < kTokenSums) {
-      double s = 0.0;
-      for (unsigned b = 0; b < gridDim.x; ++b) s += __ldcg(a.partials + (int64_t)b * IKRL_LOSS_NSUMS + threadIdx.x);
-      a.sums[threadIdx.x] = s;
+    // Fixed-order reduction of the per-block partials by the whole block: thread i takes blocks
+    // i, i + blockDim, ... in order, then the block tree combines the threads.
+    double t[kTokenSums];
+#pragma unroll
+    for (int i = 0; i < kTokenSums; ++i) t[i] = 0.0;
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+#pragma unroll
+      for (int i = 0; i < kTokenSums; ++i) t[i] += __ldcg(a.partials + (int64_t)b * IKRL_LOSS_NSUMS + i);
+    }
+    block_sum<double, kTokenSums>(t, scratch);
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int i = 0; i < kTokenSums; ++i) a.sums[i] = t[i];
     }
     // Batch-level terms: rewards.mean() and the zero-variance group count (dapo.py:132-135).
     double r[2] = {0.0, 0.0};
@@ -538,7 +610,7 @@ __global__ void simpo_bwd_kernel(const float* __restrict__ row_coef, const uint8
   }
 }
 
-int loss_grid(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, kLossThreads), kLossMaxBlocks)); }
+int loss_grid(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(cdiv(n, 4), kLossThreads), kLossMaxBlocks)); }
 
 }  // namespace
 }  // namespace ikrl
@@ -674,13 +746,19 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
   IKRL_CUDA(cudaMemsetAsync(a.ticket, 0, sizeof(unsigned), s));
   const int grid = loss_grid(n);
   const bool bf = lp_dtype == IKRL_DTYPE_BF16;
+  auto al = [](const void* p, uintptr_t m) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
+  const bool vec = (n % 4 == 0) && al(new_lp, bf ? 8 : 16) && al(old_lp, 16) && al(ref_lp, 16) && al(adv, 16) &&
+                   al(mask, 4) && al(values, 16) && al(old_values, 16) && al(dlp_out, bf ? 8 : 16) &&
+                   al(dvalues_out, 16);
+#define IKRL_LAUNCH_LOSS(FAM, BF, VEC) clip_loss_kernel<FAM, BF, VEC><<<grid, kLossThreads, 0, s>>>(a)
   if (params->family == IKRL_LOSS_GRPO) {
-    if (bf) clip_loss_kernel<IKRL_LOSS_GRPO, true><<<grid, kLossThreads, 0, s>>>(a);
-    else clip_loss_kernel<IKRL_LOSS_GRPO, false><<<grid, kLossThreads, 0, s>>>(a);
+    if (bf) { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, true, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, true, false); }
+    else { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, false, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, false, false); }
   } else {
-    if (bf) clip_loss_kernel<IKRL_LOSS_PPO, true><<<grid, kLossThreads, 0, s>>>(a);
-    else clip_loss_kernel<IKRL_LOSS_PPO, false><<<grid, kLossThreads, 0, s>>>(a);
+    if (bf) { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, true, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, true, false); }
+    else { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, false, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, false, false); }
   }
+#undef IKRL_LAUNCH_LOSS
   return check_launch("clip_loss_kernel");
 }
 

@@ -7,6 +7,8 @@ current stream; nothing here computes on the CPU or falls back to ATen for the h
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _native as N
@@ -342,3 +344,114 @@ def logits_logprob_raw(logits: torch.Tensor, ids: torch.Tensor, with_target: boo
     call("ikrl_logits_logprob_fwd", ptr(logits), i64(logits.stride(0)), ptr(ids), i64(Nr), i32(V), ptr(logp),
          ptr(lse), ptr(tgt), N.stream_of(dev))
     return (logp, lse, tgt) if with_target else (logp, lse)
+
+
+# ---------------------------------------------------------------------------------------------
+# K1: fused LM-head log-prob (policy.py:124-191)
+# ---------------------------------------------------------------------------------------------
+
+DEFAULT_DS_CHUNK_BYTES = 8 << 30  # bf16 dlogits workspace of one backward chunk
+
+
+def default_chunk_rows(N: int, V: int, budget_bytes: int = DEFAULT_DS_CHUNK_BYTES) -> int:
+    lds = (V + 63) // 64 * 64
+    rows = max(128, (budget_bytes // (2 * lds)) // 128 * 128)
+    return min(N, rows) if N > rows else N
+
+
+def lmhead_forward_raw(hidden: torch.Tensor, weight: torch.Tensor, ids: torch.Tensor):
+    """(logp [N] fp32, lse [N] fp32) of the fused kernel; hidden [N, H] and weight [V, H] bf16."""
+    dev = N.require_cuda(hidden, weight, ids)
+    Nr, H = hidden.shape
+    V = weight.shape[0]
+    logp = torch.empty(Nr, dtype=torch.float32, device=dev)
+    lse = torch.empty(Nr, dtype=torch.float32, device=dev)
+    nbytes = int(N.lib().ikrl_lmhead_fwd_workspace_bytes(Nr, H, V))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    call("ikrl_lmhead_logprob_fwd", ptr(hidden), ptr(weight), ptr(ids), i64(Nr), i32(H), i32(V), ptr(logp),
+         ptr(lse), ptr(ws), sz(nbytes), N.stream_of(dev))
+    if _CHECK_DEVICE_STATUS:
+        lmhead_status(ws)
+    return logp, lse
+
+
+def lmhead_backward_raw(hidden, weight, ids, lse, dlogp, want_dh=True, want_dw=True, dw_dtype=torch.bfloat16,
+                        chunk_rows: int | None = None, dweight_out: torch.Tensor | None = None):
+    """(dhidden bf16 [N, H] | None, dweight [V, H] | None) for upstream dlogp [N] fp32."""
+    dev = N.require_cuda(hidden, weight, ids, lse, dlogp)
+    Nr, H = hidden.shape
+    V = weight.shape[0]
+    if chunk_rows is None:
+        chunk_rows = default_chunk_rows(Nr, V)
+    dh = torch.empty_like(hidden) if want_dh else None
+    accumulate = 0
+    if want_dw:
+        if dweight_out is not None:
+            dw = dweight_out
+            accumulate = 1
+        else:
+            dw = torch.empty(V, H, dtype=dw_dtype, device=dev)
+    else:
+        dw = None
+    dcode = N.IKRL_DTYPE_F32 if (dw is not None and dw.dtype == torch.float32) else N.IKRL_DTYPE_BF16
+    nbytes = int(N.lib().ikrl_lmhead_bwd_workspace_bytes(Nr, H, V, chunk_rows, dcode, accumulate))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    call("ikrl_lmhead_logprob_bwd", ptr(hidden), ptr(weight), ptr(ids), ptr(lse), ptr(dlogp), i64(Nr), i32(H),
+         i32(V), i64(chunk_rows), ptr(dh), ptr(dw), i32(dcode), i32(accumulate), ptr(ws), sz(nbytes),
+         N.stream_of(dev))
+    if _CHECK_DEVICE_STATUS:
+        lmhead_status(ws)
+    return dh, dw
+
+
+def lmhead_status(ws: torch.Tensor) -> None:
+    """Raise if a tensor-core kernel that used `ws` recorded a device-side error (synchronises)."""
+    st = N.c_int32(0)
+    call("ikrl_lmhead_status", ptr(ws), N.byref(st), N.stream_of(ws.device))
+
+
+# Tests set this to read the device status word after every tensor-core call (a host sync).
+_CHECK_DEVICE_STATUS = os.environ.get("INVOKERL_B200_CHECK_STATUS", "0") == "1"
+
+
+class LMHeadLogProb(torch.autograd.Function):
+    """log p(targets) of hidden @ weight.T without materialising the logits; fp32 output."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, ids, chunk_rows):
+        logp, lse = lmhead_forward_raw(hidden, weight, ids)
+        ctx.save_for_backward(hidden, weight, ids, lse)
+        ctx.chunk_rows = chunk_rows
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        hidden, weight, ids, lse = ctx.saved_tensors
+        want_dh, want_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (want_dh or want_dw):
+            return None, None, None, None
+        dh, dw = lmhead_backward_raw(hidden, weight, ids, lse, g.contiguous().float(), want_dh, want_dw,
+                                     weight.dtype if weight.dtype == torch.float32 else torch.bfloat16,
+                                     ctx.chunk_rows)
+        return dh, dw, None, None
+
+
+def lmhead_logprob(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
+                   chunk_rows: int | None = None) -> torch.Tensor:
+    """Fused F.linear(hidden, weight) + log-softmax gather: hidden [..., H], targets [...] -> fp32 [...].
+    Targets of -100 give 0 (ignored rows)."""
+    N.require_cuda(hidden, weight, targets)
+    H = hidden.shape[-1]
+    shape = targets.shape
+    h = hidden.reshape(-1, H)
+    if h.dtype != torch.bfloat16:
+        h = h.to(torch.bfloat16)
+    if not h.is_contiguous():
+        h = h.contiguous()
+    w = weight if weight.dtype == torch.bfloat16 else weight.to(torch.bfloat16)
+    if not w.is_contiguous():
+        w = w.contiguous()
+    ids = targets.reshape(-1).to(torch.int64).contiguous()
+    if h.shape[0] != ids.shape[0]:
+        raise ValueError(f"{h.shape[0]} hidden rows but {ids.shape[0]} targets")
+    return LMHeadLogProb.apply(h, w, ids, chunk_rows).reshape(shape)

@@ -82,16 +82,19 @@ def algo_cases() -> None:
     save("grpo_bf16_simplekl", kind="grpo", kwargs=dict(clip_eps=0.2, beta=0.1, kl_type="simple"),
          batch=batch_dict(b), new_lp=nl, out=run_algo(GRPO(clip_eps=0.2, beta=0.1, kl_type="simple"), b, nl))
 
-    # Edge cases: an all-masked row, a zero-variance group, ratios exactly at 1 +- eps
-    # (clamp boundary, min ties), zero advantages.
+    # Edge cases: an all-masked row, a zero-variance group (zero advantages, min ties), ratios
+    # just inside and just outside both clamp bounds and exactly 1 (a ratio exactly at 1 +- eps
+    # depends on the last ulp of exp, which differs between libraries, so it is not pinned).
     b = rollout_batch(2, 4, 32, prompt_len=(4, 8), completion_len=(8, 20), seed=3)
     b.response_mask[0] = False
     b.rewards[4:8] = 1.0
     nl = b.extras["new_log_probs"].clone()
     eps = 0.2
-    r = torch.tensor([1.0 - eps, 1.0 + eps, 1.0, 0.5, 2.0])
-    nl[1, 10:15] = b.old_log_probs[1, 10:15] + torch.log(r)
-    nl[2, 10:15] = b.old_log_probs[2, 10:15] + torch.log(r)
+    r = torch.tensor([1.0 - eps - 1e-3, 1.0 - eps + 1e-3, 1.0, 1.0 + eps - 1e-3, 1.0 + eps + 1e-3, 0.5, 2.0])
+    for row in (1, 2, 5):
+        nl[row, 10:17] = b.old_log_probs[row, 10:17] + torch.log(r)
+        b.response_mask[row, 10:17] = True
+    nl[3, 12] = b.old_log_probs[3, 12]  # log ratio exactly 0
     save("grpo_edges", kind="grpo", kwargs=dict(clip_eps=eps, beta=0.04), batch=batch_dict(b), new_lp=nl,
          out=run_algo(GRPO(clip_eps=eps, beta=0.04), b, nl))
 

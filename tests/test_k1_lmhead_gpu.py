@@ -1,0 +1,137 @@
+"""K1 parity on the GPU: the fused tcgen05 LM-head log-prob forward/backward against the
+reference golden vectors, the CPU oracle, and size-independent properties at full size."""
+
+import pytest
+import torch
+
+import oracle
+from helpers import load
+from invokerl_b200 import ops
+from invokerl_b200.synthetic import lmhead_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def check_device_status(monkeypatch):
+    # read the kernels' device status word after every call
+    monkeypatch.setattr(ops, "_CHECK_DEVICE_STATUS", True)
+
+
+def rel_fro(a, b):
+    return float((a.float() - b.float()).norm() / b.float().norm().clamp(min=1e-30))
+
+
+def run_k1(h, w, t, g, chunk_rows=None, dw_dtype=torch.bfloat16):
+    hd, wd, td = h.to(DEV), w.to(DEV), t.to(DEV)
+    lp, lse = ops.lmhead_forward_raw(hd, wd, td)
+    dh, dw = ops.lmhead_backward_raw(hd, wd, td, lse, g.to(DEV).float().contiguous(), dw_dtype=dw_dtype,
+                                     chunk_rows=chunk_rows)
+    torch.cuda.synchronize()
+    return lp.cpu(), lse.cpu(), dh.cpu(), dw.cpu()
+
+
+def test_golden_small():
+    g = load("lmhead_small")
+    h = g["hidden"].reshape(-1, g["hidden"].shape[-1])
+    t = g["targets"].reshape(-1)
+    lp, _, dh, dw = run_k1(h, g["weight"], t, g["upstream"].reshape(-1))
+    assert float((lp - g["lp_fp32"].reshape(-1)).abs().max()) <= 2e-3
+    assert rel_fro(dh, g["dh_fp32"].reshape(dh.shape)) <= 1e-2
+    assert rel_fro(dw, g["dw_fp32"]) <= 1e-2
+
+
+def test_golden_reference_chunked_branch():
+    """The reference's chunk loop (B*T*V*4 >= 2 GiB) on the full vocabulary; H=32 < one K tile."""
+    g = load("lmhead_chunked_seed")
+    B, T, H, V = g["shape"]
+    li = lmhead_inputs(B * T, H, V, seed=g["seed"], w_std=g["w_std"])
+    lp, _ = ops.lmhead_forward_raw(li.hidden.to(DEV), li.weight.to(DEV), li.targets.to(DEV))
+    assert float((lp.cpu() - g["lp_fp32"].reshape(-1)).abs().max()) <= 2e-3
+
+
+@pytest.mark.parametrize("N,H,V,chunk", [
+    (300, 128, 5000, None),        # ragged rows and vocab tail (5000 = 19*256 + 136)
+    (129, 64, 1000, 64),           # several chunks, tail chunk of 1 row
+    (600, 256, 33000, 256),        # 3 chunks with a ragged last one
+    (256, 1024, 151936, None),     # Qwen3-0.6B head shape
+    (160, 4096, 151936, 128),      # Qwen3-8B head shape, 2 chunks
+    (40, 200, 777, None),          # H not a multiple of 64, V odd
+])
+def test_against_oracle(N, H, V, chunk):
+    li = lmhead_inputs(N, H, V, seed=N + H + V, w_std=0.05 if H > 512 else 0.3)
+    gen = torch.Generator().manual_seed(1)
+    g = torch.randn(N, generator=gen) * torch.bernoulli(torch.full((N,), 0.7), generator=gen)
+    lp, lse, dh, dw = run_k1(li.hidden, li.weight, li.targets, g, chunk_rows=chunk)
+    lp_o, dh_o, dw_o = oracle.lmhead_logprob_grads(li.hidden, li.weight, li.targets, g)
+    assert float((lp - lp_o).abs().max()) <= 2e-3
+    assert rel_fro(dh, dh_o) <= 1e-2
+    assert rel_fro(dw, dw_o) <= 1e-2
+    # rows with zero upstream have exactly zero hidden gradient
+    z = g == 0
+    if z.any():
+        assert float(dh[z].abs().max()) == 0.0
+
+
+def test_fp32_dweight_accumulates():
+    N, H, V = 200, 128, 3000
+    li = lmhead_inputs(N, H, V, seed=3, w_std=0.3)
+    g = torch.randn(N, generator=torch.Generator().manual_seed(2))
+    hd, wd, td = li.hidden.to(DEV), li.weight.to(DEV), li.targets.to(DEV)
+    _, lse = ops.lmhead_forward_raw(hd, wd, td)
+    base = torch.randn(V, H, device=DEV)
+    acc = base.clone()
+    ops.lmhead_backward_raw(hd, wd, td, lse, g.to(DEV), want_dh=False, dweight_out=acc, chunk_rows=128)
+    _, _, dw_o = oracle.lmhead_logprob_grads(li.hidden, li.weight, li.targets, g)
+    assert rel_fro((acc - base).cpu(), dw_o) <= 1e-2
+
+
+def test_ignored_rows_and_autograd_function():
+    N, H, V = 96, 64, 2048
+    li = lmhead_inputs(N, H, V, seed=5, w_std=0.3)
+    t = li.targets.clone()
+    t[::7] = -100
+    h = li.hidden.to(DEV).requires_grad_(True)
+    w = li.weight.to(DEV).requires_grad_(True)
+    lp = ops.lmhead_logprob(h, w, t.to(DEV))
+    up = torch.randn(N, generator=torch.Generator().manual_seed(4))
+    (lp * up.to(DEV)).sum().backward()
+    keep = t != -100
+    assert (lp.detach().cpu()[~keep] == 0).all()
+    lp_o, dh_o, dw_o = oracle.lmhead_logprob_grads(li.hidden[keep], li.weight, t[keep], up[keep])
+    assert float((lp.detach().cpu()[keep] - lp_o).abs().max()) <= 2e-3
+    assert float(h.grad.cpu()[~keep].abs().max()) == 0.0
+    assert rel_fro(h.grad.cpu()[keep], dh_o) <= 1e-2
+    assert rel_fro(w.grad.cpu(), dw_o) <= 1e-2
+
+
+@pytest.mark.parametrize("N,H", [(131072, 1024), (65536, 4096)])
+def test_full_size_properties(N, H):
+    """Config-3 size (and half of config 4's rows): log-probs of sampled rows against the oracle;
+    dH of sampled rows; dW on sampled vocab rows from the kernel's own lse; sum_v dW[v] = 0."""
+    V = 151936
+    gen = torch.Generator(device=DEV).manual_seed(7)
+    h = torch.randn(N, H, device=DEV, generator=gen).to(torch.bfloat16)
+    w = (0.02 * torch.randn(V, H, device=DEV, generator=gen)).to(torch.bfloat16)
+    t = torch.randint(0, V, (N,), device=DEV, generator=gen)
+    g = torch.randn(N, device=DEV, generator=gen)
+    lp, lse = ops.lmhead_forward_raw(h, w, t)
+    dh, dw = ops.lmhead_backward_raw(h, w, t, lse, g, dw_dtype=torch.float32)
+    torch.cuda.synchronize()
+    rows = torch.randint(0, N, (48,), generator=torch.Generator().manual_seed(0))
+    hs, ws, ts, gs = h[rows].cpu(), w.cpu(), t[rows].cpu(), g[rows].cpu()
+    lp_o, dh_o, _ = oracle.lmhead_logprob_grads(hs, ws, ts, gs)
+    assert float((lp[rows].cpu() - lp_o).abs().max()) <= 2e-3
+    lse_o = torch.logsumexp(hs.float() @ ws.float().t(), dim=1)
+    assert float((lse[rows].cpu() - lse_o).abs().max()) <= 2e-3
+    assert rel_fro(dh[rows].cpu(), dh_o) <= 1e-2
+    # dW on a vocab subset: sum_n g_n ([t_n = v] - exp(h_n.W_v - lse_n)) h_n, from the kernel's lse
+    vs = torch.randint(0, V, (16,), generator=torch.Generator().manual_seed(1))
+    hf = h.float()
+    p = torch.exp(hf @ w[vs.to(DEV)].float().t() - lse[:, None])  # [N, 16] on the GPU (fp32 torch)
+    onehot = (t[:, None] == vs.to(DEV)[None, :]).float()
+    dw_sub = ((onehot - p) * g[:, None]).t() @ hf
+    assert rel_fro(dw[vs.to(DEV)], dw_sub) <= 1e-2
+    colsum = dw.sum(dim=0)
+    assert float(colsum.norm() / dw.norm()) <= 1e-2
