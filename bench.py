@@ -117,7 +117,6 @@ def make_workload(rank: int, world: int, device: torch.device, H: int = H_8B):
     batch = rollout_batch(B_GLOBAL // G, G, T, prompt_len=(64, 512), completion_len=(512, 3584), vocab=V, seed=0)
     local = shard_batch(batch, rank, world)
     Bl = local.token_ids.shape[0]
-    g0 = (batch.token_ids.shape[0] // G) * 0  # groups are generated by absolute index below
     first_group = int(local.group_ids[0]) if local.group_ids is not None else 0
     # Hidden rows and W generated on the device per prompt group: the global data is the same for
     # any number of ranks.
@@ -129,9 +128,18 @@ def make_workload(rank: int, world: int, device: torch.device, H: int = H_8B):
     gw = torch.Generator(device=device).manual_seed(7)
     weight = (0.02 * torch.randn(V, H, device=device, generator=gw)).to(torch.bfloat16)
     ids = local.token_ids.reshape(-1).to(device)
+    # Rollout-time log-probs of the same policy: old = lp + N(0, 0.05), ref = lp + N(0, 0.1), so
+    # ratios and KL terms have realistic magnitudes (the config's distributions around -Exp(1)
+    # describe a trained policy; here the policy is the random-init head itself).
+    from invokerl_b200 import ops
+
+    lp, _ = ops.lmhead_forward_raw(hidden, weight, ids)
+    gr = torch.Generator(device=device).manual_seed(11 + first_group)
+    local.old_log_probs = (lp.view(Bl, T) + 0.05 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
+    local.ref_log_probs = (lp.view(Bl, T) + 0.1 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
+    del lp
     dev_batch = type(local)(**{k: (v.to(device) if isinstance(v, torch.Tensor) else v)
                                for k, v in vars(local).items() if k != "extras"}, extras={})
-    del g0
     return local, dev_batch, hidden, weight, ids
 
 
@@ -219,7 +227,7 @@ def run_native(args, rank, world, device) -> dict | None:
     ms, k1_ms = float(t[0]), float(t[1])
 
     # ---- end to end through the public API with host (pinned) buffers ----
-    e2e = run_e2e(args, local, algo, weight, device, world)
+    e2e = run_e2e(args, local, algo, hidden, weight, device, world)
 
     if rank != 0:
         return None
@@ -274,15 +282,14 @@ def run_native(args, rank, world, device) -> dict | None:
     return res
 
 
-def run_e2e(args, local, algo, weight, device, world) -> dict:
+def run_e2e(args, local, algo, hidden, weight, device, world) -> dict:
     """Same step through the public API with inputs in pinned host memory: every step copies the
     rank's hidden rows, token ids, old/ref log-probs, masks and rewards to the device and reads the
     loss and metrics back (compute_loss returns them as Python floats)."""
     from invokerl_b200.algorithms import RolloutBatch
 
     Bl = local.token_ids.shape[0]
-    gen = torch.Generator(device=device).manual_seed(4242)
-    host_hidden = torch.randn(Bl * T, H_8B, device=device, generator=gen).to(torch.bfloat16).cpu().pin_memory()
+    host_hidden = hidden.detach().cpu().pin_memory()
     host = {k: v.pin_memory() for k, v in vars(local).items() if isinstance(v, torch.Tensor)}
     h2d = host_hidden.numel() * 2 + sum(host[k].numel() * host[k].element_size()
                                         for k in ("token_ids", "response_mask", "old_log_probs",
@@ -341,9 +348,12 @@ def cpu_sample(rows: int, steps: int = 1, H: int = H_8B) -> tuple[float, int, fl
     adv = oracle.group_advantages(rewards, torch.ones(G, 1, dtype=torch.bool), G).reshape(-1)
     adv = adv.repeat_interleave((rows + G - 1) // G)[:rows]
 
+    hh = h.requires_grad_(True)
+    ww = w.requires_grad_(True)
+
     def one():
-        hh = h.clone().requires_grad_(True)
-        ww = w.clone().requires_grad_(True)
+        hh.grad = None
+        ww.grad = None
         logits = hh @ ww.t()
         lp = torch.gather(logits, 1, li.targets[:, None]).squeeze(1) - torch.logsumexp(logits, dim=1)
         ratio = torch.exp(lp - old)
@@ -414,10 +424,10 @@ def main() -> int:
         res = run_native(args, rank, world, device)
         if rank == 0 and res is not None:
             if world == 1 and not args.no_cpu_baseline:
-                rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", "16"))
-                tok_s, cores, dt = cpu_sample(rows, 2)
+                rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", "32"))
+                tok_s, cores, dt = cpu_sample(rows, 3)
                 res["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
-                                       "sample": f"{rows} rows of the workload per step, 2 steps "
+                                       "sample": f"{rows} rows of the workload per step, 3 steps "
                                                  f"({dt:.1f} s/step; fp32 torch on the host CPU)"}
             print(json.dumps(res), flush=True)
     finally:

@@ -263,11 +263,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
           run_s += cs;
+          // Target gather without a dynamically indexed register array (which would go to local
+          // memory): exactly one term is v[rel] * 1, every other term adds zero.
           const int64_t rel = tgt - col0;
           if (rel >= 0 && rel < nvalid) {
+            const int rr = (int)rel;
+            float acc_t = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i == (int)rel) tval = v[i];
+            for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
+            tval = acc_t;
           }
         } else if constexpr (EPI == EPI_DLOGITS) {
           uint32_t w[16];
