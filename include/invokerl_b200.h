@@ -221,6 +221,17 @@ IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, con
                                      int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
                                      size_t ws_bytes, void* stream);
 
+/* Allocation-free variant of ikrl_lmhead_logprob_fwd.  It has no counterpart in the reference.
+ * For callers that cannot allocate device memory when they need log-probs (during stream capture
+ * into a CUDA graph, inside hosts whose own allocator owns all device memory): the scratch comes
+ * from a 4 MiB array built into the library, held on every GPU that loads it until exit.  Calls
+ * needing more scratch (large N) fail with IKRL_ERR_WORKSPACE.  All calls on a device share the
+ * array, so calls that overlap on the GPU race; the first call on a device looks up the array's
+ * address and should come before any stream capture. */
+IKRL_API int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* weight,
+                                             const int64_t* ids, int64_t N, int32_t H, int32_t V,
+                                             float* logp, float* lse, void* stream);
+
 /* Device status word of the last K1 call that used workspace `ws` (synchronises `stream`):
  * IKRL_OK, or IKRL_ERR_DEVICE with *status_out = the recorded code (a bounded wait expired). */
 IKRL_API int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream);

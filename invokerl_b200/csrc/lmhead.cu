@@ -655,3 +655,68 @@ int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream) {
 }
 
 }  // extern "C"
+
+// ---- allocation-free forward -------------------------------------------------------------------
+//
+// Some callers cannot allocate device memory at the moment they need log-probs: code running
+// while a stream is being captured into a CUDA graph (an allocation there is not part of the
+// graph and may be refused), hosts that embed this library behind their own device-memory
+// manager and forbid side allocations, or callers whose framework has already reserved all free
+// memory in its pool.  For them the forward below takes its scratch (the per-split row statistics
+// and the device error word) from a fixed array compiled into the library instead of a
+// caller-provided workspace.
+//
+// Limits and sharing rules:
+//   * the array is kNoAllocScratchBytes (4 MiB) and lives on every GPU that loads the library
+//     until the process exits; calls whose scratch would not fit are rejected with
+//     IKRL_ERR_WORKSPACE (the message gives the sizes) -- use ikrl_lmhead_logprob_fwd instead;
+//   * every call on a device uses the same array: calls whose kernels may overlap on the GPU
+//     (different streams without ordering) race on it, so order them on one stream;
+//   * the array keeps whatever the last call left in it; the error word at its start is cleared
+//     by every call, the rest is fully rewritten before it is read;
+//   * the first call on each device looks up the array's device address (cudaGetSymbolAddress)
+//     with that device current; make that first call before any stream capture begins.
+
+namespace ikrl {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  IKRL_CUDA(cudaGetDevice(&dev));
+  IKRL_REQUIRE(dev >= 0 && dev < kMaxDevices, IKRL_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    IKRL_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return IKRL_OK;
+}
+
+}  // namespace
+}  // namespace ikrl
+
+extern "C" int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* weight, const int64_t* ids,
+                                               int64_t N, int32_t H, int32_t V, float* logp, float* lse,
+                                               void* stream) {
+  clear_error();
+  int rc = check_common(hidden, weight, ids, N, H, V, "ikrl_lmhead_logprob_fwd_noalloc");
+  if (rc) return rc;
+  const size_t need = ikrl_lmhead_fwd_workspace_bytes(N, H, V);
+  IKRL_REQUIRE(need <= kNoAllocScratchBytes, IKRL_ERR_WORKSPACE,
+               "ikrl_lmhead_logprob_fwd_noalloc: N=%lld rows (H=%d, V=%d) need %zu bytes of scratch, more than the "
+               "built-in %zu; split the rows or call ikrl_lmhead_logprob_fwd with a workspace",
+               (long long)N, H, V, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch))) return rc;
+  return ikrl_lmhead_logprob_fwd(hidden, weight, ids, N, H, V, logp, lse, scratch, kNoAllocScratchBytes, stream);
+}
