@@ -1,17 +1,27 @@
-"""Benchmark of the log-prob + GRPO-loss hot path, forward and backward, on 1..8 B200s.
+"""Benchmark of invokerl's log-prob + GRPO-loss hot path (forward and backward) on 1..8 B200s.
 
-Workload (the Qwen3-8B LM-head configuration): hidden bf16 [B*T, 4096] ~ N(0,1), untied
-W_lm bf16 [151936, 4096] ~ N(0, 0.02), B = 128 (16 prompts x group 8), T = 4096, completion
-length U[512, 3584]; one step = fused LM-head log-prob forward over all B*T rows, GRPO group
-advantages, GRPO clipped-ratio + k3-KL loss with the token-count all-reduce, backward through the
-loss and the LM head (dHidden and dW).  Rows are sharded over ranks by whole prompt groups (the
-global batch stays B = 128, so scaling is strong).  Inputs are synthetic and seeded.
+Default workload, the headline: the Qwen3-8B LM-head configuration.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+* hidden bf16 [B*T, 4096] ~ N(0,1) and untied W_lm bf16 [151936, 4096] ~ N(0, 0.02);
+* B = 128 (16 prompts x group 8), T = 4096, completion length U[512, 3584];
+* one step = the fused LM-head log-prob forward over all B*T rows, GRPO group advantages, the
+  GRPO clipped-ratio + k3-KL loss with the token-count all-reduce, and the backward through the
+  loss and the LM head (dHidden and dW).
 
-Prints one JSON line (rank 0).  `--impl reference` times the reference algorithm on the host
-CPU cores (the CPU restatement in oracle/, which the reference itself is: torch on the CPU) on a
-bounded row sample of the same workload.
+Rows are sharded over ranks by whole prompt groups. The global batch stays B = 128, so
+scaling is strong. Inputs are synthetic and seeded.
+
+Other workloads (`--workload`), one JSON line each:
+
+* lmhead-0.6b: the Qwen3-0.6B head (H=1024, tied, B=64, T=2048) with the same step.
+* logits: the unfused logits -> log-prob forward + backward, bf16 [16384, 151936].
+* grpo / grpo-hbm: GRPO advantages + loss + backward on a [16, 512] batch, or on its HBM-sized
+  variant [1024, 8192].
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference] [--workload W]
+
+`--impl reference` times the reference algorithm on the host CPU cores, on a bounded sample of
+the same workload. The reference is torch on the CPU, restated in oracle/.
 """
 
 from __future__ import annotations
@@ -35,7 +45,7 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "log-prob+GRPO loss tokens/s fwd+bwd"
 UNIT = "tokens/s"
-H_8B, V, B_GLOBAL, T, G = 4096, 151936, 128, 4096, 8
+V = 151936
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -107,44 +117,9 @@ class ClockSampler:
         }
 
 
-# ---- workload ---------------------------------------------------------------------------------------
-
-
-def make_workload(rank: int, world: int, device: torch.device, H: int = H_8B):
-    from invokerl_b200.distributed import shard_batch
-    from invokerl_b200.synthetic import rollout_batch
-
-    batch = rollout_batch(B_GLOBAL // G, G, T, prompt_len=(64, 512), completion_len=(512, 3584), vocab=V, seed=0)
-    local = shard_batch(batch, rank, world)
-    Bl = local.token_ids.shape[0]
-    first_group = int(local.group_ids[0]) if local.group_ids is not None else 0
-    # Hidden rows and W generated on the device per prompt group: the global data is the same for
-    # any number of ranks.
-    hidden = torch.empty(Bl * T, H, dtype=torch.bfloat16, device=device)
-    for j in range(Bl // G):
-        gen = torch.Generator(device=device).manual_seed(1000 + first_group + j)
-        rows = slice(j * G * T, (j + 1) * G * T)
-        hidden[rows] = torch.randn(G * T, H, device=device, generator=gen).to(torch.bfloat16)
-    gw = torch.Generator(device=device).manual_seed(7)
-    weight = (0.02 * torch.randn(V, H, device=device, generator=gw)).to(torch.bfloat16)
-    ids = local.token_ids.reshape(-1).to(device)
-    # Rollout-time log-probs of the same policy: old = lp + N(0, 0.05), ref = lp + N(0, 0.1), so
-    # ratios and KL terms have realistic magnitudes (the config's distributions around -Exp(1)
-    # describe a trained policy; here the policy is the random-init head itself).
-    from invokerl_b200 import ops
-
-    lp, _ = ops.lmhead_forward_raw(hidden, weight, ids)
-    gr = torch.Generator(device=device).manual_seed(11 + first_group)
-    local.old_log_probs = (lp.view(Bl, T) + 0.05 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
-    local.ref_log_probs = (lp.view(Bl, T) + 0.1 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
-    del lp
-    dev_batch = type(local)(**{k: (v.to(device) if isinstance(v, torch.Tensor) else v)
-                               for k, v in vars(local).items() if k != "extras"}, extras={})
-    return local, dev_batch, hidden, weight, ids
-
-
-class K1Timer:
-    """CUDA events around every fused LM-head call (forward and backward) of the timed steps."""
+class EventTimer:
+    """CUDA events around every call of the wrapped functions while active (the launching stream
+    is the current stream; every op here launches on it)."""
 
     def __init__(self):
         self.pairs: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
@@ -167,36 +142,372 @@ class K1Timer:
         return sum(s.elapsed_time(e) for s, e in self.pairs)
 
 
-def grpo_step(algo, dev_batch, hidden, weight, ids, Bl):
-    from invokerl_b200 import ops
+def to_device_batch(b, device):
+    from invokerl_b200.algorithms import RolloutBatch
 
-    h = hidden.requires_grad_(True) if not hidden.requires_grad else hidden
-    lp = ops.lmhead_logprob(h, weight, ids).view(Bl, T)
-    adv = algo.compute_advantages(dev_batch)
-    loss, metrics = algo.compute_loss(lp, dev_batch, adv)
-    loss.backward()
-    return loss, metrics
+    return RolloutBatch(**{k: (v.to(device, non_blocking=True) if isinstance(v, torch.Tensor) else v)
+                           for k, v in vars(b).items() if k != "extras"}, extras={})
+
+
+def host_batch(b):
+    """Pinned host copy of a RolloutBatch's tensors."""
+    from invokerl_b200.algorithms import RolloutBatch
+
+    return RolloutBatch(**{k: (v.pin_memory() if isinstance(v, torch.Tensor) else v)
+                           for k, v in vars(b).items() if k != "extras"}, extras={})
+
+
+def batch_bytes(b) -> int:
+    return sum(v.numel() * v.element_size() for v in vars(b).values() if isinstance(v, torch.Tensor))
+
+
+# ---- workloads -------------------------------------------------------------------------------------
+
+
+class LMHeadGRPO:
+    """Fused LM-head log-prob + GRPO loss, forward and backward (configs 3 and 4)."""
+
+    PRESETS = {
+        "lmhead-8b": dict(H=4096, B=128, T=4096, prompt=(64, 512), completion=(512, 3584),
+                          name="Qwen3-8B LM head: hidden bf16 [128*4096, 4096], W bf16 [151936, 4096] untied"),
+        "lmhead-0.6b": dict(H=1024, B=64, T=2048, prompt=(64, 256), completion=(32, 256),
+                            name="Qwen3-0.6B LM head: hidden bf16 [64*2048, 1024], W bf16 [151936, 1024] tied"),
+    }
+    G = 8
+
+    def __init__(self, key, args):
+        p = dict(self.PRESETS[key])
+        if args.batch:
+            p["B"] = args.batch
+        self.key, self.p = key, p
+        self.H, self.B, self.T = p["H"], p["B"], p["T"]
+
+    def setup(self, rank, world, device):
+        from invokerl_b200 import ops
+        from invokerl_b200.algorithms import GRPO
+        from invokerl_b200.distributed import shard_batch
+        from invokerl_b200.synthetic import rollout_batch
+
+        H, B, T, G = self.H, self.B, self.T, self.G
+        batch = rollout_batch(B // G, G, T, prompt_len=self.p["prompt"], completion_len=self.p["completion"],
+                              vocab=V, seed=0)
+        local = shard_batch(batch, rank, world)
+        local.extras = {}
+        Bl = local.token_ids.shape[0]
+        first_group = int(local.group_ids[0])
+        # Hidden rows and W are generated on the device per prompt group, so the global data is
+        # the same for any number of ranks.
+        hidden = torch.empty(Bl * T, H, dtype=torch.bfloat16, device=device)
+        for j in range(Bl // G):
+            gen = torch.Generator(device=device).manual_seed(1000 + first_group + j)
+            hidden[j * G * T:(j + 1) * G * T] = torch.randn(G * T, H, device=device, generator=gen).to(torch.bfloat16)
+        gw = torch.Generator(device=device).manual_seed(7)
+        weight = (0.02 * torch.randn(V, H, device=device, generator=gw)).to(torch.bfloat16)
+        ids = local.token_ids.reshape(-1).to(device)
+        # Rollout-time log-probs of the same policy: old = lp + N(0, 0.05), ref = lp + N(0, 0.1), so
+        # ratios and KL terms have realistic sizes for this random-init head.
+        lp, _ = ops.lmhead_forward_raw(hidden, weight, ids)
+        gr = torch.Generator(device=device).manual_seed(11 + first_group)
+        local.old_log_probs = (lp.view(Bl, T) + 0.05 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
+        local.ref_log_probs = (lp.view(Bl, T) + 0.1 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
+        del lp
+        self.local, self.Bl = local, Bl
+        self.dev_batch = to_device_batch(local, device)
+        self.hidden = hidden.requires_grad_(True)
+        self.weight = weight.requires_grad_(True)
+        self.ids = ids
+        self.algo = GRPO(clip_eps=0.2, beta=0.04, row_sharded=world > 1)
+        self.device = device
+
+    def timed_functions(self):
+        return ["lmhead_forward_raw", "lmhead_backward_raw"]
+
+    def _step(self, batch, hidden, ids):
+        from invokerl_b200 import ops
+
+        lp = ops.lmhead_logprob(hidden, self.weight, ids).view(self.Bl, self.T)
+        adv = self.algo.compute_advantages(batch)
+        loss, metrics = self.algo.compute_loss(lp, batch, adv)
+        loss.backward()
+        return float(loss.detach()), metrics
+
+    def step(self):
+        self.hidden.grad = None
+        self.weight.grad = None
+        return self._step(self.dev_batch, self.hidden, self.ids)
+
+    def tokens_per_step(self):
+        return self.B * self.T
+
+    def roofline(self, kernel_ms_per_step, peaks, peak_src):
+        flops = 6.0 * (self.Bl * self.T) * self.H * V
+        achieved = flops / (kernel_ms_per_step / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        return {
+            "kernel": "fused LM-head log-prob fwd+bwd: tcgen05 GEMMs with online-LSE / dlogits epilogues",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": achieved / peak,
+            "frac_of_burst_peak": achieved / peaks["bf16_tflops"],
+            "peak_source": f"{peak_src} bf16 sustained (kernel timed inside a multi-second step)",
+            "algorithmic": "6*N*H*V FLOP per step: fwd 2NHV + dH 2NHV + dW 2NHV (the 2NHV logits "
+                           "recompute of the backward is executed but not counted)",
+            "traffic": None,
+        }
+
+    def config(self, world):
+        return {
+            "workload": self.p["name"] + f", GRPO G={self.G} k3 KL, fwd+bwd (dHidden, dW), row-sharded by group",
+            "global_batch": self.B,
+            "seq_len": self.T,
+            "hidden": self.H,
+            "vocab": V,
+            "group_size": self.G,
+            "parallelism": f"dp{world} (row shards of whole groups; scalar NCCL all-reduce)",
+            "l2": f"inputs larger than L2 (hidden {self.B * self.T * self.H * 2 / 1e9:.1f} GB per step), no flush",
+        }
+
+    def e2e(self):
+        """The same step through the public API with inputs in pinned host memory: every step copies
+        the rank's hidden rows, token ids, log-probs, masks and rewards to the device and reads the
+        loss and metrics back."""
+        host_hidden = self.hidden.detach().cpu().pin_memory()
+        hb = host_batch(self.local)
+        h2d = host_hidden.numel() * 2 + batch_bytes(hb)
+        d2h = 4 + 4 * 12
+
+        def one():
+            hid = host_hidden.to(self.device, non_blocking=True).requires_grad_(True)
+            b = to_device_batch(hb, self.device)
+            self.weight.grad = None
+            return self._step(b, hid, b.token_ids.reshape(-1))
+
+        return one, h2d, d2h
+
+    def cpu_sample(self, rows, steps):
+        """Reference arithmetic on the host CPU: fp32 LM-head log-probs + GRPO loss + autograd."""
+        import oracle
+        from invokerl_b200.synthetic import lmhead_inputs
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        li = lmhead_inputs(rows, self.H, V, seed=3)
+        hh = li.hidden.float().requires_grad_(True)
+        ww = li.weight.float().requires_grad_(True)
+        g = torch.Generator().manual_seed(5)
+        old = -torch.empty(rows).exponential_(1.0, generator=g)
+        ref = old + 0.1 * torch.randn(rows, generator=g)
+        mask = torch.rand(rows, generator=g) < 0.6
+        rewards = torch.bernoulli(torch.full((self.G,), 0.5), generator=g)
+        adv = oracle.group_advantages(rewards, torch.ones(self.G, 1, dtype=torch.bool), self.G).reshape(-1)
+        adv = adv.repeat_interleave((rows + self.G - 1) // self.G)[:rows]
+
+        def one():
+            hh.grad = None
+            ww.grad = None
+            logits = hh @ ww.t()
+            lp = torch.gather(logits, 1, li.targets[:, None]).squeeze(1) - torch.logsumexp(logits, dim=1)
+            ratio = torch.exp(lp - old)
+            pl = -torch.minimum(ratio * adv, torch.clamp(ratio, 0.8, 1.2) * adv)
+            d = ref - lp
+            loss = ((pl + 0.04 * (torch.exp(d) - d - 1)) * mask).sum() / mask.sum().clamp(min=1)
+            loss.backward()
+
+        one()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        dt = (time.perf_counter() - t0) / steps
+        return rows / dt, dt, f"{rows} rows x H={self.H} x V={V} per step (fp32 torch on the host CPU)"
+
+
+class LogitsLogProb:
+    """Unfused logits -> log-prob forward + backward (config 2): bf16 [16384, 151936] ~ N(0, 2),
+    uniform targets, upstream N(0,1) times a 50% mask."""
+
+    def __init__(self, key, args):
+        self.N = args.rows or 16384
+
+    def setup(self, rank, world, device):
+        gen = torch.Generator(device=device).manual_seed(0)
+        self.logits = (2.0 * torch.randn(self.N, V, device=device, generator=gen)).to(torch.bfloat16)
+        self.t = torch.randint(0, V, (self.N,), device=device, generator=gen)
+        self.up = torch.randn(self.N, device=device, generator=gen) * (
+            torch.rand(self.N, device=device, generator=gen) < 0.5).float()
+        self.n_act = int((self.up != 0).sum())
+        self.x = self.logits.requires_grad_(True)
+        self.device = device
+
+    def timed_functions(self):
+        return []  # the step is the two kernels; the whole step is timed
+
+    def step(self):
+        from invokerl_b200 import ops
+
+        self.x.grad = None
+        lp = ops.logits_logprob(self.x, self.t)
+        lp.backward(self.up)
+        return 0.0, {}
+
+    def tokens_per_step(self):
+        return self.N
+
+    def roofline(self, kernel_ms_per_step, peaks, peak_src):
+        nbytes = 2.0 * self.N * V + 2.0 * self.N * V + 2.0 * self.n_act * V
+        achieved = nbytes / (kernel_ms_per_step / 1e3) / 1e9
+        return {"kernel": "logits log-prob fwd + bwd (one CTA per row, 16-byte streaming loads)", "bound": "hbm",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                "peak_source": f"{peak_src} HBM copy",
+                "algorithmic": "fwd reads 2NV bytes; bwd writes 2NV and reads 2*N_active*V (rows with a zero "
+                               "upstream are written as zeros without reading)", "traffic": None}
+
+    def config(self, world):
+        return {"workload": "unfused logits->log-prob fwd+bwd: logits bf16 [16384, 151936] N(0,2), 50% masked upstream",
+                "rows": self.N, "vocab": V, "l2": "5 GB of logits per step, larger than L2, no flush"}
+
+    def e2e(self):
+        host_logits = self.logits.detach().cpu().pin_memory()
+        host_t, host_up = self.t.cpu().pin_memory(), self.up.cpu().pin_memory()
+        h2d = host_logits.numel() * 2 + host_t.numel() * 8 + host_up.numel() * 4
+        d2h = 4
+
+        def one():
+            from invokerl_b200 import ops
+
+            x = host_logits.to(self.device, non_blocking=True).requires_grad_(True)
+            lp = ops.logits_logprob(x, host_t.to(self.device, non_blocking=True))
+            lp.backward(host_up.to(self.device, non_blocking=True))
+            return float(lp.detach().sum()), {}
+
+        return one, h2d, d2h
+
+    def cpu_sample(self, rows, steps):
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator().manual_seed(1)
+        x = (2.0 * torch.randn(rows, V, generator=g)).float().requires_grad_(True)
+        t = torch.randint(0, V, (rows,), generator=g)
+        up = torch.randn(rows, generator=g)
+
+        def one():
+            x.grad = None
+            lp = -torch.nn.functional.cross_entropy(x, t, reduction="none")
+            lp.backward(up)
+
+        one()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        dt = (time.perf_counter() - t0) / steps
+        return rows / dt, dt, f"{rows} rows x V={V} per step (fp32 -F.cross_entropy + autograd on the host CPU)"
+
+
+class GRPOHooks:
+    """GRPO compute_advantages + compute_loss + backward on a synthetic RolloutBatch (config 1 and its
+    HBM-sized variant)."""
+
+    PRESETS = {"grpo": (4, 4, 512, (64, 256), (32, 256)), "grpo-hbm": (128, 8, 8192, (64, 256), (512, 4096))}
+
+    def __init__(self, key, args):
+        self.key = key
+        self.P, self.G, self.T, self.pl, self.cl = self.PRESETS[key]
+
+    def setup(self, rank, world, device):
+        from invokerl_b200.algorithms import GRPO
+        from invokerl_b200.distributed import shard_batch
+        from invokerl_b200.synthetic import rollout_batch
+
+        b = rollout_batch(self.P, self.G, self.T, prompt_len=self.pl, completion_len=self.cl, seed=0)
+        self.local = shard_batch(b, rank, world)
+        self.new = self.local.extras["new_log_probs"].contiguous()
+        self.dev_batch = to_device_batch(self.local, device)
+        self.lp = self.new.to(device).requires_grad_(True)
+        self.algo = GRPO(clip_eps=0.2, beta=0.04, row_sharded=world > 1)
+        self.device = device
+
+    def timed_functions(self):
+        return ["_clip_loss_launch"]
+
+    def _step(self, batch, lp):
+        adv = self.algo.compute_advantages(batch)
+        loss, metrics = self.algo.compute_loss(lp, batch, adv)
+        loss.backward()
+        return float(loss.detach()), metrics
+
+    def step(self):
+        self.lp.grad = None
+        return self._step(self.dev_batch, self.lp)
+
+    def tokens_per_step(self):
+        return self.P * self.G * self.T
+
+    def roofline(self, kernel_ms_per_step, peaks, peak_src):
+        nbytes = 21.0 * self.lp.numel()
+        achieved = nbytes / (kernel_ms_per_step / 1e3) / 1e9
+        return {"kernel": "fused ratio+clip+KL+masked-sum loss with d loss/d lp (one pass)", "bound": "hbm",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                "peak_source": f"{peak_src} HBM copy",
+                "algorithmic": "21 B/token: reads new, old, ref, adv (fp32) + mask (1 B), writes dlp (fp32)",
+                "traffic": None}
+
+    def config(self, world):
+        B = self.P * self.G
+        return {"workload": f"GRPO compute_advantages+compute_loss+backward, fp32 RolloutBatch B={B} "
+                            f"({self.P} prompts x group {self.G}), T={self.T}",
+                "global_batch": B, "seq_len": self.T, "group_size": self.G,
+                "l2": ("inputs smaller than L2 (launch-bound); timed back to back" if self.key == "grpo"
+                       else "inputs larger than L2 (176 MB per step), no flush")}
+
+    def e2e(self):
+        hb = host_batch(self.local)
+        host_lp = self.new.pin_memory()
+        h2d = batch_bytes(hb) + host_lp.numel() * 4
+        d2h = 4 + 4 * 12
+
+        def one():
+            b = to_device_batch(hb, self.device)
+            lp = host_lp.to(self.device, non_blocking=True).requires_grad_(True)
+            return self._step(b, lp)
+
+        return one, h2d, d2h
+
+    def cpu_sample(self, rows, steps):
+        import oracle
+        from invokerl_b200.synthetic import rollout_batch
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        b = rollout_batch(self.P, self.G, self.T, prompt_len=self.pl, completion_len=self.cl, seed=0)
+
+        def one():
+            adv = oracle.group_advantages(b.rewards, b.response_mask, self.G)
+            oracle.clip_ratio_loss(b.extras["new_log_probs"], b.old_log_probs, b.ref_log_probs, adv,
+                                   b.response_mask, b.rewards)
+
+        one()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        dt = (time.perf_counter() - t0) / steps
+        n = self.P * self.G * self.T
+        return n / dt, dt, f"the whole batch ({n} tokens) per step (fp32 torch on the host CPU)"
+
+
+WORKLOADS = {"lmhead-8b": LMHeadGRPO, "lmhead-0.6b": LMHeadGRPO, "logits": LogitsLogProb, "grpo": GRPOHooks,
+             "grpo-hbm": GRPOHooks}
+CPU_ROWS = {"lmhead-8b": 32, "lmhead-0.6b": 96, "logits": 1024, "grpo": 0, "grpo-hbm": 0}
 
 
 def run_native(args, rank, world, device) -> dict | None:
     from invokerl_b200 import _native, ops
-    from invokerl_b200.algorithms import GRPO
 
-    local, dev_batch, hidden, weight, ids = make_workload(rank, world, device)
-    weight.requires_grad_(True)
-    Bl = local.token_ids.shape[0]
-    algo = GRPO(clip_eps=0.2, beta=0.04, row_sharded=world > 1)
-    timer = K1Timer()
-    ops.lmhead_forward_raw = timer.wrap(ops.lmhead_forward_raw)
-    ops.lmhead_backward_raw = timer.wrap(ops.lmhead_backward_raw)
-
-    def step():
-        hidden.grad = None
-        weight.grad = None
-        return grpo_step(algo, dev_batch, hidden, weight, ids, Bl)
+    wl = WORKLOADS[args.workload](args.workload, args)
+    wl.setup(rank, world, device)
+    timer = EventTimer()
+    for name in wl.timed_functions():
+        setattr(ops, name, timer.wrap(getattr(ops, name)))
 
     for _ in range(args.warmup):
-        step()
+        wl.step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -210,8 +521,9 @@ def run_native(args, rank, world, device) -> dict | None:
     if world > 1:
         dist.barrier()
     start.record()
+    loss = 0.0
     for _ in range(args.steps):
-        loss, metrics = step()
+        loss, _ = wl.step()
     end.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -220,27 +532,38 @@ def run_native(args, rank, world, device) -> dict | None:
     launches = _native.lib().ikrl_launch_count() - launches0
     clocks = sampler.stop()
     ms = start.elapsed_time(end)
-    k1_ms = timer.total_ms()
-    t = torch.tensor([ms, k1_ms], dtype=torch.float64, device=device)
+    kms = timer.total_ms() if timer.pairs else ms
+    t = torch.tensor([ms, kms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, k1_ms = float(t[0]), float(t[1])
+    ms, kms = float(t[0]), float(t[1])
 
-    # ---- end to end through the public API with host (pinned) buffers ----
-    e2e = run_e2e(args, local, algo, hidden, weight, device, world)
+    e2e = None
+    if not args.no_e2e:
+        one, h2d, d2h = wl.e2e()
+        one()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        n = max(1, min(args.steps, 3))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            one()
+        e.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([s.elapsed_time(e)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": wl.tokens_per_step() * n / (float(te[0]) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n}
 
     if rank != 0:
         return None
     peaks, peak_src = load_peaks()
-    tokens_per_step = B_GLOBAL * T
-    value = tokens_per_step * args.steps / (ms / 1e3)
-    flops_step_rank = 6.0 * (Bl * T) * H_8B * V  # algorithmic 6NHV of this rank's rows
-    k1_s_per_step = k1_ms / 1e3 / args.steps
-    achieved = flops_step_rank / k1_s_per_step / 1e12
-    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     res = {
         "metric": METRIC,
-        "value": value,
+        "value": wl.tokens_per_step() * args.steps / (ms / 1e3),
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
@@ -249,134 +572,34 @@ def run_native(args, rank, world, device) -> dict | None:
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded; random-init LM-head weights)",
-        "config": {
-            "workload": "Qwen3-8B LM head: hidden bf16 [128*4096, 4096], W bf16 [151936, 4096] untied, "
-                        "GRPO G=8 k3 KL, fwd+bwd (dHidden, dW), row-sharded by prompt group",
-            "global_batch": B_GLOBAL,
-            "seq_len": T,
-            "hidden": H_8B,
-            "vocab": V,
-            "group_size": G,
-            "parallelism": f"dp{world} (row shards of whole groups; scalar NCCL all-reduce)",
-            "l2": "inputs larger than L2 (hidden 4.3 GB/step), no flush needed",
-        },
-        "roofline": {
-            "kernel": "fused LM-head log-prob fwd+bwd (tcgen05 GEMMs with LSE / dlogits epilogues)",
-            "bound": "tensor",
-            "achieved": achieved,
-            "peak": peak,
-            "unit": "TFLOP/s",
-            "frac": achieved / peak,
-            "peak_source": f"{peak_src} bf16 sustained (kernel timed inside a multi-second step)",
-            "algorithmic": "6*N*H*V per step (fwd 2NHV, dH 2NHV, dW 2NHV; the backward's 2NHV "
-                           "recompute of the logits is not counted)",
-            "traffic": None,
-        },
+        "dtype": "f32" if args.workload.startswith("grpo") else "bf16",
+        "data": "synthetic (seeded; random-init weights)",
+        "config": wl.config(world),
+        "roofline": wl.roofline(kms / args.steps, peaks, peak_src),
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clocks,
-        "loss": float(loss.detach()),
+        "loss": loss,
     }
+    if world == 1 and not args.no_cpu_baseline:
+        rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", CPU_ROWS[args.workload]))
+        tok_s, dt, sample = wl.cpu_sample(rows, 3)
+        res["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": sample + f"; 3 steps of {dt:.2f} s"}
     return res
 
 
-def run_e2e(args, local, algo, hidden, weight, device, world) -> dict:
-    """Same step through the public API with inputs in pinned host memory: every step copies the
-    rank's hidden rows, token ids, old/ref log-probs, masks and rewards to the device and reads the
-    loss and metrics back (compute_loss returns them as Python floats)."""
-    from invokerl_b200.algorithms import RolloutBatch
-
-    Bl = local.token_ids.shape[0]
-    host_hidden = hidden.detach().cpu().pin_memory()
-    host = {k: v.pin_memory() for k, v in vars(local).items() if isinstance(v, torch.Tensor)}
-    h2d = host_hidden.numel() * 2 + sum(host[k].numel() * host[k].element_size()
-                                        for k in ("token_ids", "response_mask", "old_log_probs",
-                                                  "ref_log_probs", "rewards"))
-    d2h = 4 + 4 * 7  # loss + metrics floats
-
-    def step():
-        hid = host_hidden.to(device, non_blocking=True).requires_grad_(True)
-        tb = {k: host[k].to(device, non_blocking=True) for k in host}
-        b = RolloutBatch(token_ids=tb["token_ids"], prompt_mask=tb["prompt_mask"], response_mask=tb["response_mask"],
-                         attention_mask=tb["attention_mask"], rewards=tb["rewards"], token_rewards=None,
-                         old_log_probs=tb["old_log_probs"], ref_log_probs=tb["ref_log_probs"],
-                         group_ids=tb.get("group_ids"), group_size=G)
-        weight.grad = None
-        loss, metrics = grpo_step(algo, b, hid, weight, b.token_ids.reshape(-1), Bl)
-        return float(loss.detach()), metrics
-
-    n = max(1, min(args.steps, 3))
-    for _ in range(1):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(n):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = torch.tensor([s.elapsed_time(e)], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms[0])
-    return {"value": B_GLOBAL * T * n / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": n}
-
-
-# ---- CPU baseline (oracle restatement of the reference, torch on the host cores) ------------------
-
-
-def cpu_sample(rows: int, steps: int = 1, H: int = H_8B) -> tuple[float, int, float]:
-    """Time `steps` CPU steps of the reference algorithm on `rows` rows of the workload: fp32
-    LM-head log-probs + GRPO loss + autograd (dHidden, dW).  Returns (tokens/s, threads, s/step)."""
-    import oracle
-    from invokerl_b200.synthetic import lmhead_inputs
-
-    torch.set_num_threads(os.cpu_count() or 1)
-    li = lmhead_inputs(rows, H, V, seed=3)
-    h = li.hidden.float()
-    w = li.weight.float()
-    g = torch.Generator().manual_seed(5)
-    old = -torch.empty(rows).exponential_(1.0, generator=g)
-    ref = old + 0.1 * torch.randn(rows, generator=g)
-    mask = torch.rand(rows, generator=g) < 0.6
-    rewards = torch.bernoulli(torch.full((G,), 0.5), generator=g)
-    adv = oracle.group_advantages(rewards, torch.ones(G, 1, dtype=torch.bool), G).reshape(-1)
-    adv = adv.repeat_interleave((rows + G - 1) // G)[:rows]
-
-    hh = h.requires_grad_(True)
-    ww = w.requires_grad_(True)
-
-    def one():
-        hh.grad = None
-        ww.grad = None
-        logits = hh @ ww.t()
-        lp = torch.gather(logits, 1, li.targets[:, None]).squeeze(1) - torch.logsumexp(logits, dim=1)
-        ratio = torch.exp(lp - old)
-        pl = -torch.minimum(ratio * adv, torch.clamp(ratio, 0.8, 1.2) * adv)
-        d = ref - lp
-        loss = ((pl + 0.04 * (torch.exp(d) - d - 1)) * mask).sum() / mask.sum().clamp(min=1)
-        loss.backward()
-
-    one()  # warm-up
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        one()
-    dt = (time.perf_counter() - t0) / steps
-    return rows / dt, torch.get_num_threads(), dt
-
-
 def run_reference(args, rank, world) -> dict | None:
+    """The reference's CPU arithmetic on the host cores (rank 0 only), same metric and config."""
     if rank != 0:
         return None
-    rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", "16"))
-    for _ in range(args.warmup):
-        cpu_sample(rows, 1)
-    tok_s, cores, dt = cpu_sample(rows, max(1, args.steps))
+    wl = WORKLOADS[args.workload](args.workload, args)
+    rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", max(1, CPU_ROWS[args.workload] // 2)))
+    for _ in range(max(0, args.warmup - 1)):
+        wl.cpu_sample(rows, 1)
+    tok_s, dt, sample = wl.cpu_sample(rows, max(1, args.steps))
+    cfg = dict(wl.config(world)) if not isinstance(wl, GRPOHooks) else dict(wl.config(world))
+    cfg["sample"] = sample
     return {
         "metric": METRIC,
         "value": tok_s,
@@ -391,11 +614,9 @@ def run_reference(args, rank, world) -> dict | None:
         "dtype": "f32",
         "data": "synthetic (seeded)",
         "impl": "reference",
-        "config": {"workload": "Qwen3-8B LM head + GRPO fwd+bwd, bounded row sample on the host CPU",
-                   "rows_per_step": rows, "hidden": H_8B, "vocab": V},
-        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{rows} rows x H={H_8B} x V={V} per step (fp32 torch on CPU, "
-                                   "the reference's own arithmetic restated in oracle/)"},
+        "config": cfg,
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
         "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -406,7 +627,11 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="lmhead-8b")
+    ap.add_argument("--batch", type=int, default=0, help="override the global batch B of the lmhead workloads")
+    ap.add_argument("--rows", type=int, default=0, help="override the rows of the logits workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -423,12 +648,6 @@ def main() -> int:
     try:
         res = run_native(args, rank, world, device)
         if rank == 0 and res is not None:
-            if world == 1 and not args.no_cpu_baseline:
-                rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", "32"))
-                tok_s, cores, dt = cpu_sample(rows, 3)
-                res["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": cores, "kind": "port",
-                                       "sample": f"{rows} rows of the workload per step, 3 steps "
-                                                 f"({dt:.1f} s/step; fp32 torch on the host CPU)"}
             print(json.dumps(res), flush=True)
     finally:
         if world > 1:

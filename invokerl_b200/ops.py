@@ -350,10 +350,14 @@ def logits_logprob_raw(logits: torch.Tensor, ids: torch.Tensor, with_target: boo
 # K1: fused LM-head log-prob (policy.py:124-191)
 # ---------------------------------------------------------------------------------------------
 
-DEFAULT_DS_CHUNK_BYTES = 8 << 30  # bf16 dlogits workspace of one backward chunk
+# bf16 dlogits workspace of one backward chunk; INVOKERL_B200_DS_CHUNK_BYTES overrides it.
+DEFAULT_DS_CHUNK_BYTES = int(os.environ.get("INVOKERL_B200_DS_CHUNK_BYTES", str(8 << 30)))
 
 
-def default_chunk_rows(N: int, V: int, budget_bytes: int = DEFAULT_DS_CHUNK_BYTES) -> int:
+def default_chunk_rows(N: int, V: int, budget_bytes: int | None = None) -> int:
+    """Rows per backward chunk so that one chunk of bf16 dlogits fits `budget_bytes`."""
+    if budget_bytes is None:
+        budget_bytes = DEFAULT_DS_CHUNK_BYTES
     lds = (V + 63) // 64 * 64
     rows = max(128, (budget_bytes // (2 * lds)) // 128 * 128)
     return min(N, rows) if N > rows else N
