@@ -178,6 +178,8 @@ class LMHeadGRPO:
     def __init__(self, key, args):
         p = dict(self.PRESETS[key])
         if args.batch:
+            if args.batch % self.G:
+                raise SystemExit(f"--batch must be a multiple of the group size {self.G}")
             p["B"] = args.batch
         self.key, self.p = key, p
         self.H, self.B, self.T = p["H"], p["B"], p["T"]
@@ -426,7 +428,53 @@ class GRPOHooks:
         self.device = device
 
     def timed_functions(self):
-        return ["_clip_loss_launch"]
+        return []
+
+    def kernel_ms(self, reps: int = 20) -> dict:
+        """Device time of the fused loss kernel and of the advantage kernel, each launched `reps`
+        times back to back between two CUDA events (the step itself is bound by host launches)."""
+        from invokerl_b200 import _native as N
+        from invokerl_b200 import ops
+
+        b = self.dev_batch
+        adv = self.algo.compute_advantages(b)
+        params = self.algo._params()
+        m = N.as_mask(b.response_mask)
+        ntok = ops.mask_count(m)
+        lp = self.lp.detach()
+        Bn, T = lp.shape
+        dlp = torch.empty_like(lp)
+        sums = torch.empty(N.LOSS_NSUMS, dtype=torch.float64, device=lp.device)
+        nbytes = int(N.lib().ikrl_clip_loss_workspace_bytes(Bn * T))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=lp.device)
+        st = N.stream_of(lp.device)
+
+        def loss_once():
+            N.call("ikrl_clip_loss_fwd", N.ptr(lp), N.i32(N.IKRL_DTYPE_F32), N.ptr(b.old_log_probs),
+                   N.ptr(b.ref_log_probs), N.ptr(adv), N.ptr(m), N.ptr(b.rewards), N.i32(Bn), N.i32(T),
+                   N.i32(self.G), N.ptr(ntok), None, None, None, params, N.ptr(dlp), None, N.ptr(sums),
+                   N.ptr(ws), N.sz(nbytes), st)
+
+        out = torch.empty_like(adv)
+        r = b.rewards.contiguous().float()
+
+        def adv_once():
+            N.call("ikrl_group_advantages", N.ptr(r), N.ptr(m), None, N.i32(Bn), N.i32(T), N.i32(self.G), N.i32(0),
+                   N.f32(0.0), N.ptr(out), None, st)
+
+        res = {}
+        for name, fn in (("loss", loss_once), ("advantages", adv_once)):
+            for _ in range(3):
+                fn()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            s.record()
+            for _ in range(reps):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            res[name] = s.elapsed_time(e) / reps
+        return res
 
     def _step(self, batch, lp):
         adv = self.algo.compute_advantages(batch)
@@ -442,12 +490,18 @@ class GRPOHooks:
         return self.P * self.G * self.T
 
     def roofline(self, kernel_ms_per_step, peaks, peak_src):
-        nbytes = 21.0 * self.lp.numel()
-        achieved = nbytes / (kernel_ms_per_step / 1e3) / 1e9
+        km = self.kernel_ms()
+        n = self.lp.numel()
+        achieved = 21.0 * n / (km["loss"] / 1e3) / 1e9
+        adv_gbs = 5.0 * n / (km["advantages"] / 1e3) / 1e9
         return {"kernel": "fused ratio+clip+KL+masked-sum loss with d loss/d lp (one pass)", "bound": "hbm",
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "peak_source": f"{peak_src} HBM copy",
                 "algorithmic": "21 B/token: reads new, old, ref, adv (fp32) + mask (1 B), writes dlp (fp32)",
+                "kernel_ms": km["loss"], "timing": "20 back-to-back launches between CUDA events",
+                "advantages_kernel": {"ms": km["advantages"], "achieved_gbs": adv_gbs,
+                                      "frac": adv_gbs / peaks["hbm_gbs"],
+                                      "algorithmic": "5 B/token: reads mask (1 B), writes adv (fp32)"},
                 "traffic": None}
 
     def config(self, world):

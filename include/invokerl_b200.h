@@ -232,6 +232,11 @@ IKRL_API int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* wei
                                              const int64_t* ids, int64_t N, int32_t H, int32_t V,
                                              float* logp, float* lse, void* stream);
 
+/* Selects the K1 GEMM kernel for later calls in this process: CTA pairs (tcgen05 cta_group::2,
+ * clusters of two; the default) or single CTAs (enable = 0).  Returns the previous setting.  The
+ * environment variable INVOKERL_B200_CTA_PAIRS=0 sets the initial choice. */
+IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
+
 /* Device status word of the last K1 call that used workspace `ws` (synchronises `stream`):
  * IKRL_OK, or IKRL_ERR_DEVICE with *status_out = the recorded code (a bounded wait expired). */
 IKRL_API int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream);

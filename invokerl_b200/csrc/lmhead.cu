@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#include <atomic>
 #include <mutex>
 
 namespace ikrl {
@@ -78,6 +79,135 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, i
 
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Epilogue role (warps 2-5): drain accumulator tiles from TMEM, one row per thread, and apply the
+// epilogue EPI.  acc_full[a] are this CTA's barriers; acc_empty[a] are the addresses the warps
+// arrive on when a tile is consumed (this CTA's, or the pair leader's when cluster_arrive).
+template <int EPI>
+__device__ __forceinline__ void epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
+                                              int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
+                                              const uint32_t (&acc_empty)[2], bool cluster_arrive,
+                                              volatile int* abort_v) {
+  const int ntiles = t_end - t_begin;
+  const int q = warp & 3;  // TMEM lane quadrant this warp may access
+  const int r = q * 32 + lane;
+  const int grow = m0 + r;
+  const bool row_ok = grow < p.M;
+  int64_t tgt = -1;
+  float lse2 = 0.f, gval = 0.f;
+  if constexpr (EPI == EPI_LSE || EPI == EPI_DLOGITS) {
+    if (row_ok) tgt = p.ids[grow];
+  }
+  if constexpr (EPI == EPI_DLOGITS) {
+    if (row_ok) {
+      lse2 = p.lse[grow] * kLog2e;
+      gval = p.g[grow];
+      if (tgt == -100) gval = 0.f;  // ignore_index rows have zero gradient
+    }
+  }
+  float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
+  for (int j = 0; j < ntiles; ++j) {
+    const int acc = j & 1;
+    const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+    if (!mbar_wait(acc_full[acc], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) break;
+    tc_fence_after();
+    const int n0 = (t_begin + j) * BN;
+    const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      const int col0 = n0 + c;
+      if (col0 >= p.N) break;  // warp-uniform
+      float v[32];
+      tmem_ld32(tbase + (uint32_t)c, v);
+      tmem_wait_ld();
+      const int nvalid = min(32, p.N - col0);
+      if constexpr (EPI == EPI_LSE) {
+        float cm = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nvalid) cm = fmaxf(cm, v[i]);
+        cm *= kLog2e;
+        if (cm > run_m) {
+          run_s *= fast_exp2(run_m - cm);
+          run_m = cm;
+        }
+        float cs = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
+        run_s += cs;
+        // Target gather without a dynamically indexed register array (which would go to local
+        // memory): exactly one term is v[rel] * 1, every other term adds zero.
+        const int64_t rel = tgt - col0;
+        if (rel >= 0 && rel < nvalid) {
+          const int rr = (int)rel;
+          float acc_t = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
+          tval = acc_t;
+        }
+      } else if constexpr (EPI == EPI_DLOGITS) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = fast_exp2(fmaf(v[i], kLog2e, -lse2));
+          const float p1 = fast_exp2(fmaf(v[i + 1], kLog2e, -lse2));
+          const float d0 = gval * (((int64_t)(col0 + i) == tgt ? 1.f : 0.f) - p0);
+          const float d1 = gval * (((int64_t)(col0 + i + 1) == tgt ? 1.f : 0.f) - p1);
+          w[i >> 1] = pack_bf16x2(d0, d1);
+        }
+        if (row_ok) {
+          uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        }
+      } else if constexpr (EPI == EPI_STORE_BF16) {
+        if (row_ok) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) w[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
+          uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        }
+      } else {  // EPI_F32
+        if (row_ok) {
+          float* dst = p.out_f32 + (int64_t)grow * p.ld_f32 + col0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (4 * k >= nvalid) break;
+            float4 x = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            if (p.f32_mode != F32_STORE) {
+              const float4 o = *reinterpret_cast<const float4*>(dst + 4 * k);
+              x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+            }
+            if (p.f32_mode == F32_ADD_TO_BF16) {
+              uint16_t* d16 = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0 + 4 * k;
+              *reinterpret_cast<uint2*>(d16) = make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
+            } else {
+              *reinterpret_cast<float4*>(dst + 4 * k) = x;
+            }
+          }
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (cluster_arrive) mbar_arrive_cluster(acc_empty[acc]);
+      else mbar_arrive(acc_empty[acc]);
+    }
+  }
+  if constexpr (EPI == EPI_LSE) {
+    if (row_ok && !*abort_v) {
+      p.part_m[(int64_t)split * p.M + grow] = run_m;
+      p.part_s[(int64_t)split * p.M + grow] = run_s;
+      if (tgt >= (int64_t)t_begin * BN && tgt < (int64_t)t_end * BN && tgt < p.N) p.part_t[grow] = tval;
+    }
+  }
 }
 
 template <int EPI, bool A_MN, bool B_MN>
@@ -216,121 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int r = q * 32 + lane;
-    const int grow = m0 + r;
-    const bool row_ok = grow < p.M;
-    int64_t tgt = -1;
-    float lse2 = 0.f, gval = 0.f;
-    if constexpr (EPI == EPI_LSE || EPI == EPI_DLOGITS) {
-      if (row_ok) tgt = p.ids[grow];
-    }
-    if constexpr (EPI == EPI_DLOGITS) {
-      if (row_ok) {
-        lse2 = p.lse[grow] * kLog2e;
-        gval = p.g[grow];
-        if (tgt == -100) gval = 0.f;  // ignore_index rows have zero gradient
-      }
-    }
-    float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
-    for (int j = 0; j < ntiles; ++j) {
-      const int acc = j & 1;
-      const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
-      if (!mbar_wait(smem_u32(&acc_full[acc]), acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) break;
-      tc_fence_after();
-      const int n0 = (t_begin + j) * BN;
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        const int col0 = n0 + c;
-        if (col0 >= p.N) break;  // warp-uniform
-        float v[32];
-        tmem_ld32(tbase + (uint32_t)c, v);
-        tmem_wait_ld();
-        const int nvalid = min(32, p.N - col0);
-        if constexpr (EPI == EPI_LSE) {
-          float cm = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < nvalid) cm = fmaxf(cm, v[i]);
-          cm *= kLog2e;
-          if (cm > run_m) {
-            run_s *= fast_exp2(run_m - cm);
-            run_m = cm;
-          }
-          float cs = 0.f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
-          run_s += cs;
-          // Target gather without a dynamically indexed register array (which would go to local
-          // memory): exactly one term is v[rel] * 1, every other term adds zero.
-          const int64_t rel = tgt - col0;
-          if (rel >= 0 && rel < nvalid) {
-            const int rr = (int)rel;
-            float acc_t = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
-            tval = acc_t;
-          }
-        } else if constexpr (EPI == EPI_DLOGITS) {
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float p0 = fast_exp2(fmaf(v[i], kLog2e, -lse2));
-            const float p1 = fast_exp2(fmaf(v[i + 1], kLog2e, -lse2));
-            const float d0 = gval * (((int64_t)(col0 + i) == tgt ? 1.f : 0.f) - p0);
-            const float d1 = gval * (((int64_t)(col0 + i + 1) == tgt ? 1.f : 0.f) - p1);
-            w[i >> 1] = pack_bf16x2(d0, d1);
-          }
-          if (row_ok) {
-            uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-          }
-        } else if constexpr (EPI == EPI_STORE_BF16) {
-          if (row_ok) {
-            uint32_t w[16];
-#pragma unroll
-            for (int i = 0; i < 32; i += 2) w[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
-            uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-          }
-        } else {  // EPI_F32
-          if (row_ok) {
-            float* dst = p.out_f32 + (int64_t)grow * p.ld_f32 + col0;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              if (4 * k >= nvalid) break;
-              float4 x = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-              if (p.f32_mode != F32_STORE) {
-                const float4 o = *reinterpret_cast<const float4*>(dst + 4 * k);
-                x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-              }
-              if (p.f32_mode == F32_ADD_TO_BF16) {
-                uint16_t* d16 = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0 + 4 * k;
-                *reinterpret_cast<uint2*>(d16) = make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
-              } else {
-                *reinterpret_cast<float4*>(dst + 4 * k) = x;
-              }
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
-    }
-    if constexpr (EPI == EPI_LSE) {
-      if (row_ok && !*abort_v) {
-        p.part_m[(int64_t)split * p.M + grow] = run_m;
-        p.part_s[(int64_t)split * p.M + grow] = run_s;
-        if (tgt >= (int64_t)t_begin * BN && tgt < (int64_t)t_end * BN && tgt < p.N) p.part_t[grow] = tval;
-      }
-    }
+    const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
+    const uint32_t ae[2] = {smem_u32(&acc_empty[0]), smem_u32(&acc_empty[1])};
+    epilogue_role<EPI>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, false, abort_v);
   }
 
   tc_fence_before();
@@ -339,6 +357,173 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+// CTA-pair variant (cluster of two, tcgen05 cta_group::2): the pair computes a 256 x 256 tile
+// per MMA; each CTA stages its own 128 A rows and 128 of the 256 B rows, so shared-memory and
+// L2 traffic per MMA flop is 2/3 of the single-CTA kernel and the ring is 6 stages deep.  The
+// even CTA issues the MMAs and commits to both CTAs' barriers; both CTAs run the epilogue on
+// their own 128 accumulator rows and release the accumulator on the even CTA's barrier.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairTileB = (BN / 2) * BK * 2;  // 16 KB: this CTA's half of the B tile
+constexpr uint32_t kPairStageBytes = kTileA + kPairTileB;
+constexpr uint32_t kPairSmemBytes = kPairStages * kPairStageBytes + 1024;
+
+template <int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    lmhead_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kPairStages], empty_bar[kPairStages], acc_full[2], acc_empty[2], drain_bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+
+  // 1-D grid of pairs, split-major: pair q covers split q % splits and row blocks
+  // 2 * (q / splits) + {0, 1}, so pairs running together share B tiles of the same split.
+  const int pair_id = blockIdx.x >> 1;
+  const int split = pair_id % p.splits;
+  const int m_blk = 2 * (pair_id / p.splits) + (int)rank;
+  const int m0 = m_blk * BM;
+  const int t_begin = split * p.tiles_per_split;
+  const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+  const int ntiles = t_end - t_begin;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
+    }
+    mbar_init(smem_u32(&drain_bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    fence_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_holder;
+  volatile int* abort_v = &abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0 && ntiles > 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = t_begin; t < t_end && ok; ++t) {
+        const int nb = t * BN + (int)rank * (BN / 2);  // this CTA's half of the N tile
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = smem_u32(&full_bar[stage]);
+          const uint32_t fb_leader = mapa_shared(fb_local, 0);
+          if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * kPairStageBytes);
+          const uint32_t a_dst = smem_base + stage * kPairStageBytes;
+          const uint32_t b_dst = a_dst + kTileA;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, fb_leader, k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c) tma_load_2d_pair(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, fb_leader, k0, nb);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 128; ++c) tma_load_2d_pair(b_dst + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0);
+          }
+          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (ok) {
+        for (int s = 0; s < kPairStages; ++s) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) break;
+          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+        }
+      } else {
+        // Abort: the copies' completion is counted on the even CTA's barrier, which this CTA
+        // cannot wait on; give copies already issued 1 ms to land before shared memory goes away.
+        for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA only) ----------------
+    if (rank == 0 && lane == 0 && ntiles > 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(2 * BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int acc = j & 1;
+        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_base + stage * kPairStageBytes;
+          const uint32_t b_addr = a_addr + kTileA;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
+                                     : smem_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, kMnAtomBytes, 1024)
+                                     : smem_desc(b_addr + k * 32, 16, 1024);
+            mma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&empty_bar[stage]);
+          mma_commit_pair(mapa_shared(eb, 0));
+          mma_commit_pair(mapa_shared(eb, 1));
+          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) {
+          const uint32_t fb = smem_u32(&acc_full[acc]);
+          mma_commit_pair(mapa_shared(fb, 0));
+          mma_commit_pair(mapa_shared(fb, 1));
+        }
+      }
+      if (!ok) {
+        mma_commit_pair(mapa_shared(smem_u32(&drain_bar), 0));
+        mbar_wait_drain(smem_u32(&drain_bar), 0, p.err);
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs, own 128 rows) ----------------
+    const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
+    const uint32_t ae[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0), mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    epilogue_role<EPI>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers or shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  (void)peer;
 }
 
 // Merge the per-split (max, sum) pairs of each row: lse = ln2 * (M + log2 sum_s s_s 2^(m_s - M)).
@@ -412,6 +597,63 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
   const dim3 grid = p.split_major ? dim3(p.splits, m_tiles) : dim3(m_tiles, p.splits);
   kern<<<grid, kThreads, kSmemBytes, s>>>(a, b, p);
   return check_launch("lmhead_gemm_kernel");
+}
+
+// Pair launch: a 1-D grid of splits x (row blocks rounded up to even) CTAs in clusters of 2.
+template <int EPI, bool A_MN, bool B_MN>
+int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int m_tiles, cudaStream_t s) {
+  auto kern = lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
+  IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes));
+  IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
+  const int64_t mt = (m_tiles + 1) & ~1;
+  const int64_t nblocks = mt * p.splits;
+  IKRL_REQUIRE(nblocks <= 0x7fffffffLL, IKRL_ERR_UNSUPPORTED, "too many CTAs (%lld)", (long long)nblocks);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)nblocks, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, p);
+  if (e != cudaSuccess) {
+    int nclusters = -1;
+    cudaError_t e2 = cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg);
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, kern);
+    (void)cudaGetLastError();
+    set_error("pair kernel launch failed: %s (grid %u x %u, max active clusters %d [%s], static smem %zu, "
+              "dynamic %u, max dyn %d, regs %d, max threads %d)",
+              cudaGetErrorString(e), cfg.gridDim.x, cfg.gridDim.y, nclusters, cudaGetErrorString(e2), fa.sharedSizeBytes,
+              kPairSmemBytes, fa.maxDynamicSharedSizeBytes, fa.numRegs, fa.maxThreadsPerBlock);
+    return IKRL_ERR_CUDA;
+  }
+  return check_launch("lmhead_gemm_pair_kernel");
+}
+
+// Kernel choice: CTA pairs by default; INVOKERL_B200_CTA_PAIRS=0 in the environment, or
+// ikrl_lmhead_set_cta_pairs(0), selects the single-CTA kernel.
+std::atomic<int> g_pairs{-1};
+bool use_pairs() {
+  int v = g_pairs.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = getenv("INVOKERL_B200_CTA_PAIRS");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+    g_pairs.store(v, std::memory_order_relaxed);
+  }
+  return v == 1;
+}
+
+template <int EPI, bool A_MN, bool B_MN>
+int launch_any(const CUtensorMap& a_single, const CUtensorMap& b_single, const CUtensorMap& a_pair,
+               const CUtensorMap& b_pair, const GemmParams& p, int m_tiles, cudaStream_t s) {
+  if (use_pairs()) return launch_gemm_pair<EPI, A_MN, B_MN>(a_pair, b_pair, p, m_tiles, s);
+  return launch_gemm<EPI, A_MN, B_MN>(a_single, b_single, p, m_tiles, s);
 }
 
 int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -511,9 +753,10 @@ int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_
   int* err = reinterpret_cast<int*>(w + L.err_off);
   IKRL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
 
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tb2;
   if ((rc = make_tmap(&ta, hidden, H, N, H, BM, "hidden"))) return rc;
   if ((rc = make_tmap(&tb, weight, H, V, H, BN, "weight"))) return rc;
+  if ((rc = make_tmap(&tb2, weight, H, V, H, BN / 2, "weight"))) return rc;
   GemmParams p{};
   p.M = (int)N; p.N = V; p.K = H;
   p.n_tiles = (int)cdiv64(V, BN);
@@ -526,7 +769,7 @@ int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_
   p.part_t = reinterpret_cast<float*>(w + L.pt_off);
   p.err = err;
   const int m_tiles = (int)cdiv64(N, BM);
-  if ((rc = launch_gemm<EPI_LSE, false, false>(ta, tb, p, m_tiles, s))) return rc;
+  if ((rc = launch_any<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, s))) return rc;
   lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V, L.splits,
                                                               logp, lse, err);
   return check_launch("lse_combine_kernel");
@@ -572,8 +815,9 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
   const int n_ht = (int)cdiv64(H, BN);
   const int64_t nchunks = cdiv64(N, L.chunk);
 
-  CUtensorMap t_w_k, t_w_mn;
+  CUtensorMap t_w_k, t_w_k2, t_w_mn;
   if ((rc = make_tmap(&t_w_k, weight, H, V, H, BN, "weight"))) return rc;
+  if ((rc = make_tmap(&t_w_k2, weight, H, V, H, BN / 2, "weight"))) return rc;
   if ((rc = make_tmap(&t_w_mn, weight, H, V, H, 64, "weight^T"))) return rc;
 
   for (int64_t ci = 0; ci < nchunks; ++ci) {
@@ -595,7 +839,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       p.ids = ids + c0; p.lse = lse + c0; p.g = dlogp + c0;
       p.out_bf16 = dS; p.ld_bf16 = L.lds;
       p.err = err;
-      if ((rc = launch_gemm<EPI_DLOGITS, false, false>(ta, t_w_k, p, m_tiles, s))) return rc;
+      if ((rc = launch_any<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, s))) return rc;
     }
     // 2) dH[chunk] = dS W
     if (dhidden) {
@@ -606,7 +850,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       p.n_tiles = n_ht; p.tiles_per_split = 1; p.splits = n_ht; p.split_major = 1;
       p.out_bf16 = reinterpret_cast<uint16_t*>(dhidden) + c0 * H; p.ld_bf16 = H;
       p.err = err;
-      if ((rc = launch_gemm<EPI_STORE_BF16, false, true>(ta, t_w_mn, p, m_tiles, s))) return rc;
+      if ((rc = launch_any<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, s))) return rc;
     }
     // 3) dW (+)= dS^T h[chunk]
     if (dweight) {
@@ -621,7 +865,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       const bool last = ci == nchunks - 1;
       if (dweight_dtype == IKRL_DTYPE_BF16 && !L.need_dw32) {
         p.out_bf16 = reinterpret_cast<uint16_t*>(dweight); p.ld_bf16 = H;
-        if ((rc = launch_gemm<EPI_STORE_BF16, true, true>(ta, tb, p, v_tiles, s))) return rc;
+        if ((rc = launch_any<EPI_STORE_BF16, true, true>(ta, tb, ta, tb, p, v_tiles, s))) return rc;
       } else {
         if (dweight_dtype == IKRL_DTYPE_F32) {
           p.out_f32 = reinterpret_cast<float*>(dweight);
@@ -632,11 +876,17 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
           p.f32_mode = last ? F32_ADD_TO_BF16 : (ci == 0 ? F32_STORE : F32_ADD);
         }
         p.ld_f32 = H;
-        if ((rc = launch_gemm<EPI_F32, true, true>(ta, tb, p, v_tiles, s))) return rc;
+        if ((rc = launch_any<EPI_F32, true, true>(ta, tb, ta, tb, p, v_tiles, s))) return rc;
       }
     }
   }
   return IKRL_OK;
+}
+
+int ikrl_lmhead_set_cta_pairs(int32_t enable) {
+  const int prev = use_pairs() ? 1 : 0;
+  g_pairs.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return prev;
 }
 
 int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream) {

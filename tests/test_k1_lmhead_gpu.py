@@ -19,6 +19,16 @@ def check_device_status(monkeypatch):
     monkeypatch.setattr(ops, "_CHECK_DEVICE_STATUS", True)
 
 
+@pytest.fixture(params=["cta_pairs", "single_cta"])
+def kernel_variant(request):
+    """Run a test on both K1 GEMM kernels: CTA pairs (cta_group::2) and single CTAs."""
+    from invokerl_b200 import _native as N
+
+    prev = N.lib().ikrl_lmhead_set_cta_pairs(1 if request.param == "cta_pairs" else 0)
+    yield request.param
+    N.lib().ikrl_lmhead_set_cta_pairs(prev)
+
+
 def rel_fro(a, b):
     return float((a.float() - b.float()).norm() / b.float().norm().clamp(min=1e-30))
 
@@ -32,7 +42,7 @@ def run_k1(h, w, t, g, chunk_rows=None, dw_dtype=torch.bfloat16):
     return lp.cpu(), lse.cpu(), dh.cpu(), dw.cpu()
 
 
-def test_golden_small():
+def test_golden_small(kernel_variant):
     g = load("lmhead_small")
     h = g["hidden"].reshape(-1, g["hidden"].shape[-1])
     t = g["targets"].reshape(-1)
@@ -42,7 +52,7 @@ def test_golden_small():
     assert rel_fro(dw, g["dw_fp32"]) <= 1e-2
 
 
-def test_golden_reference_chunked_branch():
+def test_golden_reference_chunked_branch(kernel_variant):
     """The reference's chunk loop (B*T*V*4 >= 2 GiB) on the full vocabulary; H=32 < one K tile."""
     g = load("lmhead_chunked_seed")
     B, T, H, V = g["shape"]
@@ -59,7 +69,7 @@ def test_golden_reference_chunked_branch():
     (160, 4096, 151936, 128),      # Qwen3-8B head shape, 2 chunks
     (40, 200, 777, None),          # H not a multiple of 64, V odd
 ])
-def test_against_oracle(N, H, V, chunk):
+def test_against_oracle(N, H, V, chunk, kernel_variant):
     li = lmhead_inputs(N, H, V, seed=N + H + V, w_std=0.05 if H > 512 else 0.3)
     gen = torch.Generator().manual_seed(1)
     g = torch.randn(N, generator=gen) * torch.bernoulli(torch.full((N,), 0.7), generator=gen)
@@ -74,7 +84,7 @@ def test_against_oracle(N, H, V, chunk):
         assert float(dh[z].abs().max()) == 0.0
 
 
-def test_fp32_dweight_accumulates():
+def test_fp32_dweight_accumulates(kernel_variant):
     N, H, V = 200, 128, 3000
     li = lmhead_inputs(N, H, V, seed=3, w_std=0.3)
     g = torch.randn(N, generator=torch.Generator().manual_seed(2))
@@ -107,7 +117,7 @@ def test_ignored_rows_and_autograd_function():
 
 
 @pytest.mark.parametrize("N,H", [(131072, 1024), (65536, 4096)])
-def test_full_size_properties(N, H):
+def test_full_size_properties(N, H, kernel_variant):
     """Config-3 size (and half of config 4's rows): log-probs of sampled rows against the oracle;
     dH of sampled rows; dW on sampled vocab rows from the kernel's own lse; sum_v dW[v] = 0."""
     V = 151936
