@@ -179,6 +179,19 @@ IKRL_API int ikrl_simpo_fwd(const void* lp, int32_t lp_dtype, const uint8_t* mas
 IKRL_API int ikrl_simpo_bwd(const float* row_coef, const uint8_t* mask, int32_t B, int32_t T,
                    const float* scale, void* dlp_out, int32_t dlp_dtype, void* stream);
 
+/* ---- K3: DPO (invokerl/algorithms/dpo.py:51-106) ----------------------------------------------- */
+
+/* Per-row masked sum of (lp - ref_lp), pairwise -logsigmoid(beta*(chosen - rejected)) with label
+ * smoothing, mean over pairs.  loss_out[0]; metrics_out[IKRL_SIMPO_NMETRICS]: loss, reward,
+ * chosen_reward, rejected_reward, reward_accuracy, margin, 0, num_pairs.  row_coef_out[B] =
+ * d loss / d lp[b,t] on masked tokens (upstream 1); the backward is ikrl_simpo_bwd. */
+IKRL_API size_t ikrl_dpo_workspace_bytes(int32_t B);
+IKRL_API int ikrl_dpo_fwd(const void* lp, int32_t lp_dtype, const float* ref_lp, const uint8_t* mask,
+                          const float* rewards, int32_t B, int32_t T, float beta,
+                          float label_smoothing, int32_t chosen_first, float* loss_out,
+                          float* metrics_out, float* row_coef_out, void* ws, size_t ws_bytes,
+                          void* stream);
+
 /* ---- K2: logits -> log-prob (unfused path) ------------------------------------------------ */
 
 /* Replaces -F.cross_entropy(logits, targets, reduction="none") of invokerl/policy.py:100-104

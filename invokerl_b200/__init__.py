@@ -8,6 +8,6 @@ Drop-in surface (same names and signatures as the reference):
 """
 
 from . import _native, ops  # noqa: F401
-from .algorithms import DAPO, GRPO, PPO, BaseAlgorithm, RolloutBatch, SimPO  # noqa: F401
+from .algorithms import DAPO, DPO, GRPO, PPO, BaseAlgorithm, RolloutBatch, SimPO  # noqa: F401
 
 __version__ = "0.1.0"

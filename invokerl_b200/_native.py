@@ -94,6 +94,11 @@ _SIGNATURES: dict[str, tuple] = {
          c_size_t, _P],
     ),
     "ikrl_simpo_bwd": (ctypes.c_int, [_P, _P, c_int32, c_int32, _P, _P, c_int32, _P]),
+    "ikrl_dpo_workspace_bytes": (c_size_t, [c_int32]),
+    "ikrl_dpo_fwd": (
+        ctypes.c_int,
+        [_P, c_int32, _P, _P, _P, c_int32, c_int32, c_float, c_float, c_int32, _P, _P, _P, _P, c_size_t, _P],
+    ),
     "ikrl_logits_logprob_fwd": (
         ctypes.c_int,
         [_P, c_int64, _P, c_int64, c_int32, _P, _P, _P, _P],

@@ -2,8 +2,9 @@
 
 from .base import BaseAlgorithm, RolloutBatch
 from .dapo import DAPO
+from .dpo import DPO
 from .grpo import GRPO
 from .ppo import PPO
 from .simpo import SimPO
 
-__all__ = ["BaseAlgorithm", "RolloutBatch", "GRPO", "PPO", "SimPO", "DAPO"]
+__all__ = ["BaseAlgorithm", "RolloutBatch", "GRPO", "DPO", "PPO", "SimPO", "DAPO"]

@@ -84,12 +84,15 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 // Epilogue role (warps 2-5): drain accumulator tiles from TMEM, one row per thread, and apply the
 // epilogue EPI.  acc_full[a] are this CTA's barriers; acc_empty[a] are the addresses the warps
 // arrive on when a tile is consumed (this CTA's, or the pair leader's when cluster_arrive).
+// tile_base: number of tiles this CTA consumed before this unit (accumulator ring position).
+// Returns false when a wait gave up (abort).
 template <int EPI>
-__device__ __forceinline__ void epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
+__device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
                                               int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
                                               const uint32_t (&acc_empty)[2], bool cluster_arrive,
-                                              volatile int* abort_v) {
+                                              volatile int* abort_v, int tile_base = 0) {
   const int ntiles = t_end - t_begin;
+  bool ok = true;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
   const int r = q * 32 + lane;
   const int grow = m0 + r;
@@ -108,9 +111,24 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, uint32_t tmem
   }
   float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
   for (int j = 0; j < ntiles; ++j) {
-    const int acc = j & 1;
-    const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
-    if (!mbar_wait(acc_full[acc], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) break;
+    const int acc = (tile_base + j) & 1;
+    const uint32_t acc_phase = (uint32_t)((tile_base + j) >> 1) & 1u;
+    if constexpr (EPI == EPI_F32) {
+      // Pull this row's slice of the fp32 accumulator into L2 while the MMAs run, so the
+      // read-modify-write below hits L2.
+      if (row_ok && p.f32_mode != F32_STORE) {
+        const int n0p = (t_begin + j) * BN;
+        const int ncols = min(BN, p.N - n0p);
+        if (ncols > 0)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
+                       "r"((uint32_t)ncols * 4u)
+                       : "memory");
+      }
+    }
+    if (!mbar_wait(acc_full[acc], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) {
+      ok = false;
+      break;
+    }
     tc_fence_after();
     const int n0 = (t_begin + j) * BN;
     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -208,6 +226,7 @@ __device__ __forceinline__ void epilogue_role(const GemmParams& p, uint32_t tmem
       if (tgt >= (int64_t)t_begin * BN && tgt < (int64_t)t_end * BN && tgt < p.N) p.part_t[grow] = tval;
     }
   }
+  return ok;
 }
 
 template <int EPI, bool A_MN, bool B_MN>
@@ -381,17 +400,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t rank = cluster_ctarank();
-  const uint32_t peer = rank ^ 1u;
 
-  // 1-D grid of pairs, split-major: pair q covers split q % splits and row blocks
-  // 2 * (q / splits) + {0, 1}, so pairs running together share B tiles of the same split.
+  // Persistent pairs.  A work unit is (split, row-block pair); unit u covers split u % splits and
+  // row blocks 2 * (u / splits) + {0, 1}.  Pair c processes units c, c + npairs, ...; the units
+  // in flight at any time are consecutive, so pairs that run together share the B tiles of a
+  // split and the A rows of a row-block pair through L2, and proceed in step.
   const int pair_id = blockIdx.x >> 1;
-  const int split = pair_id % p.splits;
-  const int m_blk = 2 * (pair_id / p.splits) + (int)rank;
-  const int m0 = m_blk * BM;
-  const int t_begin = split * p.tiles_per_split;
-  const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-  const int ntiles = t_end - t_begin;
+  const int npairs = gridDim.x >> 1;
+  const int m_pairs = (((p.M + BM - 1) / BM) + 1) >> 1;
+  const int nunits = m_pairs * p.splits;
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -424,36 +441,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
-    if (lane == 0 && ntiles > 0) {
+    if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = t_begin; t < t_end && ok; ++t) {
-        const int nb = t * BN + (int)rank * (BN / 2);  // this CTA's half of the N tile
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb_local = smem_u32(&full_bar[stage]);
-          const uint32_t fb_leader = mapa_shared(fb_local, 0);
-          if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * kPairStageBytes);
-          const uint32_t a_dst = smem_base + stage * kPairStageBytes;
-          const uint32_t b_dst = a_dst + kTileA;
-          const int k0 = kb * BK;
-          if constexpr (!A_MN) {
-            tma_load_2d_pair(a_dst, &tmA, fb_leader, k0, m0);
-          } else {
+      for (int u = pair_id; u < nunits && ok; u += npairs) {
+        const int split = u % p.splits;
+        const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
+        const int t_begin = split * p.tiles_per_split;
+        const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+        for (int t = t_begin; t < t_end && ok; ++t) {
+          const int nb = t * BN + (int)rank * (BN / 2);  // this CTA's half of the N tile
+          for (int kb = 0; kb < nk; ++kb) {
+            if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb_local = smem_u32(&full_bar[stage]);
+            const uint32_t fb_leader = mapa_shared(fb_local, 0);
+            if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * kPairStageBytes);
+            const uint32_t a_dst = smem_base + stage * kPairStageBytes;
+            const uint32_t b_dst = a_dst + kTileA;
+            const int k0 = kb * BK;
+            if constexpr (!A_MN) {
+              tma_load_2d_pair(a_dst, &tmA, fb_leader, k0, m0);
+            } else {
 #pragma unroll
-            for (int c = 0; c < BM / 64; ++c) tma_load_2d_pair(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0);
-          }
-          if constexpr (!B_MN) {
-            tma_load_2d_pair(b_dst, &tmB, fb_leader, k0, nb);
-          } else {
+              for (int c = 0; c < BM / 64; ++c)
+                tma_load_2d_pair(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0);
+            }
+            if constexpr (!B_MN) {
+              tma_load_2d_pair(b_dst, &tmB, fb_leader, k0, nb);
+            } else {
 #pragma unroll
-            for (int c = 0; c < BN / 128; ++c) tma_load_2d_pair(b_dst + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0);
+              for (int c = 0; c < BN / 128; ++c)
+                tma_load_2d_pair(b_dst + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0);
+            }
+            if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
           }
-          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
         }
       }
       if (ok) {
@@ -469,39 +494,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA only) ----------------
-    if (rank == 0 && lane == 0 && ntiles > 0) {
+    if (rank == 0 && lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(2 * BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int acc = j & 1;
-        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+      int j = 0;  // tiles issued so far (accumulator ring position)
+      for (int u = pair_id; u < nunits && ok; u += npairs) {
+        const int split = u % p.splits;
+        const int t_begin = split * p.tiles_per_split;
+        const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+        for (int t = t_begin; t < t_end && ok; ++t, ++j) {
+          const int acc = j & 1;
+          const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+          if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1u, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_base + stage * kPairStageBytes;
-          const uint32_t b_addr = a_addr + kTileA;
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+          for (int kb = 0; kb < nk; ++kb) {
+            if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_addr = smem_base + stage * kPairStageBytes;
+            const uint32_t b_addr = a_addr + kTileA;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
-                                     : smem_desc(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, kMnAtomBytes, 1024)
-                                     : smem_desc(b_addr + k * 32, 16, 1024);
-            mma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
+                                       : smem_desc(a_addr + k * 32, 16, 1024);
+              const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, kMnAtomBytes, 1024)
+                                       : smem_desc(b_addr + k * 32, 16, 1024);
+              mma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+            const uint32_t eb = smem_u32(&empty_bar[stage]);
+            mma_commit_pair(mapa_shared(eb, 0));
+            mma_commit_pair(mapa_shared(eb, 1));
+            if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
           }
-          const uint32_t eb = smem_u32(&empty_bar[stage]);
-          mma_commit_pair(mapa_shared(eb, 0));
-          mma_commit_pair(mapa_shared(eb, 1));
-          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
-        }
-        if (ok) {
-          const uint32_t fb = smem_u32(&acc_full[acc]);
-          mma_commit_pair(mapa_shared(fb, 0));
-          mma_commit_pair(mapa_shared(fb, 1));
+          if (ok) {
+            const uint32_t fb = smem_u32(&acc_full[acc]);
+            mma_commit_pair(mapa_shared(fb, 0));
+            mma_commit_pair(mapa_shared(fb, 1));
+          }
         }
       }
       if (!ok) {
@@ -513,7 +544,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (both CTAs, own 128 rows) ----------------
     const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
     const uint32_t ae[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0), mapa_shared(smem_u32(&acc_empty[1]), 0)};
-    epilogue_role<EPI>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v);
+    int jb = 0;
+    for (int u = pair_id; u < nunits; u += npairs) {
+      const int split = u % p.splits;
+      const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
+      const int t_begin = split * p.tiles_per_split;
+      const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+      if (!epilogue_role<EPI>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v, jb)) break;
+      jb += t_end - t_begin;
+    }
   }
 
   tc_fence_before();
@@ -523,7 +562,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
-  (void)peer;
 }
 
 // Merge the per-split (max, sum) pairs of each row: lse = ln2 * (M + log2 sum_s s_s 2^(m_s - M)).
@@ -599,17 +637,23 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
   return check_launch("lmhead_gemm_kernel");
 }
 
-// Pair launch: a 1-D grid of splits x (row blocks rounded up to even) CTAs in clusters of 2.
+// Pair launch: a persistent 1-D grid of one CTA pair (cluster of 2) per two SMs.
 template <int EPI, bool A_MN, bool B_MN>
 int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int m_tiles, cudaStream_t s) {
   auto kern = lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
   IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes));
   IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
-  const int64_t mt = (m_tiles + 1) & ~1;
-  const int64_t nblocks = mt * p.splits;
-  IKRL_REQUIRE(nblocks <= 0x7fffffffLL, IKRL_ERR_UNSUPPORTED, "too many CTAs (%lld)", (long long)nblocks);
+  const int64_t nunits = (int64_t)((m_tiles + 1) / 2) * p.splits;
+  IKRL_REQUIRE(nunits <= 0x3fffffffLL, IKRL_ERR_UNSUPPORTED, "too many work units (%lld)", (long long)nunits);
+  int dev = 0, nsm = kNumSMs;
+  IKRL_CUDA(cudaGetDevice(&dev));
+  IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  // One resident pair per two SMs; INVOKERL_B200_PERSISTENT=0 launches one pair per unit instead.
+  const char* pe = getenv("INVOKERL_B200_PERSISTENT");
+  const bool persistent = !(pe != nullptr && pe[0] == '0');
+  const int64_t npairs = std::max<int64_t>(1, persistent ? std::min<int64_t>(nunits, nsm / 2) : nunits);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)nblocks, 1, 1);
+  cfg.gridDim = dim3((unsigned)(2 * npairs), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kPairSmemBytes;
   cfg.stream = s;
@@ -661,7 +705,9 @@ int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Vocab splits for the row-sweeping GEMMs: enough that the row blocks resident at once keep their
 // A tiles in L2 (about 24 MB of hidden rows), and enough CTAs to fill the GPU.
 int choose_splits(int64_t m_tiles, int n_tiles, int H) {
-  const int64_t resident_rows_budget = (24ll << 20) / (2ll * H);   // rows whose A tiles fit ~24 MB
+  int64_t budget_mb = 24;
+  if (const char* e = getenv("INVOKERL_B200_L2_BUDGET_MB")) budget_mb = std::max<int64_t>(1, atoll(e));
+  const int64_t resident_rows_budget = (budget_mb << 20) / (2ll * H);   // rows whose A tiles fit the budget
   const int64_t blocks_resident = std::max<int64_t>(1, resident_rows_budget / BM);
   int64_t s = cdiv64(kNumSMs, std::min<int64_t>(blocks_resident, m_tiles));
   s = std::max<int64_t>(s, cdiv64(2 * kNumSMs, m_tiles));

@@ -56,19 +56,29 @@ __device__ inline void group_stats(const float* r, int G, double& mean, double& 
 __device__ __forceinline__ void broadcast_row(float a, const uint8_t* __restrict__ mrow, float* __restrict__ arow,
                                               int T) {
   int t0 = 0;
-  if (((reinterpret_cast<uintptr_t>(mrow) & 15) == 0) && ((reinterpret_cast<uintptr_t>(arow) & 15) == 0)) {
-    const int n16 = T >> 4;
-    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
-      const uint4 m = __ldg(reinterpret_cast<const uint4*>(mrow) + i);
-      const uint32_t w[4] = {m.x, m.y, m.z, m.w};
-      float4* o = reinterpret_cast<float4*>(arow) + 4 * i;
+  if (((reinterpret_cast<uintptr_t>(mrow) & 3) == 0) && ((reinterpret_cast<uintptr_t>(arow) & 15) == 0)) {
+    // 4 tokens per thread per step: a 4-byte mask word in, one 16-byte store out; consecutive
+    // threads touch consecutive words, so loads and stores coalesce fully.
+    const int n4 = T >> 2;
+    const uint32_t* m32 = reinterpret_cast<const uint32_t*>(mrow);
+    float4* o = reinterpret_cast<float4*>(arow);
+    int i = threadIdx.x;
+    for (; i + 3 * (int)blockDim.x < n4; i += 4 * blockDim.x) {
+      uint32_t w[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        o[k] = make_float4(a * ((w[k] & 0xffu) ? 1.f : 0.f), a * ((w[k] & 0xff00u) ? 1.f : 0.f),
-                           a * ((w[k] & 0xff0000u) ? 1.f : 0.f), a * ((w[k] & 0xff000000u) ? 1.f : 0.f));
-      }
+      for (int u = 0; u < 4; ++u) w[u] = __ldg(m32 + i + u * blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        o[i + u * blockDim.x] = make_float4(a * ((w[u] & 0xffu) ? 1.f : 0.f), a * ((w[u] & 0xff00u) ? 1.f : 0.f),
+                                            a * ((w[u] & 0xff0000u) ? 1.f : 0.f),
+                                            a * ((w[u] & 0xff000000u) ? 1.f : 0.f));
     }
-    t0 = n16 << 4;
+    for (; i < n4; i += blockDim.x) {
+      const uint32_t w = __ldg(m32 + i);
+      o[i] = make_float4(a * ((w & 0xffu) ? 1.f : 0.f), a * ((w & 0xff00u) ? 1.f : 0.f),
+                         a * ((w & 0xff0000u) ? 1.f : 0.f), a * ((w & 0xff000000u) ? 1.f : 0.f));
+    }
+    t0 = n4 << 2;
   }
   for (int t = t0 + threadIdx.x; t < T; t += blockDim.x) arow[t] = a * (mrow[t] ? 1.f : 0.f);
 }
@@ -398,16 +408,29 @@ __global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
   const float wmean = whiten_on ? a.whiten[0] : 0.f, wstd = whiten_on ? a.whiten[1] : 0.f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if constexpr (VEC) {
+    // Software-pipelined: the loads of the next quad are in flight while this quad is computed.
     const int64_t nq = a.n >> 2;
-    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += stride) {
-      float lp[4], old[4], ref[4] = {0.f, 0.f, 0.f, 0.f}, adv[4], vv[4] = {0.f, 0.f, 0.f, 0.f},
-            ov[4] = {0.f, 0.f, 0.f, 0.f}, d[4], dv[4] = {0.f, 0.f, 0.f, 0.f};
-      load_lp4<BF16>(a.new_lp, q, lp);
-      ld4(a.old_lp, q, old);
-      if (a.ref_lp) ld4(a.ref_lp, q, ref);
-      ld4(a.adv, q, adv);
-      const uint32_t mw = __ldg(reinterpret_cast<const uint32_t*>(a.mask) + q);
-      if (a.values) { ld4(a.values, q, vv); ld4(a.old_values, q, ov); }
+    int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float lp[4], old[4], ref[4] = {0.f, 0.f, 0.f, 0.f}, adv[4], vv[4] = {0.f, 0.f, 0.f, 0.f},
+          ov[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t mw = 0;
+    auto load_quad = [&](int64_t qq, float (&l)[4], float (&o)[4], float (&rf)[4], float (&ad)[4], uint32_t& m,
+                         float (&v)[4], float (&ovv)[4]) {
+      load_lp4<BF16>(a.new_lp, qq, l);
+      ld4(a.old_lp, qq, o);
+      if (a.ref_lp) ld4(a.ref_lp, qq, rf);
+      ld4(a.adv, qq, ad);
+      m = __ldg(reinterpret_cast<const uint32_t*>(a.mask) + qq);
+      if (a.values) { ld4(a.values, qq, v); ld4(a.old_values, qq, ovv); }
+    };
+    if (q < nq) load_quad(q, lp, old, ref, adv, mw, vv, ov);
+    for (; q < nq; q += stride) {
+      float lp2[4], old2[4], ref2[4] = {0.f, 0.f, 0.f, 0.f}, adv2[4], vv2[4] = {0.f, 0.f, 0.f, 0.f},
+            ov2[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t mw2 = 0;
+      const int64_t qn = q + stride;
+      if (qn < nq) load_quad(qn, lp2, old2, ref2, adv2, mw2, vv2, ov2);
+      float d[4], dv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint8_t mk = (uint8_t)((mw >> (8 * j)) & 0xffu);
@@ -416,6 +439,11 @@ __global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
       }
       if (a.dlp) store_lp4<BF16>(a.dlp, q, d);
       if (a.dvalues) reinterpret_cast<float4*>(a.dvalues)[q] = make_float4(dv[0], dv[1], dv[2], dv[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lp[j] = lp2[j]; old[j] = old2[j]; ref[j] = ref2[j]; adv[j] = adv2[j]; vv[j] = vv2[j]; ov[j] = ov2[j];
+      }
+      mw = mw2;
     }
   } else {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
@@ -607,6 +635,71 @@ __global__ void simpo_bwd_kernel(const float* __restrict__ row_coef, const uint8
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
     const int64_t i = (int64_t)b * T + t;
     store_lp<BF16>(dlp, i, c * (mask[i] ? 1.f : 0.f));
+  }
+}
+
+// ---- DPO -------------------------------------------------------------------------------------
+// log_ratio[b] = sum_t (lp - ref) * m  (dpo.py:66-70), then the pairwise sigmoid loss.
+
+template <bool BF16>
+__global__ void dpo_rows_kernel(const void* lp, const float* __restrict__ ref, const uint8_t* __restrict__ mask,
+                                int T, float* __restrict__ log_ratio) {
+  __shared__ float scratch[2 * 32];
+  const int b = blockIdx.x;
+  float v[2] = {0.f, 0.f};
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const int64_t i = (int64_t)b * T + t;
+    const float m = mask[i] ? 1.f : 0.f;
+    v[0] += load_lp<BF16>(lp, i) * m;
+    v[1] += ref[i] * m;
+  }
+  block_sum<float, 2>(v, scratch);
+  if (threadIdx.x == 0) log_ratio[b] = v[0] - v[1];
+}
+
+__global__ void dpo_pairs_kernel(const float* __restrict__ lr, const float* __restrict__ rewards, int B, float beta,
+                                 float smoothing, int chosen_first, float* __restrict__ loss_out,
+                                 float* __restrict__ metrics, float* __restrict__ row_coef) {
+  __shared__ double scratch[5 * 32];
+  const int P = B / 2;
+  double v[5] = {0, 0, 0, 0, 0};
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const int ic = chosen_first ? 2 * i : 2 * i + 1;
+    const int ir = chosen_first ? 2 * i + 1 : 2 * i;
+    const float c = lr[ic], r = lr[ir];
+    const float margin = beta * (c - r);
+    float li, dm;
+    const float sg = 1.f / (1.f + expf(-margin));
+    if (smoothing > 0.f) {
+      li = (1.f - smoothing) * -log_sigmoid(margin) + smoothing * -log_sigmoid(-margin);
+      dm = (1.f - smoothing) * (sg - 1.f) + smoothing * sg;
+    } else {
+      li = -log_sigmoid(margin);
+      dm = sg - 1.f;
+    }
+    dm /= (float)P;
+    v[0] += li;
+    v[1] += beta * c;
+    v[2] += beta * r;
+    v[3] += (beta * c > beta * r) ? 1.0 : 0.0;
+    v[4] += margin;
+    row_coef[ic] = beta * dm;
+    row_coef[ir] = -beta * dm;
+  }
+  block_sum<double, 5>(v, scratch);
+  if (threadIdx.x == 0) {
+    double rs = 0.0;
+    for (int b = 0; b < B; ++b) rs += rewards ? rewards[b] : 0.0;
+    const float loss = (float)(v[0] / P);
+    loss_out[0] = loss;
+    metrics[0] = loss;
+    metrics[1] = rewards ? (float)(rs / B) : 0.f;
+    metrics[2] = (float)(v[1] / P);
+    metrics[3] = (float)(v[2] / P);
+    metrics[4] = (float)(v[3] / P);
+    metrics[5] = (float)(v[4] / P);
+    metrics[6] = 0.f;
+    metrics[7] = (float)P;
   }
 }
 
@@ -820,6 +913,34 @@ int ikrl_simpo_bwd(const float* row_coef, const uint8_t* mask, int32_t B, int32_
   if (dlp_dtype == IKRL_DTYPE_BF16) simpo_bwd_kernel<true><<<B, 256, 0, as_stream(stream)>>>(row_coef, mask, T, scale, dlp_out);
   else simpo_bwd_kernel<false><<<B, 256, 0, as_stream(stream)>>>(row_coef, mask, T, scale, dlp_out);
   return check_launch("simpo_bwd_kernel");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+size_t ikrl_dpo_workspace_bytes(int32_t B) { return (size_t)(B > 0 ? B : 0) * sizeof(float) + 256; }
+
+int ikrl_dpo_fwd(const void* lp, int32_t lp_dtype, const float* ref_lp, const uint8_t* mask, const float* rewards,
+                 int32_t B, int32_t T, float beta, float label_smoothing, int32_t chosen_first, float* loss_out,
+                 float* metrics_out, float* row_coef_out, void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(B > 0 && T >= 0 && B % 2 == 0, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_dpo_fwd: B=%d must be positive and even (chosen/rejected pairs)", B);
+  IKRL_REQUIRE(lp && ref_lp && mask && loss_out && metrics_out && row_coef_out, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_dpo_fwd: null pointer");
+  IKRL_REQUIRE(lp_dtype == IKRL_DTYPE_F32 || lp_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
+               "ikrl_dpo_fwd: lp_dtype %d unsupported", lp_dtype);
+  IKRL_REQUIRE(ws && ws_bytes >= ikrl_dpo_workspace_bytes(B), IKRL_ERR_WORKSPACE, "ikrl_dpo_fwd: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  float* lr = reinterpret_cast<float*>(ws);
+  if (lp_dtype == IKRL_DTYPE_BF16) dpo_rows_kernel<true><<<B, 256, 0, s>>>(lp, ref_lp, mask, T, lr);
+  else dpo_rows_kernel<false><<<B, 256, 0, s>>>(lp, ref_lp, mask, T, lr);
+  int rc = check_launch("dpo_rows_kernel");
+  if (rc) return rc;
+  dpo_pairs_kernel<<<1, 256, 0, s>>>(lr, rewards, B, beta, label_smoothing, chosen_first, loss_out, metrics_out,
+                                     row_coef_out);
+  return check_launch("dpo_pairs_kernel");
 }
 
 }  // extern "C"

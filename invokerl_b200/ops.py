@@ -459,3 +459,50 @@ def lmhead_logprob(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Te
     if h.shape[0] != ids.shape[0]:
         raise ValueError(f"{h.shape[0]} hidden rows but {ids.shape[0]} targets")
     return LMHeadLogProb.apply(h, w, ids, chunk_rows).reshape(shape)
+
+
+# ---------------------------------------------------------------------------------------------
+# DPO (dpo.py:51-106)
+# ---------------------------------------------------------------------------------------------
+
+
+class DPOLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, lp, ref, mask_u8, rewards, beta, smoothing, chosen_first):
+        dev = lp.device
+        B, T = lp.shape
+        loss = torch.empty((), dtype=torch.float32, device=dev)
+        metrics = torch.empty(N.SIMPO_NMETRICS, dtype=torch.float32, device=dev)
+        coef = torch.empty(B, dtype=torch.float32, device=dev)
+        ws = N.workspace(dev, int(N.lib().ikrl_dpo_workspace_bytes(B)))
+        call("ikrl_dpo_fwd", ptr(lp), i32(N.dtype_code(lp)), ptr(ref), ptr(mask_u8), ptr(rewards), i32(B), i32(T),
+             f32(beta), f32(smoothing), i32(1 if chosen_first else 0), ptr(loss), ptr(metrics), ptr(coef), ptr(ws),
+             sz(ws.numel()), N.stream_of(dev))
+        ctx.save_for_backward(coef, mask_u8)
+        ctx.lp_dtype = lp.dtype
+        ctx.shape = (B, T)
+        ctx.mark_non_differentiable(metrics)
+        return loss, metrics
+
+    @staticmethod
+    def backward(ctx, g_loss, g_metrics):
+        if g_loss is None:
+            return (None,) * 7
+        coef, m = ctx.saved_tensors
+        B, T = ctx.shape
+        dlp = torch.empty(B, T, dtype=ctx.lp_dtype, device=coef.device)
+        s = g_loss.detach().reshape(1).float().contiguous()
+        call("ikrl_simpo_bwd", ptr(coef), ptr(m), i32(B), i32(T), ptr(s), ptr(dlp), i32(N.dtype_code(dlp)),
+             N.stream_of(coef.device))
+        return dlp, None, None, None, None, None, None
+
+
+def dpo_loss(lp, ref_lp, response_mask, rewards, beta, label_smoothing, chosen_first):
+    N.require_cuda(lp, ref_lp, response_mask, rewards)
+    B, T = lp.shape
+    if B % 2:
+        raise ValueError(f"DPO needs an even batch of chosen/rejected pairs, got B={B}")
+    x = lp if lp.dtype in (torch.float32, torch.bfloat16) else lp.float()
+    return DPOLoss.apply(x.contiguous(), ref_lp.contiguous().float(), N.as_mask(response_mask),
+                         None if rewards is None else rewards.contiguous().float(), float(beta),
+                         float(label_smoothing), bool(chosen_first))

@@ -20,6 +20,7 @@ __all__ = [
     "gae_advantages",
     "clip_ratio_loss",
     "simpo_loss",
+    "dpo_loss",
 ]
 
 
@@ -221,5 +222,30 @@ def simpo_loss(new_lp, mask, rewards, beta=2.0, gamma=0.5, chosen_first=True):
         margin=float(margin.detach().mean()),
         avg_log_prob=float(avg.detach().mean()),
     )
+    loss.backward()
+    return loss.detach(), metrics, lp.grad.to(new_lp.dtype)
+
+
+def dpo_loss(new_lp, ref_lp, mask, rewards, beta=0.1, label_smoothing=0.0, chosen_first=True):
+    """dpo.py:62-106: pairwise sigmoid loss on the policy-minus-reference sequence log-ratios."""
+    lp = new_lp.detach().float().requires_grad_(True)
+    m = mask.float()
+    lr = (lp * m).sum(dim=1) - (ref_lp.float() * m).sum(dim=1)
+    c, r = (lr[0::2], lr[1::2]) if chosen_first else (lr[1::2], lr[0::2])
+    margin = beta * (c - r)
+    ls = torch.nn.functional.logsigmoid
+    if label_smoothing > 0:
+        loss = ((1 - label_smoothing) * -ls(margin) + label_smoothing * -ls(-margin)).mean()
+    else:
+        loss = -ls(margin).mean()
+    with torch.no_grad():
+        metrics = dict(
+            loss=float(loss),
+            reward=float(rewards.float().mean()),
+            chosen_reward=float((beta * c).mean()),
+            rejected_reward=float((beta * r).mean()),
+            reward_accuracy=float((beta * c > beta * r).float().mean()),
+            margin=float(margin.mean()),
+        )
     loss.backward()
     return loss.detach(), metrics, lp.grad.to(new_lp.dtype)

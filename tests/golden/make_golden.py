@@ -27,7 +27,7 @@ REF = os.environ.get("INVOKERL_REFERENCE", "/root/reference")
 if REF not in sys.path:
     sys.path.insert(0, REF)
 
-from invokerl.algorithms import DAPO, GRPO, PPO, SimPO  # noqa: E402
+from invokerl.algorithms import DAPO, DPO, GRPO, PPO, SimPO  # noqa: E402
 from invokerl.algorithms import RolloutBatch as RefBatch  # noqa: E402
 from invokerl.policy import PolicyModel  # noqa: E402
 
@@ -144,6 +144,14 @@ def algo_cases() -> None:
     save("simpo_default", kind="simpo", kwargs=dict(), batch=batch_dict(b), new_lp=nl, out=run_algo(SimPO(), b, nl))
     save("simpo_rejected_first", kind="simpo", kwargs=dict(beta=1.5, gamma=0.2, chosen_first=False),
          batch=batch_dict(b), new_lp=nl, out=run_algo(SimPO(beta=1.5, gamma=0.2, chosen_first=False), b, nl))
+
+    # DPO pairs (dpo.py): default, label smoothing, rejected-first ordering.
+    b = rollout_batch(4, 2, 64, prompt_len=(8, 20), completion_len=(8, 40), seed=17)
+    nl = b.extras["new_log_probs"]
+    save("dpo_default", kind="dpo", kwargs=dict(), batch=batch_dict(b), new_lp=nl, out=run_algo(DPO(), b, nl))
+    save("dpo_smoothing", kind="dpo", kwargs=dict(beta=0.3, label_smoothing=0.1, chosen_first=False),
+         batch=batch_dict(b), new_lp=nl,
+         out=run_algo(DPO(beta=0.3, label_smoothing=0.1, chosen_first=False), b, nl))
 
 
 def logprob_cases() -> None:

@@ -21,6 +21,8 @@ ALGO_CASES = [
     "ppo_token_rewards",
     "simpo_default",
     "simpo_rejected_first",
+    "dpo_default",
+    "dpo_smoothing",
 ]
 
 

@@ -7,12 +7,12 @@ import torch
 import oracle
 from helpers import ALGO_CASES, assert_metrics_close, load, make_batch
 from invokerl_b200 import ops
-from invokerl_b200.algorithms import DAPO, GRPO, PPO, SimPO
+from invokerl_b200.algorithms import DAPO, DPO, GRPO, PPO, SimPO
 from invokerl_b200.synthetic import rollout_batch
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-CLS = {"grpo": GRPO, "dapo": DAPO, "ppo": PPO, "simpo": SimPO}
+CLS = {"grpo": GRPO, "dapo": DAPO, "ppo": PPO, "simpo": SimPO, "dpo": DPO}
 
 
 def run(algo, batch, new_lp, scale=1.0):

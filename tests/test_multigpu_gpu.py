@@ -1,0 +1,90 @@
+"""Row sharding on 2 GPUs over NCCL: each rank runs the fused LM head and GRPO loss on its whole
+prompt groups; the all-reduced metrics and the summed loss shares equal the single-process
+oracle on the full batch, and each rank's gradients are the full-batch gradients of its rows.
+Skipped when fewer than two GPUs are visible."""
+
+import datetime
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+P, G, T, H, V = 4, 4, 64, 128, 3000
+
+
+def make_inputs():
+    from invokerl_b200.synthetic import lmhead_inputs, rollout_batch
+
+    b = rollout_batch(P, G, T, prompt_len=(4, 20), completion_len=(8, 40), vocab=V, seed=3)
+    li = lmhead_inputs(P * G * T, H, V, seed=4, w_std=0.3)
+    return b, li
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from invokerl_b200 import ops
+    from invokerl_b200.algorithms import GRPO
+    from invokerl_b200.distributed import group_shard_bounds, shard_batch
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        b, li = make_inputs()
+        s, e = group_shard_bounds(P * G, G, rank, world)
+        local = shard_batch(b, rank, world)
+        local.extras = {}
+        db = type(local)(**{k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in vars(local).items()
+                            if k != "extras"}, extras={})
+        h = li.hidden.reshape(P * G, T, H)[s:e].reshape(-1, H).to(dev).requires_grad_(True)
+        w = li.weight.to(dev).requires_grad_(True)
+        lp = ops.lmhead_logprob(h, w, db.token_ids.reshape(-1)).view(e - s, T)
+        algo = GRPO(row_sharded=True)
+        adv = algo.compute_advantages(db)
+        loss, metrics = algo.compute_loss(lp, db, adv)
+        loss.backward()
+        tot = loss.detach().clone()
+        dist.all_reduce(tot)
+        dw = w.grad.float().clone()
+        dist.all_reduce(dw)
+        grads = [torch.empty_like(h.grad) for _ in range(world)]
+        dist.all_gather(grads, h.grad.contiguous())
+        if rank == 0:
+            q.put((float(tot), metrics, torch.cat(grads).cpu(), dw.cpu(), lp.detach().cpu()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_row_sharding_matches_full_batch():
+    import oracle
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 500
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    tot, metrics, dh, dw, _ = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    b, li = make_inputs()
+    lp_full = oracle.lmhead_logprob(li.hidden, li.weight, b.token_ids.reshape(-1)).view(P * G, T)
+    adv = oracle.group_advantages(b.rewards, b.response_mask, G)
+    loss, met, g = oracle.clip_ratio_loss(lp_full, b.old_log_probs, b.ref_log_probs, adv, b.response_mask, b.rewards)
+    assert abs(tot - float(loss)) <= 1e-4 * abs(float(loss)) + 1e-6
+    for k in ("loss", "reward", "kl", "policy_loss", "clip_frac", "approx_kl", "advantages_mean"):
+        assert abs(metrics[k] - met[k]) <= 1e-4 * abs(met[k]) + 1e-6, k
+    _, dh_o, dw_o = oracle.lmhead_logprob_grads(li.hidden, li.weight, b.token_ids.reshape(-1), g.reshape(-1))
+    rel = lambda a, c: float((a.float() - c.float()).norm() / c.float().norm())  # noqa: E731
+    assert rel(dh, dh_o) <= 1e-2
+    assert rel(dw, dw_o) <= 1e-2

@@ -48,6 +48,10 @@ def test_oracle_matches_reference_algorithms(name):
         loss, metrics, grad = oracle.simpo_loss(g["new_lp"], b["response_mask"], b["rewards"],
                                                 beta=kw.get("beta", 2.0), gamma=kw.get("gamma", 0.5),
                                                 chosen_first=kw.get("chosen_first", True))
+    elif kind == "dpo":
+        loss, metrics, grad = oracle.dpo_loss(g["new_lp"], b["ref_log_probs"], b["response_mask"], b["rewards"],
+                                              beta=kw.get("beta", 0.1), label_smoothing=kw.get("label_smoothing", 0.0),
+                                              chosen_first=kw.get("chosen_first", True))
     else:
         okw = ORACLE_KW[kind](kw)
         ex = b["extras"]
