@@ -15,7 +15,8 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().with_name("libinvokerl_b200.so")
+# The in-tree build; INVOKERL_B200_LIBRARY may point at another build of the same ABI.
+LIB_PATH = Path(os.environ.get("INVOKERL_B200_LIBRARY") or Path(__file__).resolve().with_name("libinvokerl_b200.so"))
 
 IKRL_DTYPE_F32 = 0
 IKRL_DTYPE_BF16 = 1

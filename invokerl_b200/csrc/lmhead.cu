@@ -383,7 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // L2 traffic per MMA flop is 2/3 of the single-CTA kernel and the ring is 6 stages deep.  The
 // even CTA issues the MMAs and commits to both CTAs' barriers; both CTAs run the epilogue on
 // their own 128 accumulator rows and release the accumulator on the even CTA's barrier.
-constexpr int kPairStages = 6;
+#ifndef IKRL_PAIR_STAGES
+#define IKRL_PAIR_STAGES 6
+#endif
+constexpr int kPairStages = IKRL_PAIR_STAGES;
 constexpr uint32_t kPairTileB = (BN / 2) * BK * 2;  // 16 KB: this CTA's half of the B tile
 constexpr uint32_t kPairStageBytes = kTileA + kPairTileB;
 constexpr uint32_t kPairSmemBytes = kPairStages * kPairStageBytes + 1024;

@@ -15,7 +15,15 @@ namespace ikrl {
 namespace {
 
 constexpr int kLossThreads = 256;
-constexpr int kLossMaxBlocks = kNumSMs * 8;
+#ifndef IKRL_LOSS_UNROLL
+#define IKRL_LOSS_UNROLL 2
+#endif
+#ifndef IKRL_LOSS_BLOCKS_PER_SM
+#define IKRL_LOSS_BLOCKS_PER_SM 3
+#endif
+constexpr int kLossUnroll = IKRL_LOSS_UNROLL;
+constexpr int kLossBlocksPerSM = IKRL_LOSS_BLOCKS_PER_SM;
+constexpr int kLossMaxBlocks = kNumSMs * kLossBlocksPerSM;
 constexpr int kTokenSums = 9;  // sums[0..8] are per-token; [9..15] batch-level
 
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -313,7 +321,8 @@ __device__ __forceinline__ float token_step(const LossArgs& a, float lp, float o
   const float m = mk ? 1.f : 0.f;
   if (whiten_on) adv = ((adv - wmean) / (wstd + 1e-8f)) * m;
   const float lr = lp - old;
-  const float rho = expf(lr);
+  // ratio = e^lr as 2^(lr * log2 e) on the MUFU unit: a few ulp, well inside the 1e-4 parity bound.
+  const float rho = fast_exp2(lr * kLog2e);
   const float s1 = rho * adv;
   const float rc = torch_clamp(rho, p.ratio_lo, p.ratio_hi);
   const float s2 = rc * adv;
@@ -396,7 +405,7 @@ __device__ __forceinline__ void ld4(const float* p, int64_t q, float (&x)[4]) {
 
 // VEC: four tokens per thread per step with 16-byte loads (n % 4 == 0, aligned pointers).
 template <int FAMILY, bool BF16, bool VEC>
-__global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
+__global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kernel(LossArgs a) {
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
   __shared__ bool am_last;
   float acc[kTokenSums];
@@ -408,42 +417,41 @@ __global__ void __launch_bounds__(kLossThreads) clip_loss_kernel(LossArgs a) {
   const float wmean = whiten_on ? a.whiten[0] : 0.f, wstd = whiten_on ? a.whiten[1] : 0.f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if constexpr (VEC) {
-    // Software-pipelined: the loads of the next quad are in flight while this quad is computed.
+    // kLossUnroll quads per thread per step, all loads issued before any compute.
     const int64_t nq = a.n >> 2;
-    int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    float lp[4], old[4], ref[4] = {0.f, 0.f, 0.f, 0.f}, adv[4], vv[4] = {0.f, 0.f, 0.f, 0.f},
-          ov[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t mw = 0;
-    auto load_quad = [&](int64_t qq, float (&l)[4], float (&o)[4], float (&rf)[4], float (&ad)[4], uint32_t& m,
-                         float (&v)[4], float (&ovv)[4]) {
-      load_lp4<BF16>(a.new_lp, qq, l);
-      ld4(a.old_lp, qq, o);
-      if (a.ref_lp) ld4(a.ref_lp, qq, rf);
-      ld4(a.adv, qq, ad);
-      m = __ldg(reinterpret_cast<const uint32_t*>(a.mask) + qq);
-      if (a.values) { ld4(a.values, qq, v); ld4(a.old_values, qq, ovv); }
-    };
-    if (q < nq) load_quad(q, lp, old, ref, adv, mw, vv, ov);
-    for (; q < nq; q += stride) {
-      float lp2[4], old2[4], ref2[4] = {0.f, 0.f, 0.f, 0.f}, adv2[4], vv2[4] = {0.f, 0.f, 0.f, 0.f},
-            ov2[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t mw2 = 0;
-      const int64_t qn = q + stride;
-      if (qn < nq) load_quad(qn, lp2, old2, ref2, adv2, mw2, vv2, ov2);
-      float d[4], dv[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t q0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q0 < nq; q0 += stride * kLossUnroll) {
+      float lp[kLossUnroll][4], old[kLossUnroll][4], ref[kLossUnroll][4], adv[kLossUnroll][4];
+      float vv[kLossUnroll][4], ov[kLossUnroll][4];
+      uint32_t mw[kLossUnroll];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint8_t mk = (uint8_t)((mw >> (8 * j)) & 0xffu);
-        d[j] = token_step<FAMILY>(a, lp[j], old[j], ref[j], adv[j], mk, inv_n, wmean, wstd, whiten_on, vv[j],
-                                  ov[j], dv[j], acc);
-      }
-      if (a.dlp) store_lp4<BF16>(a.dlp, q, d);
-      if (a.dvalues) reinterpret_cast<float4*>(a.dvalues)[q] = make_float4(dv[0], dv[1], dv[2], dv[3]);
+      for (int u = 0; u < kLossUnroll; ++u) {
+        const int64_t q = q0 + u * stride;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        lp[j] = lp2[j]; old[j] = old2[j]; ref[j] = ref2[j]; adv[j] = adv2[j]; vv[j] = vv2[j]; ov[j] = ov2[j];
+        for (int j = 0; j < 4; ++j) { ref[u][j] = 0.f; vv[u][j] = 0.f; ov[u][j] = 0.f; }
+        mw[u] = 0;
+        if (q < nq) {
+          load_lp4<BF16>(a.new_lp, q, lp[u]);
+          ld4(a.old_lp, q, old[u]);
+          if (a.ref_lp) ld4(a.ref_lp, q, ref[u]);
+          ld4(a.adv, q, adv[u]);
+          mw[u] = __ldg(reinterpret_cast<const uint32_t*>(a.mask) + q);
+          if (a.values) { ld4(a.values, q, vv[u]); ld4(a.old_values, q, ov[u]); }
+        }
       }
-      mw = mw2;
+#pragma unroll
+      for (int u = 0; u < kLossUnroll; ++u) {
+        const int64_t q = q0 + u * stride;
+        if (q >= nq) break;
+        float d[4], dv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint8_t mk = (uint8_t)((mw[u] >> (8 * j)) & 0xffu);
+          d[j] = token_step<FAMILY>(a, lp[u][j], old[u][j], ref[u][j], adv[u][j], mk, inv_n, wmean, wstd,
+                                    whiten_on, vv[u][j], ov[u][j], dv[j], acc);
+        }
+        if (a.dlp) store_lp4<BF16>(a.dlp, q, d);
+        if (a.dvalues) reinterpret_cast<float4*>(a.dvalues)[q] = make_float4(dv[0], dv[1], dv[2], dv[3]);
+      }
     }
   } else {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
