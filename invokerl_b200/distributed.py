@@ -51,3 +51,78 @@ def shard_batch(batch: RolloutBatch, rank: int, world: int) -> RolloutBatch:
         weight_version=batch.weight_version,
         extras={k: shard_rows(v, s, e, B) for k, v in batch.extras.items()},
     )
+
+
+def scatter_batch(batch: RolloutBatch | None, src: int = 0, group=None,
+                  device: torch.device | str | None = None) -> RolloutBatch:
+    """Give every rank its whole prompt groups of the batch held by rank `src`.
+
+    Replaces the replicate-everything `broadcast_batch` of invokerl/distributed.py:236-330: the
+    metadata (field shapes, dtypes, group size, extras layout) is broadcast as a small object,
+    then rank `src` sends each rank only its rows, so each byte of the batch crosses the network
+    once instead of world_size - 1 times.  Tensors whose leading dimension is B are sharded;
+    other tensors and non-tensor extras are broadcast whole.  Collective over `group`."""
+    import torch.distributed as dist
+
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    src_global = dist.get_global_rank(group, src) if group is not None else src
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else "cpu"
+
+    fields = ["token_ids", "prompt_mask", "response_mask", "attention_mask", "rewards", "token_rewards",
+              "old_log_probs", "ref_log_probs", "group_ids"]
+    if rank == src:
+        B = batch.token_ids.shape[0]
+        meta = {"B": B, "G": batch.group_size, "weight_version": batch.weight_version, "fields": {}, "extras": {}}
+        for f in fields:
+            t = getattr(batch, f)
+            meta["fields"][f] = None if t is None else (tuple(t.shape), t.dtype)
+        for k, v in batch.extras.items():
+            if isinstance(v, torch.Tensor):
+                meta["extras"][k] = ("rows" if (v.dim() >= 1 and v.shape[0] == B) else "whole", tuple(v.shape), v.dtype)
+            else:
+                meta["extras"][k] = ("object", v, None)
+        obj = [meta]
+    else:
+        obj = [None]
+    dist.broadcast_object_list(obj, src=src_global, group=group)
+    meta = obj[0]
+    B, G = meta["B"], meta["G"]
+    bounds = [group_shard_bounds(B, G, r, world) for r in range(world)]
+    s, e = bounds[rank]
+
+    def move(name, full, shape, dtype, rows: bool):
+        """Rank src sends slices (rows) or the whole tensor; returns this rank's part."""
+        if rows:
+            my_shape = (e - s,) + tuple(shape[1:])
+            if rank == src:
+                for r in range(world):
+                    if r == src:
+                        continue
+                    rs, re_ = bounds[r]
+                    dist.send(full[rs:re_].contiguous().to(device), dst=dist.get_global_rank(group, r)
+                              if group is not None else r, group=group)
+                return full[s:e].contiguous().to(device)
+            out = torch.empty(my_shape, dtype=dtype, device=device)
+            dist.recv(out, src=src_global, group=group)
+            return out
+        out = full.contiguous().to(device) if rank == src else torch.empty(shape, dtype=dtype, device=device)
+        dist.broadcast(out, src=src_global, group=group)
+        return out
+
+    vals = {}
+    for f in fields:
+        m = meta["fields"][f]
+        if m is None:
+            vals[f] = None
+            continue
+        shape, dtype = m
+        vals[f] = move(f, getattr(batch, f) if rank == src else None, shape, dtype, rows=True)
+    extras = {}
+    for k, (kind, a, b) in meta["extras"].items():
+        if kind == "object":
+            extras[k] = a
+        else:
+            extras[k] = move(k, batch.extras[k] if rank == src else None, a, b, rows=(kind == "rows"))
+    return RolloutBatch(**vals, group_size=G, weight_version=meta["weight_version"], extras=extras)

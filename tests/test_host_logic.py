@@ -108,3 +108,47 @@ def test_row_sharded_loss_matches_global_gloo():
                                         b.response_mask, b.rewards)
     assert abs(tot - float(loss)) <= 1e-5 * abs(float(loss)) + 1e-7
     torch.testing.assert_close(grad, g, rtol=1e-5, atol=1e-8)
+
+
+def _scatter_worker(rank, world, port, q):
+    import datetime
+
+    from invokerl_b200.distributed import scatter_batch
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        b = None
+        if rank == 0:
+            b = rollout_batch(6, 4, 48, prompt_len=(4, 16), completion_len=(4, 30), seed=31)
+            b.extras["truncated"] = torch.arange(24) % 5 == 0
+            b.extras["note"] = "kept"
+            b.extras["scale"] = torch.tensor([2.0, 3.0])
+        local = scatter_batch(b, src=0, device="cpu")
+        q.put((rank, local.token_ids, local.rewards, local.response_mask, local.extras["truncated"],
+               local.extras["note"], local.extras["scale"], local.group_size))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_scatter_batch_sends_each_rank_its_groups(world):
+    from invokerl_b200.distributed import shard_batch
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + world + os.getpid() % 200
+    procs = [ctx.Process(target=_scatter_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    full = rollout_batch(6, 4, 48, prompt_len=(4, 16), completion_len=(4, 30), seed=31)
+    full.extras["truncated"] = torch.arange(24) % 5 == 0
+    for rank, ids, rew, rm, tr, note, scale, G in got:
+        ref = shard_batch(full, rank, world)
+        assert torch.equal(ids, ref.token_ids) and torch.equal(rew, ref.rewards)
+        assert torch.equal(rm, ref.response_mask) and torch.equal(tr, ref.extras["truncated"])
+        assert note == "kept" and torch.equal(scale, torch.tensor([2.0, 3.0])) and G == 4
