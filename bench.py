@@ -697,6 +697,9 @@ def main() -> int:
         return 0
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    # Keep stdout to the one JSON line: NCCL's version banner would otherwise precede it.
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
