@@ -86,7 +86,7 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 // arrive on when a tile is consumed (this CTA's, or the pair leader's when cluster_arrive).
 // tile_base: number of tiles this CTA consumed before this unit (accumulator ring position).
 // Returns false when a wait gave up (abort).
-template <int EPI>
+template <int EPI, int TILE_N = BN, int NBUF = 2>
 __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
                                               int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
                                               const uint32_t (&acc_empty)[2], bool cluster_arrive,
@@ -111,14 +111,14 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   }
   float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
   for (int j = 0; j < ntiles; ++j) {
-    const int acc = (tile_base + j) & 1;
-    const uint32_t acc_phase = (uint32_t)((tile_base + j) >> 1) & 1u;
+    const int acc = NBUF == 2 ? ((tile_base + j) & 1) : 0;
+    const uint32_t acc_phase = NBUF == 2 ? ((uint32_t)((tile_base + j) >> 1) & 1u) : ((uint32_t)(tile_base + j) & 1u);
     if constexpr (EPI == EPI_F32) {
       // Pull this row's slice of the fp32 accumulator into L2 while the MMAs run, so the
       // read-modify-write below hits L2.
       if (row_ok && p.f32_mode != F32_STORE) {
-        const int n0p = (t_begin + j) * BN;
-        const int ncols = min(BN, p.N - n0p);
+        const int n0p = (t_begin + j) * TILE_N;
+        const int ncols = min(TILE_N, p.N - n0p);
         if (ncols > 0)
           asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
                        "r"((uint32_t)ncols * 4u)
@@ -130,10 +130,10 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       break;
     }
     tc_fence_after();
-    const int n0 = (t_begin + j) * BN;
-    const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+    const int n0 = (t_begin + j) * TILE_N;
+    const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 0; c < TILE_N; c += 32) {
       const int col0 = n0 + c;
       if (col0 >= p.N) break;  // warp-uniform
       float v[32];
@@ -223,7 +223,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
     if (row_ok && !*abort_v) {
       p.part_m[(int64_t)split * p.M + grow] = run_m;
       p.part_s[(int64_t)split * p.M + grow] = run_s;
-      if (tgt >= (int64_t)t_begin * BN && tgt < (int64_t)t_end * BN && tgt < p.N) p.part_t[grow] = tval;
+      if (tgt >= (int64_t)t_begin * TILE_N && tgt < (int64_t)t_end * TILE_N && tgt < p.N) p.part_t[grow] = tval;
     }
   }
   return ok;
@@ -567,6 +567,194 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Wide CTA-pair variant for long K: the pair computes a 256 x 512 tile per K step with two
+// N=256 MMAs into all 512 TMEM columns.  Each CTA stages 128 A rows and 256 of the 512 B rows per
+// 64-deep K block (48 KB, 4 stages), so L2 and shared-memory reads per MMA flop are 3/4 of the
+// 256 x 256 pair kernel.  The single accumulator is not double-buffered: the epilogue of tile j
+// delays the first MMA of tile j+1, which costs a few percent when K is long (H = 4096, dH, dW).
+constexpr int WN = 512;
+constexpr int kWideStages = 4;
+constexpr uint32_t kWideTileB = (WN / 2) * BK * 2;  // 32 KB: this CTA's half of the B tile
+constexpr uint32_t kWideStageBytes = kTileA + kWideTileB;
+constexpr uint32_t kWideSmemBytes = kWideStages * kWideStageBytes + 1024;
+
+template <int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    lmhead_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                            const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kWideStages], empty_bar[kWideStages], acc_full[2], acc_empty[2], drain_bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t rank = cluster_ctarank();
+  const int pair_id = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int m_pairs = (((p.M + BM - 1) / BM) + 1) >> 1;
+  const int nunits = m_pairs * p.splits;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWideStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
+    }
+    mbar_init(smem_u32(&drain_bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    fence_async_shared();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&tmem_holder), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_holder;
+  volatile int* abort_v = &abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = pair_id; u < nunits && ok; u += npairs) {
+        const int split = u % p.splits;
+        const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
+        const int t_begin = split * p.tiles_per_split;
+        const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+        for (int t = t_begin; t < t_end && ok; ++t) {
+          for (int kb = 0; kb < nk; ++kb) {
+            if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb_local = smem_u32(&full_bar[stage]);
+            const uint32_t fb_leader = mapa_shared(fb_local, 0);
+            if (rank == 0) mbar_arrive_expect_tx(fb_local, 2 * kWideStageBytes);
+            const uint32_t a_dst = smem_base + stage * kWideStageBytes;
+            const uint32_t b_dst = a_dst + kTileA;
+            const int k0 = kb * BK;
+            if constexpr (!A_MN) {
+              tma_load_2d_pair(a_dst, &tmA, fb_leader, k0, m0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BM / 64; ++c)
+                tma_load_2d_pair(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              // B rows of MMA h that this CTA provides: [t*512 + 256h + 128*rank, +128)
+              const int nb = t * WN + h * BN + (int)rank * (BN / 2);
+              const uint32_t bh = b_dst + h * ((BN / 2) * BK * 2);
+              if constexpr (!B_MN) {
+                tma_load_2d_pair(bh, &tmB, fb_leader, k0, nb);
+              } else {
+#pragma unroll
+                for (int c = 0; c < BN / 128; ++c) tma_load_2d_pair(bh + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0);
+              }
+            }
+            if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
+          }
+        }
+      }
+      if (ok) {
+        for (int s = 0; s < kWideStages; ++s) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) break;
+          if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
+        }
+      } else {
+        for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA only) ----------------
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(2 * BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int j = 0;
+      for (int u = pair_id; u < nunits && ok; u += npairs) {
+        const int split = u % p.splits;
+        const int t_begin = split * p.tiles_per_split;
+        const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+        for (int t = t_begin; t < t_end && ok; ++t, ++j) {
+          if (!mbar_wait(smem_u32(&acc_empty[0]), ((uint32_t)j & 1u) ^ 1u, abort_v, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int kb = 0; kb < nk; ++kb) {
+            if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_addr = smem_base + stage * kWideStageBytes;
+            const uint32_t b_addr = a_addr + kTileA;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
+                                       : smem_desc(a_addr + k * 32, 16, 1024);
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t bh = b_addr + h * ((BN / 2) * BK * 2);
+                const uint64_t bd = B_MN ? smem_desc(bh + k * 2048, kMnAtomBytes, 1024) : smem_desc(bh + k * 32, 16, 1024);
+                mma_bf16_pair(tmem_base + (uint32_t)(h * BN), ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              }
+            }
+            const uint32_t eb = smem_u32(&empty_bar[stage]);
+            mma_commit_pair(mapa_shared(eb, 0));
+            mma_commit_pair(mapa_shared(eb, 1));
+            if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
+          }
+          if (ok) {
+            const uint32_t fb = smem_u32(&acc_full[0]);
+            mma_commit_pair(mapa_shared(fb, 0));
+            mma_commit_pair(mapa_shared(fb, 1));
+          }
+        }
+      }
+      if (!ok) {
+        mma_commit_pair(mapa_shared(smem_u32(&drain_bar), 0));
+        mbar_wait_drain(smem_u32(&drain_bar), 0, p.err);
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs, own 128 rows x 512 columns) ----------------
+    const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
+    const uint32_t ae[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0), mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    int jb = 0;
+    for (int u = pair_id; u < nunits; u += npairs) {
+      const int split = u % p.splits;
+      const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
+      const int t_begin = split * p.tiles_per_split;
+      const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+      if (!epilogue_role<EPI, WN, 1>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v, jb))
+        break;
+      jb += t_end - t_begin;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // Merge the per-split (max, sum) pairs of each row: lse = ln2 * (M + log2 sum_s s_s 2^(m_s - M)).
 __global__ void lse_combine_kernel(const float* __restrict__ part_m, const float* __restrict__ part_s,
                                    const float* __restrict__ part_t, const int64_t* __restrict__ ids, int M,
@@ -641,10 +829,11 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
 }
 
 // Pair launch: a persistent 1-D grid of one CTA pair (cluster of 2) per two SMs.
-template <int EPI, bool A_MN, bool B_MN>
+template <int EPI, bool A_MN, bool B_MN, bool WIDE>
 int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int m_tiles, cudaStream_t s) {
-  auto kern = lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
-  IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmemBytes));
+  auto kern = WIDE ? lmhead_gemm_wide_kernel<EPI, A_MN, B_MN> : lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
+  const uint32_t smem_bytes = WIDE ? kWideSmemBytes : kPairSmemBytes;
+  IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
   IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
   const int64_t nunits = (int64_t)((m_tiles + 1) / 2) * p.splits;
   IKRL_REQUIRE(nunits <= 0x3fffffffLL, IKRL_ERR_UNSUPPORTED, "too many work units (%lld)", (long long)nunits);
@@ -658,7 +847,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * npairs), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -677,7 +866,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
     set_error("pair kernel launch failed: %s (grid %u x %u, max active clusters %d [%s], static smem %zu, "
               "dynamic %u, max dyn %d, regs %d, max threads %d)",
               cudaGetErrorString(e), cfg.gridDim.x, cfg.gridDim.y, nclusters, cudaGetErrorString(e2), fa.sharedSizeBytes,
-              kPairSmemBytes, fa.maxDynamicSharedSizeBytes, fa.numRegs, fa.maxThreadsPerBlock);
+              smem_bytes, fa.maxDynamicSharedSizeBytes, fa.numRegs, fa.maxThreadsPerBlock);
     return IKRL_ERR_CUDA;
   }
   return check_launch("lmhead_gemm_pair_kernel");
@@ -696,10 +885,36 @@ bool use_pairs() {
   return v == 1;
 }
 
+// Wide tiles (256 x 512 per pair) for long reductions: INVOKERL_B200_WIDE=0 never, =2 always,
+// otherwise when K >= 2048.
+bool use_wide(int K) {
+  const char* e = getenv("INVOKERL_B200_WIDE");
+  if (e != nullptr && e[0] == '0') return false;
+  if (e != nullptr && e[0] == '2') return true;
+  return K >= 2048;
+}
+
+int64_t cdiv64(int64_t a, int64_t b);
+
+// Launch one K1 GEMM with the kernel the configuration selects, filling in the tile ranges:
+// splits_hint > 0 asks for that many N ranges of 256-column tiles (fewer if the tiles run out);
+// splits_hint <= 0 gives every N tile its own unit.  p.splits holds the count actually used.
 template <int EPI, bool A_MN, bool B_MN>
-int launch_any(const CUtensorMap& a_single, const CUtensorMap& b_single, const CUtensorMap& a_pair,
-               const CUtensorMap& b_pair, const GemmParams& p, int m_tiles, cudaStream_t s) {
-  if (use_pairs()) return launch_gemm_pair<EPI, A_MN, B_MN>(a_pair, b_pair, p, m_tiles, s);
+int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CUtensorMap& a_pair,
+              const CUtensorMap& b_pair, GemmParams& p, int m_tiles, int splits_hint, cudaStream_t s) {
+  const int kind = !use_pairs() ? 0 : (use_wide(p.K) ? 2 : 1);
+  const int tile_n = kind == 2 ? WN : BN;
+  p.n_tiles = (int)cdiv64(p.N, tile_n);
+  if (splits_hint <= 0) {
+    p.tiles_per_split = 1;
+    p.splits = p.n_tiles;
+  } else {
+    p.tiles_per_split = (int)cdiv64(p.n_tiles, splits_hint);
+    p.splits = (int)cdiv64(p.n_tiles, p.tiles_per_split);
+  }
+  p.split_major = 1;
+  if (kind == 2) return launch_gemm_pair<EPI, A_MN, B_MN, true>(a_pair, b_pair, p, m_tiles, s);
+  if (kind == 1) return launch_gemm_pair<EPI, A_MN, B_MN, false>(a_pair, b_pair, p, m_tiles, s);
   return launch_gemm<EPI, A_MN, B_MN>(a_single, b_single, p, m_tiles, s);
 }
 
@@ -808,18 +1023,14 @@ int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_
   if ((rc = make_tmap(&tb2, weight, H, V, H, BN / 2, "weight"))) return rc;
   GemmParams p{};
   p.M = (int)N; p.N = V; p.K = H;
-  p.n_tiles = (int)cdiv64(V, BN);
-  p.tiles_per_split = L.tps;
-  p.splits = L.splits;
-  p.split_major = 1;
   p.ids = ids;
   p.part_m = reinterpret_cast<float*>(w + L.pm_off);
   p.part_s = reinterpret_cast<float*>(w + L.ps_off);
   p.part_t = reinterpret_cast<float*>(w + L.pt_off);
   p.err = err;
   const int m_tiles = (int)cdiv64(N, BM);
-  if ((rc = launch_any<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, s))) return rc;
-  lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V, L.splits,
+  if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s))) return rc;
+  lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V, p.splits,
                                                               logp, lse, err);
   return check_launch("lse_combine_kernel");
 }
@@ -861,7 +1072,6 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
   IKRL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
   const uint16_t* h16 = reinterpret_cast<const uint16_t*>(hidden);
   const int n_vt = (int)cdiv64(V, BN);
-  const int n_ht = (int)cdiv64(H, BN);
   const int64_t nchunks = cdiv64(N, L.chunk);
 
   CUtensorMap t_w_k, t_w_k2, t_w_mn;
@@ -880,15 +1090,11 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       if ((rc = make_tmap(&ta, hc, H, rows, H, BM, "hidden chunk"))) return rc;
       GemmParams p{};
       p.M = (int)rows; p.N = V; p.K = H;
-      p.n_tiles = n_vt;
       const int sp = choose_splits(m_tiles, n_vt, H);
-      p.tiles_per_split = (int)cdiv64(n_vt, sp);
-      p.splits = (int)cdiv64(n_vt, p.tiles_per_split);
-      p.split_major = 1;
       p.ids = ids + c0; p.lse = lse + c0; p.g = dlogp + c0;
       p.out_bf16 = dS; p.ld_bf16 = L.lds;
       p.err = err;
-      if ((rc = launch_any<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, s))) return rc;
+      if ((rc = launch_k1<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, sp, s))) return rc;
     }
     // 2) dH[chunk] = dS W
     if (dhidden) {
@@ -896,10 +1102,9 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       if ((rc = make_tmap(&ta, dS, V, rows, L.lds, BM, "dS"))) return rc;
       GemmParams p{};
       p.M = (int)rows; p.N = H; p.K = V;
-      p.n_tiles = n_ht; p.tiles_per_split = 1; p.splits = n_ht; p.split_major = 1;
       p.out_bf16 = reinterpret_cast<uint16_t*>(dhidden) + c0 * H; p.ld_bf16 = H;
       p.err = err;
-      if ((rc = launch_any<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, s))) return rc;
+      if ((rc = launch_k1<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, 0, s))) return rc;
     }
     // 3) dW (+)= dS^T h[chunk]
     if (dweight) {
@@ -908,13 +1113,12 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       if ((rc = make_tmap(&tb, hc, H, rows, H, 64, "hidden chunk^T"))) return rc;
       GemmParams p{};
       p.M = V; p.N = H; p.K = (int)rows;
-      p.n_tiles = n_ht; p.tiles_per_split = 1; p.splits = n_ht; p.split_major = 1;
       p.err = err;
       const int v_tiles = (int)cdiv64(V, BM);
       const bool last = ci == nchunks - 1;
       if (dweight_dtype == IKRL_DTYPE_BF16 && !L.need_dw32) {
         p.out_bf16 = reinterpret_cast<uint16_t*>(dweight); p.ld_bf16 = H;
-        if ((rc = launch_any<EPI_STORE_BF16, true, true>(ta, tb, ta, tb, p, v_tiles, s))) return rc;
+        if ((rc = launch_k1<EPI_STORE_BF16, true, true>(ta, tb, ta, tb, p, v_tiles, 0, s))) return rc;
       } else {
         if (dweight_dtype == IKRL_DTYPE_F32) {
           p.out_f32 = reinterpret_cast<float*>(dweight);
@@ -925,7 +1129,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
           p.f32_mode = last ? F32_ADD_TO_BF16 : (ci == 0 ? F32_STORE : F32_ADD);
         }
         p.ld_f32 = H;
-        if ((rc = launch_any<EPI_F32, true, true>(ta, tb, ta, tb, p, v_tiles, s))) return rc;
+        if ((rc = launch_k1<EPI_F32, true, true>(ta, tb, ta, tb, p, v_tiles, 0, s))) return rc;
       }
     }
   }
