@@ -2,6 +2,8 @@
 
 import os
 
+import socket
+
 import pytest
 import torch
 import torch.distributed as dist
@@ -14,6 +16,13 @@ from invokerl_b200.algorithms import DAPO, GRPO, PPO
 from invokerl_b200.distributed import group_shard_bounds, shard_batch
 from invokerl_b200.synthetic import rollout_batch
 
+
+
+def free_port() -> int:
+    """A TCP port that is free on 127.0.0.1 right now (for a gloo/NCCL rendezvous)."""
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
 
 @pytest.mark.parametrize("B,G,world", [(16, 4, 1), (16, 4, 2), (16, 4, 3), (128, 8, 8), (8, 8, 4), (12, 2, 5)])
 def test_group_shards_cover_whole_groups(B, G, world):
@@ -94,7 +103,7 @@ def test_row_sharded_loss_matches_global_gloo():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + os.getpid() % 1000
+    port = free_port()
     procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
@@ -137,7 +146,7 @@ def test_scatter_batch_sends_each_rank_its_groups(world):
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + world + os.getpid() % 200
+    port = free_port()
     procs = [ctx.Process(target=_scatter_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()

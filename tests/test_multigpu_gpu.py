@@ -6,6 +6,8 @@ Skipped when fewer than two GPUs are visible."""
 import datetime
 import os
 
+import socket
+
 import pytest
 import torch
 import torch.multiprocessing as mp
@@ -14,6 +16,13 @@ pytestmark = pytest.mark.gpu
 
 P, G, T, H, V = 4, 4, 64, 128, 3000
 
+
+
+def free_port() -> int:
+    """A TCP port that is free on 127.0.0.1 right now (for a gloo/NCCL rendezvous)."""
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
 
 def make_inputs():
     from invokerl_b200.synthetic import lmhead_inputs, rollout_batch
@@ -69,7 +78,7 @@ def test_two_rank_row_sharding_matches_full_batch():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + os.getpid() % 500
+    port = free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
