@@ -675,6 +675,63 @@ def run_reference(args, rank, world) -> dict | None:
     }
 
 
+def run_reference_gpu(args, device) -> dict:
+    """The reference's own GPU path for the LM-head workloads, for comparison: invokerl's
+    PolicyModel._chunked_lm_head_ce (F.linear + -F.cross_entropy per 64-token chunk under
+    torch.utils.checkpoint, cuBLAS GEMMs) and its GRPO, imported unchanged from baseline/_ref."""
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "invokerl" / "policy.py").exists():
+        return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
+    if args.workload not in LMHeadGRPO.PRESETS:
+        return {"impl": "reference-gpu", "unavailable": f"no GPU reference leg for workload {args.workload}"}
+    sys.path.insert(0, str(ref_root))
+    from invokerl.algorithms import GRPO as RefGRPO
+    from invokerl.algorithms import RolloutBatch as RefBatch
+    from invokerl.policy import PolicyModel as RefPolicy
+
+    wl = LMHeadGRPO(args.workload, args)
+    wl.setup(0, 1, device)
+    H, B, T = wl.H, wl.B, wl.T
+    head = torch.nn.Linear(H, V, bias=False, device=device, dtype=torch.bfloat16)
+    with torch.no_grad():
+        head.weight.copy_(wl.weight.detach())
+    pm = RefPolicy.__new__(RefPolicy)
+    pm.model = torch.nn.Module()
+    pm.model.lm_head = head
+    hidden = wl.hidden.detach().view(B, T, H).clone().requires_grad_(True)
+    db = wl.dev_batch
+    rb = RefBatch(token_ids=db.token_ids, prompt_mask=db.prompt_mask, response_mask=db.response_mask,
+                  attention_mask=db.attention_mask, rewards=db.rewards, token_rewards=None,
+                  old_log_probs=db.old_log_probs, ref_log_probs=db.ref_log_probs, group_ids=db.group_ids,
+                  group_size=db.group_size)
+    algo = RefGRPO(clip_eps=0.2, beta=0.04)
+    del wl
+
+    def step():
+        hidden.grad = None
+        head.weight.grad = None
+        lp = pm._chunked_lm_head_ce(hidden, rb.token_ids, 64)
+        adv = algo.compute_advantages(rb)
+        loss, _ = algo.compute_loss(lp, rb, adv)
+        loss.backward()
+
+    for _ in range(max(1, args.warmup - 1)):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(1, min(args.steps, 3))
+    s.record()
+    for _ in range(n):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    return {"metric": METRIC, "impl": "reference-gpu", "value": B * T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+            "steps": n, "config": {"workload": LMHeadGRPO.PRESETS[args.workload]["name"] + ", invokerl's own "
+                                   "chunked F.linear + cross_entropy path and GRPO on the same GPU"},
+            "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -686,6 +743,8 @@ def main() -> int:
     ap.add_argument("--rows", type=int, default=0, help="override the rows of the logits workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--reference-gpu", action="store_true",
+                    help="time the reference's own GPU path (baseline/_ref) instead; one extra JSON line")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -697,6 +756,10 @@ def main() -> int:
         return 0
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    if args.reference_gpu:
+        if rank == 0:
+            print(json.dumps(run_reference_gpu(args, device)), flush=True)
+        return 0
     # Keep stdout to the one JSON line: NCCL's version banner would otherwise precede it.
     if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
         os.environ["NCCL_DEBUG"] = "WARN"

@@ -36,6 +36,9 @@ constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
+// The wide kernel runs two epilogue warps per TMEM lane quadrant, each on half of the 512 columns.
+constexpr int kWideEpiWarps = 8;
+constexpr int kWideThreads = 64 + 32 * kWideEpiWarps;
 constexpr uint32_t kTileA = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileB = BN * BK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileA + kTileB;
@@ -64,6 +67,7 @@ struct GemmParams {
   int64_t ld_f32;
   int f32_mode;
   int* err;               // device error word
+  int part_sets;          // LSE partial sets written (splits x column halves), set by the launcher
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
@@ -86,7 +90,7 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 // arrive on when a tile is consumed (this CTA's, or the pair leader's when cluster_arrive).
 // tile_base: number of tiles this CTA consumed before this unit (accumulator ring position).
 // Returns false when a wait gave up (abort).
-template <int EPI, int TILE_N = BN, int NBUF = 2>
+template <int EPI, int TILE_N = BN, int NBUF = 2, int HALVES = 1>
 __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
                                               int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
                                               const uint32_t (&acc_empty)[2], bool cluster_arrive,
@@ -94,6 +98,9 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   const int ntiles = t_end - t_begin;
   bool ok = true;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
+  constexpr int kCols = TILE_N / HALVES;  // columns of the tile this warp drains
+  const int half = HALVES == 1 ? 0 : (warp - 2) / 4;
+  const int c_lo = half * kCols;
   const int r = q * 32 + lane;
   const int grow = m0 + r;
   const bool row_ok = grow < p.M;
@@ -110,6 +117,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
     }
   }
   float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
+  bool found = false;
   for (int j = 0; j < ntiles; ++j) {
     const int acc = NBUF == 2 ? ((tile_base + j) & 1) : 0;
     const uint32_t acc_phase = NBUF == 2 ? ((uint32_t)((tile_base + j) >> 1) & 1u) : ((uint32_t)(tile_base + j) & 1u);
@@ -117,8 +125,8 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       // Pull this row's slice of the fp32 accumulator into L2 while the MMAs run, so the
       // read-modify-write below hits L2.
       if (row_ok && p.f32_mode != F32_STORE) {
-        const int n0p = (t_begin + j) * TILE_N;
-        const int ncols = min(TILE_N, p.N - n0p);
+        const int n0p = (t_begin + j) * TILE_N + c_lo;
+        const int ncols = min(kCols, p.N - n0p);
         if (ncols > 0)
           asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
                        "r"((uint32_t)ncols * 4u)
@@ -133,7 +141,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
     const int n0 = (t_begin + j) * TILE_N;
     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
 #pragma unroll 1
-    for (int c = 0; c < TILE_N; c += 32) {
+    for (int c = c_lo; c < c_lo + kCols; c += 32) {
       const int col0 = n0 + c;
       if (col0 >= p.N) break;  // warp-uniform
       float v[32];
@@ -164,6 +172,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
           tval = acc_t;
+          found = true;
         }
       } else if constexpr (EPI == EPI_DLOGITS) {
         uint32_t w[16];
@@ -221,9 +230,10 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   }
   if constexpr (EPI == EPI_LSE) {
     if (row_ok && !*abort_v) {
-      p.part_m[(int64_t)split * p.M + grow] = run_m;
-      p.part_s[(int64_t)split * p.M + grow] = run_s;
-      if (tgt >= (int64_t)t_begin * TILE_N && tgt < (int64_t)t_end * TILE_N && tgt < p.N) p.part_t[grow] = tval;
+      const int set = split * HALVES + half;
+      p.part_m[(int64_t)set * p.M + grow] = run_m;
+      p.part_s[(int64_t)set * p.M + grow] = run_s;
+      if (found) p.part_t[grow] = tval;
     }
   }
   return ok;
@@ -579,7 +589,7 @@ constexpr uint32_t kWideStageBytes = kTileA + kWideTileB;
 constexpr uint32_t kWideSmemBytes = kWideStages * kWideStageBytes + 1024;
 
 template <int EPI, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kWideThreads, 1)
     lmhead_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -603,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&acc_full[a]), 1);
-      mbar_init(smem_u32(&acc_empty[a]), 2 * kEpiWarps);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * kWideEpiWarps);
     }
     mbar_init(smem_u32(&drain_bar), 1);
     abort_flag = 0;
@@ -740,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
       const int t_begin = split * p.tiles_per_split;
       const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-      if (!epilogue_role<EPI, WN, 1>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v, jb))
+      if (!epilogue_role<EPI, WN, 1, 2>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v, jb))
         break;
       jb += t_end - t_begin;
     }
@@ -846,7 +856,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   const int64_t npairs = std::max<int64_t>(1, persistent ? std::min<int64_t>(nunits, nsm / 2) : nunits);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * npairs), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(WIDE ? kWideThreads : kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -913,6 +923,7 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
     p.splits = (int)cdiv64(p.n_tiles, p.tiles_per_split);
   }
   p.split_major = 1;
+  p.part_sets = p.splits * (kind == 2 ? 2 : 1);
   if (kind == 2) return launch_gemm_pair<EPI, A_MN, B_MN, true>(a_pair, b_pair, p, m_tiles, s);
   if (kind == 1) return launch_gemm_pair<EPI, A_MN, B_MN, false>(a_pair, b_pair, p, m_tiles, s);
   return launch_gemm<EPI, A_MN, B_MN>(a_single, b_single, p, m_tiles, s);
@@ -948,8 +959,9 @@ FwdLayout fwd_layout(int64_t N, int H, int V) {
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   L.err_off = 0;
   L.pm_off = 256;
-  L.ps_off = al(L.pm_off + (size_t)L.splits * N * 4);
-  L.pt_off = al(L.ps_off + (size_t)L.splits * N * 4);
+  // up to two partial sets per split (the wide kernel's two column halves)
+  L.ps_off = al(L.pm_off + (size_t)2 * L.splits * N * 4);
+  L.pt_off = al(L.ps_off + (size_t)2 * L.splits * N * 4);
   L.total = al(L.pt_off + (size_t)N * 4);
   return L;
 }
@@ -1030,8 +1042,8 @@ int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_
   p.err = err;
   const int m_tiles = (int)cdiv64(N, BM);
   if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s))) return rc;
-  lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V, p.splits,
-                                                              logp, lse, err);
+  lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V,
+                                                              p.part_sets, logp, lse, err);
   return check_launch("lse_combine_kernel");
 }
 
