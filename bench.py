@@ -242,7 +242,9 @@ class LMHeadGRPO:
         return self.B * self.T
 
     def roofline(self, kernel_ms_per_step, peaks, peak_src):
-        flops = 6.0 * (self.Bl * self.T) * self.H * V
+        n = self.Bl * self.T
+        n_act = int(self.dev_batch.response_mask.sum())  # rows with a nonzero upstream gradient
+        flops = (2.0 * n + 4.0 * n_act) * self.H * V
         achieved = flops / (kernel_ms_per_step / 1e3) / 1e12
         peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         return {
@@ -254,8 +256,11 @@ class LMHeadGRPO:
             "frac": achieved / peak,
             "frac_of_burst_peak": achieved / peaks["bf16_tflops"],
             "peak_source": f"{peak_src} bf16 sustained (kernel timed inside a multi-second step)",
-            "algorithmic": "6*N*H*V FLOP per step: fwd 2NHV + dH 2NHV + dW 2NHV (the 2NHV logits "
-                           "recompute of the backward is executed but not counted)",
+            "algorithmic": "2*N*H*V (fwd over all N rows) + 4*N_act*H*V (dH and dW over the N_act rows whose "
+                           "upstream gradient is nonzero; masked rows contribute exact zeros and are skipped); "
+                           "the 2*N_act*H*V logits recompute of the backward is executed but not counted",
+            "rows": n, "active_rows": n_act,
+            "executed_tflop_per_step": (2.0 * n + 6.0 * n_act) * self.H * V / 1e12,
             "traffic": None,
         }
 
@@ -546,9 +551,159 @@ class GRPOHooks:
         return n / dt, dt, f"the whole batch ({n} tokens) per step (fp32 torch on the host CPU)"
 
 
+
+class E2EGRPO:
+    """One GRPO training step of a random-init Qwen3-0.6B (28 layers, H=1024, 16 q / 8 kv heads of
+    128, SwiGLU 3072, V=151936, tied, bf16, sdpa attention, gradient checkpointing as the
+    reference's PolicyModel sets it): advantages -> policy forward -> GRPO loss -> backward ->
+    AdamW step, as invokerl's Trainer.train_step plus the optimizer step (trainer.py:335-346).
+    The log-prob path is the fused LM-head kernel and the loss is K3; the transformer is
+    HuggingFace's.  Rollout log-probs (old, ref) are made once at setup."""
+
+    B, T, G = 64, 2048, 8
+
+    def __init__(self, key, args):
+        self.key = key
+        if args.batch:
+            if args.batch % self.G:
+                raise SystemExit(f"--batch must be a multiple of the group size {self.G}")
+            self.B = args.batch
+
+    @staticmethod
+    def qwen3_0p6b_config():
+        from transformers import Qwen3Config
+
+        return Qwen3Config(vocab_size=V, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                           num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
+                           rms_norm_eps=1e-6, max_position_embeddings=40960, tie_word_embeddings=True,
+                           use_cache=False)
+
+    @classmethod
+    def build_model(cls, device):
+        from transformers import Qwen3ForCausalLM
+
+        cfg = cls.qwen3_0p6b_config()
+        cfg._attn_implementation = "sdpa"
+        torch.manual_seed(0)
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            with torch.device(device):
+                model = Qwen3ForCausalLM(cfg)
+        finally:
+            torch.set_default_dtype(prev)
+        model.train()
+        model.config.use_cache = False
+        model.gradient_checkpointing_enable()
+        return model
+
+    @staticmethod
+    def model_flops_per_token(cfg, T) -> float:
+        """6 x matmul parameters (LM head included) + causal attention (QK^T and AV, fwd + bwd);
+        the checkpointing recompute is not counted."""
+        H, L, I = cfg.hidden_size, cfg.num_hidden_layers, cfg.intermediate_size
+        dq, dkv = cfg.num_attention_heads * cfg.head_dim, cfg.num_key_value_heads * cfg.head_dim
+        per_layer = H * dq + 2 * H * dkv + dq * H + 3 * H * I
+        params = L * per_layer + H * cfg.vocab_size
+        attn = L * 3 * 2 * 2 * (T / 2) * dq
+        return 6.0 * params + attn
+
+    def setup(self, rank, world, device):
+        from invokerl_b200.algorithms import GRPO
+        from invokerl_b200.distributed import shard_batch
+        from invokerl_b200.policy import PolicyModel
+        from invokerl_b200.synthetic import rollout_batch
+
+        self.model = self.build_model(device)
+        self.policy = PolicyModel.from_model(self.model, device=device)
+        b = rollout_batch(self.B // self.G, self.G, self.T, prompt_len=(64, 256), completion_len=(32, 256),
+                          vocab=V, seed=0)
+        local = shard_batch(b, rank, world)
+        local.extras = {}
+        lp = self.policy.forward_no_grad(local.token_ids.to(device), local.attention_mask.to(device))
+        g = torch.Generator(device=device).manual_seed(11 + int(local.group_ids[0]))
+        local.old_log_probs = (lp + 0.05 * torch.randn(lp.shape, device=device, generator=g)).cpu()
+        local.ref_log_probs = (lp + 0.1 * torch.randn(lp.shape, device=device, generator=g)).cpu()
+        del lp
+        self.local = local
+        self.dev_batch = to_device_batch(local, device)
+        self.algo = GRPO(clip_eps=0.2, beta=0.04, row_sharded=world > 1)
+        self.opt = torch.optim.AdamW(self.model.parameters(), lr=1e-6, fused=True)
+        self.params = [p for p in self.model.parameters() if p.requires_grad]
+        self.world = world
+        self.device = device
+
+    def timed_functions(self):
+        return ["lmhead_forward_raw", "lmhead_backward_raw"]
+
+    def _reduce_grads(self):
+        # Row shards of whole groups: the rank losses sum to the global loss, so the gradients sum.
+        grads = [p.grad for p in self.params if p.grad is not None]
+        flat = torch._utils._flatten_dense_tensors(grads)
+        dist.all_reduce(flat)
+        for g, r in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+            g.copy_(r)
+
+    def _step(self, batch):
+        adv = self.algo.compute_advantages(batch)
+        lp = self.policy.forward(batch.token_ids, batch.attention_mask)
+        loss, metrics = self.algo.compute_loss(lp, batch, adv)
+        loss.backward()
+        if self.world > 1:
+            self._reduce_grads()
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        return float(loss.detach()), metrics
+
+    def step(self):
+        return self._step(self.dev_batch)
+
+    def tokens_per_step(self):
+        return self.B * self.T
+
+    def roofline(self, kernel_ms_per_step, peaks, peak_src):
+        return {}
+
+    def step_roofline(self, ms_per_step, kernel_ms_per_step, peaks, peak_src):
+        fpt = self.model_flops_per_token(self.model.config, self.T)
+        flops = fpt * self.B * self.T / max(1, self.world)
+        achieved = flops / (ms_per_step / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        H = self.model.config.hidden_size
+        n_rows = self.dev_batch.token_ids.numel()
+        head_tf = 6.0 * n_rows * H * V / (kernel_ms_per_step / 1e3) / 1e12 if kernel_ms_per_step > 0 else None
+        return {"kernel": "whole GRPO step (HF transformer + fused LM-head log-prob + K3 loss + AdamW); MFU",
+                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{peak_src} bf16 sustained",
+                "algorithmic": f"model FLOPs {fpt / 1e9:.2f} GFLOP/token: 6 x matmul params (LM head included) "
+                               "+ causal attention fwd+bwd; checkpoint recompute not counted",
+                "lmhead_kernels_ms_per_step": kernel_ms_per_step,
+                "lmhead_tflops": head_tf,
+                "traffic": None}
+
+    def config(self, world):
+        return {"workload": "GRPO train step, random-init Qwen3-0.6B (28 layers, H=1024, tied V=151936, bf16, "
+                            "sdpa, gradient checkpointing) + AdamW; log-probs via the fused LM-head kernel",
+                "global_batch": self.B, "seq_len": self.T, "group_size": self.G,
+                "parallelism": f"dp{world} (row shards of whole groups; gradient all-reduce)",
+                "l2": "activations and weights far larger than L2, no flush"}
+
+    def e2e(self):
+        hb = host_batch(self.local)
+        h2d = batch_bytes(hb)
+
+        def one():
+            return self._step(to_device_batch(hb, self.device))
+
+        return one, h2d, 4 + 4 * 12
+
+    def cpu_sample(self, rows, steps):
+        return None
+
+
 WORKLOADS = {"lmhead-8b": LMHeadGRPO, "lmhead-0.6b": LMHeadGRPO, "logits": LogitsLogProb, "grpo": GRPOHooks,
-             "grpo-hbm": GRPOHooks}
-CPU_ROWS = {"lmhead-8b": 32, "lmhead-0.6b": 96, "logits": 1024, "grpo": 0, "grpo-hbm": 0}
+             "grpo-hbm": GRPOHooks, "e2e-0.6b": E2EGRPO}
+CPU_ROWS = {"lmhead-8b": 32, "lmhead-0.6b": 96, "logits": 1024, "grpo": 0, "grpo-hbm": 0, "e2e-0.6b": 0}
 
 
 def run_native(args, rank, world, device) -> dict | None:
@@ -629,13 +784,14 @@ def run_native(args, rank, world, device) -> dict | None:
         "dtype": "f32" if args.workload.startswith("grpo") else "bf16",
         "data": "synthetic (seeded; random-init weights)",
         "config": wl.config(world),
-        "roofline": wl.roofline(kms / args.steps, peaks, peak_src),
+        "roofline": (wl.step_roofline(ms / args.steps, (kms / args.steps) if timer.pairs else 0.0, peaks, peak_src)
+                     if isinstance(wl, E2EGRPO) else wl.roofline(kms / args.steps, peaks, peak_src)),
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clocks,
         "loss": loss,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and not isinstance(wl, E2EGRPO):
         rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", CPU_ROWS[args.workload]))
         tok_s, dt, sample = wl.cpu_sample(rows, 3)
         res["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
@@ -647,6 +803,9 @@ def run_reference(args, rank, world) -> dict | None:
     """The reference's CPU arithmetic on the host cores (rank 0 only), same metric and config."""
     if rank != 0:
         return None
+    if args.workload == "e2e-0.6b":
+        return {"impl": "reference", "unavailable": "a 0.6B-parameter training step on the host CPU is not a "
+                "meaningful baseline; bench.py --workload e2e-0.6b --reference-gpu times the reference's GPU path"}
     wl = WORKLOADS[args.workload](args.workload, args)
     rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", max(1, CPU_ROWS[args.workload] // 2)))
     for _ in range(max(0, args.warmup - 1)):
@@ -682,9 +841,11 @@ def run_reference_gpu(args, device) -> dict:
     ref_root = ROOT / "baseline" / "_ref"
     if not (ref_root / "invokerl" / "policy.py").exists():
         return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
-    if args.workload not in LMHeadGRPO.PRESETS:
+    if args.workload not in LMHeadGRPO.PRESETS and args.workload != "e2e-0.6b":
         return {"impl": "reference-gpu", "unavailable": f"no GPU reference leg for workload {args.workload}"}
     sys.path.insert(0, str(ref_root))
+    if args.workload == "e2e-0.6b":
+        return run_reference_gpu_e2e(args, device)
     from invokerl.algorithms import GRPO as RefGRPO
     from invokerl.algorithms import RolloutBatch as RefBatch
     from invokerl.policy import PolicyModel as RefPolicy
@@ -729,6 +890,65 @@ def run_reference_gpu(args, device) -> dict:
     return {"metric": METRIC, "impl": "reference-gpu", "value": B * T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
             "steps": n, "config": {"workload": LMHeadGRPO.PRESETS[args.workload]["name"] + ", invokerl's own "
                                    "chunked F.linear + cross_entropy path and GRPO on the same GPU"},
+            "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
+
+
+def run_reference_gpu_e2e(args, device) -> dict:
+    """The same GRPO train step with invokerl's own PolicyModel.forward (its chunked
+    F.linear + cross_entropy log-prob path under torch.utils.checkpoint) and its GRPO, on the same
+    random-init model, batch and optimizer."""
+    from invokerl.algorithms import GRPO as RefGRPO
+    from invokerl.algorithms import RolloutBatch as RefBatch
+    from invokerl.policy import PolicyModel as RefPolicy
+    from invokerl_b200.synthetic import rollout_batch
+
+    wl = E2EGRPO(args.workload, args)
+    model = E2EGRPO.build_model(device)
+    pm = RefPolicy.__new__(RefPolicy)
+    pm.model, pm.device, pm.dtype = model, device, torch.bfloat16
+    pm.master_weights_fp32, pm._autocast_dtype, pm._fsdp_wrapped = False, None, False
+    b = rollout_batch(wl.B // wl.G, wl.G, wl.T, prompt_len=(64, 256), completion_len=(32, 256), vocab=V, seed=0)
+    ids, am = b.token_ids.to(device), b.attention_mask.to(device)
+    with torch.no_grad():
+        lp = pm.forward(ids, am).float()
+    g = torch.Generator(device=device).manual_seed(11)
+    old = lp + 0.05 * torch.randn(lp.shape, device=device, generator=g)
+    ref = lp + 0.1 * torch.randn(lp.shape, device=device, generator=g)
+    del lp
+    rb = RefBatch(token_ids=ids, prompt_mask=b.prompt_mask.to(device), response_mask=b.response_mask.to(device),
+                  attention_mask=am, rewards=b.rewards.to(device), token_rewards=None, old_log_probs=old,
+                  ref_log_probs=ref, group_ids=b.group_ids.to(device), group_size=wl.G)
+    algo = RefGRPO(clip_eps=0.2, beta=0.04)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-6, fused=True)
+
+    def step():
+        adv = algo.compute_advantages(rb)
+        new = pm.forward(rb.token_ids, rb.attention_mask)
+        loss, _ = algo.compute_loss(new, rb, adv)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    for _ in range(max(1, args.warmup - 1)):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = max(1, min(args.steps, 3))
+    s.record()
+    for _ in range(n):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    fpt = E2EGRPO.model_flops_per_token(model.config, wl.T)
+    peaks, _ = load_peaks()
+    achieved = fpt * wl.B * wl.T / (ms / 1e3) / 1e12
+    return {"metric": METRIC, "impl": "reference-gpu", "value": wl.B * wl.T / (ms / 1e3), "unit": UNIT,
+            "ms_per_step": ms, "steps": n, "mfu_tflops": achieved,
+            "mfu_frac": achieved / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
+            "config": {"workload": "GRPO train step, random-init Qwen3-0.6B + AdamW, invokerl's own "
+                                   "PolicyModel.forward (chunked F.linear + cross_entropy) and GRPO on the same GPU",
+                       "global_batch": wl.B, "seq_len": wl.T},
             "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
 
 

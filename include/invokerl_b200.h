@@ -225,7 +225,14 @@ IKRL_API int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, con
  * [V, H] (nullable; IKRL_DTYPE_BF16 or IKRL_DTYPE_F32, the latter optionally accumulated into).
  * Rows are processed in chunks of `chunk_rows` (<= 0: all rows at once); the workspace holds one
  * chunk of bf16 dlogits [chunk, round_up(V, 64)] plus, for a bf16 dweight over several chunks,
- * an fp32 [V, H] accumulator. */
+ * an fp32 [V, H] accumulator, plus the row-compaction buffers below.
+ * Rows whose dlogp is exactly zero (tokens outside the loss mask) and ignore_index rows add
+ * exact zeros to both gradients; they are left out of the GEMMs: the other rows are gathered
+ * in order into a dense block (a copy of their hidden rows, [N, H] bf16 at most), and dhidden
+ * is scattered back with zero rows elsewhere.  Choosing the chunks then needs the active-row
+ * count on the host: the call synchronises `stream` once.  Inside a stream capture, or with
+ * INVOKERL_B200_SKIP_ZERO_ROWS=0 in the environment, all rows are processed and the call does
+ * not synchronise. */
 IKRL_API size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows,
                                                 int32_t dweight_dtype, int32_t accumulate_dweight);
 IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids,

@@ -68,6 +68,7 @@ struct GemmParams {
   int f32_mode;
   int* err;               // device error word
   int part_sets;          // LSE partial sets written (splits x column halves), set by the launcher
+  int a_policy, b_policy; // L2 eviction priority of the A / B loads: 0 normal, 1 evict-last, 2 evict-first
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
@@ -637,6 +638,8 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
+      const uint64_t pol_a = l2_policy(p.a_policy);
+      const uint64_t pol_b = l2_policy(p.b_policy);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -658,11 +661,11 @@ __global__ void __launch_bounds__(kWideThreads, 1)
             const uint32_t b_dst = a_dst + kTileA;
             const int k0 = kb * BK;
             if constexpr (!A_MN) {
-              tma_load_2d_pair(a_dst, &tmA, fb_leader, k0, m0);
+              tma_load_2d_pair_hint(a_dst, &tmA, fb_leader, k0, m0, pol_a);
             } else {
 #pragma unroll
               for (int c = 0; c < BM / 64; ++c)
-                tma_load_2d_pair(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0);
+                tma_load_2d_pair_hint(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0, pol_a);
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -670,10 +673,11 @@ __global__ void __launch_bounds__(kWideThreads, 1)
               const int nb = t * WN + h * BN + (int)rank * (BN / 2);
               const uint32_t bh = b_dst + h * ((BN / 2) * BK * 2);
               if constexpr (!B_MN) {
-                tma_load_2d_pair(bh, &tmB, fb_leader, k0, nb);
+                tma_load_2d_pair_hint(bh, &tmB, fb_leader, k0, nb, pol_b);
               } else {
 #pragma unroll
-                for (int c = 0; c < BN / 128; ++c) tma_load_2d_pair(bh + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0);
+                for (int c = 0; c < BN / 128; ++c)
+                  tma_load_2d_pair_hint(bh + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0, pol_b);
               }
             }
             if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
@@ -924,6 +928,17 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
   }
   p.split_major = 1;
   p.part_sets = p.splits * (kind == 2 ? 2 : 1);
+  {
+    // Two digits "ab": L2 policy of the A and B loads of the wide kernel (0 normal, 1 evict-last,
+    // 2 evict-first).  Default "10": A (re-read by every tile of a unit) evict-last, B normal;
+    // evict-first on B measured 40% more DRAM traffic.
+    const char* e = getenv("INVOKERL_B200_L2_HINT");
+    p.a_policy = 1; p.b_policy = 0;
+    if (e != nullptr && e[0] >= '0' && e[0] <= '2') {
+      p.a_policy = e[0] - '0';
+      if (e[1] >= '0' && e[1] <= '2') p.b_policy = e[1] - '0';
+    }
+  }
   if (kind == 2) return launch_gemm_pair<EPI, A_MN, B_MN, true>(a_pair, b_pair, p, m_tiles, s);
   if (kind == 1) return launch_gemm_pair<EPI, A_MN, B_MN, false>(a_pair, b_pair, p, m_tiles, s);
   return launch_gemm<EPI, A_MN, B_MN>(a_single, b_single, p, m_tiles, s);
@@ -934,7 +949,10 @@ int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Vocab splits for the row-sweeping GEMMs: enough that the row blocks resident at once keep their
 // A tiles in L2 (about 24 MB of hidden rows), and enough CTAs to fill the GPU.
 int choose_splits(int64_t m_tiles, int n_tiles, int H) {
-  int64_t budget_mb = 24;
+  // L2 share for the A rows of the units in flight.  Long reductions (the wide kernel, whose A
+  // loads are marked evict-last) keep more rows resident and split the vocabulary less: at
+  // H = 4096, 80 MB gives 2 splits and measured 30% less DRAM traffic than 24 MB (7 splits).
+  int64_t budget_mb = H >= 2048 ? 80 : 24;
   if (const char* e = getenv("INVOKERL_B200_L2_BUDGET_MB")) budget_mb = std::max<int64_t>(1, atoll(e));
   const int64_t resident_rows_budget = (budget_mb << 20) / (2ll * H);   // rows whose A tiles fit the budget
   const int64_t blocks_resident = std::max<int64_t>(1, resident_rows_budget / BM);
@@ -970,7 +988,13 @@ struct BwdLayout {
   size_t err_off, ds_off, dw_off, total;
   int64_t chunk, lds;
   bool need_dw32;
+  // active-row compaction (rows whose upstream gradient is exactly zero are skipped)
+  size_t cnt_off, nact_off, idx_off, pos_off, idc_off, lsec_off, gc_off, hc_off;
+  int cblocks;
 };
+
+constexpr int kCompactRows = 2048;    // rows per block of the compaction kernels
+constexpr int kCompactThreads = 256;
 
 BwdLayout bwd_layout(int64_t N, int H, int V, int64_t chunk_rows, int dweight_dtype, int accumulate) {
   BwdLayout L;
@@ -985,8 +1009,131 @@ BwdLayout bwd_layout(int64_t N, int H, int V, int64_t chunk_rows, int dweight_dt
   L.err_off = 0;
   L.ds_off = 256;
   L.dw_off = al(L.ds_off + (size_t)L.chunk * L.lds * 2);
-  L.total = L.dw_off + (L.need_dw32 ? al((size_t)V * H * 4) : 0);
+  size_t o = L.dw_off + (L.need_dw32 ? al((size_t)V * H * 4) : 0);
+  L.cblocks = (int)std::max<int64_t>(1, cdiv64(N, kCompactRows));
+  L.cnt_off = o;   o = al(o + (size_t)L.cblocks * 4);
+  L.nact_off = o;  o = al(o + 8);
+  L.idx_off = o;   o = al(o + (size_t)N * 4);
+  L.pos_off = o;   o = al(o + (size_t)N * 4);
+  L.idc_off = o;   o = al(o + (size_t)N * 8);
+  L.lsec_off = o;  o = al(o + (size_t)N * 4);
+  L.gc_off = o;    o = al(o + (size_t)N * 4);
+  L.hc_off = o;    o = al(o + (size_t)N * H * 2);
+  L.total = o;
   return L;
+}
+
+// ---- active-row compaction -------------------------------------------------------------------
+//
+// A row contributes to dHidden and dW only through g * (onehot - softmax): rows whose upstream
+// gradient g is exactly zero (tokens outside the response mask) and ignore_index rows contribute
+// exact zeros.  The backward gathers the other rows, in row order, into a dense block, runs the
+// three GEMMs on that block only, and scatters dHidden back (zero rows elsewhere).  NaN gradients
+// count as active, so they propagate as in the dense computation.
+
+__device__ __forceinline__ bool row_active(const float* __restrict__ g, const int64_t* __restrict__ ids, int64_t r) {
+  return ids[r] != -100 && g[r] != 0.f;
+}
+
+__global__ void __launch_bounds__(kCompactThreads) active_count_kernel(const float* __restrict__ g,
+                                                                       const int64_t* __restrict__ ids, int64_t N,
+                                                                       int* __restrict__ counts) {
+  __shared__ int wsum[kCompactThreads / 32];
+  const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
+  int c = 0;
+  for (int i = threadIdx.x; i < kCompactRows; i += blockDim.x) {
+    const int64_t r = r0 + i;
+    if (r < N && row_active(g, ids, r)) ++c;
+  }
+  c = warp_sum(c);
+  if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kCompactThreads / 32; ++w) t += wsum[w];
+    counts[blockIdx.x] = t;
+  }
+}
+
+// Block b writes its active rows after those of blocks 0..b-1, in row order: idx[k] = row,
+// pos[row] = k (-1 for skipped rows), and the compacted ids / lse / g.  The last block writes
+// the total to n_act.
+__global__ void __launch_bounds__(kCompactThreads) compact_rows_kernel(
+    const float* __restrict__ g, const int64_t* __restrict__ ids, const float* __restrict__ lse, int64_t N,
+    const int* __restrict__ counts, int* __restrict__ idx, int* __restrict__ pos, int64_t* __restrict__ ids_c,
+    float* __restrict__ lse_c, float* __restrict__ g_c, int64_t* __restrict__ n_act) {
+  constexpr int kWarps = kCompactThreads / 32;
+  __shared__ int wtot[kWarps];
+  __shared__ int s_base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int part = 0;
+  for (int b = threadIdx.x; b < (int)blockIdx.x; b += blockDim.x) part += counts[b];
+  part = warp_sum(part);
+  if (lane == 0) wtot[warp] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kWarps; ++w) t += wtot[w];
+    s_base = t;
+  }
+  __syncthreads();
+  int base = s_base;
+  const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
+  for (int off = 0; off < kCompactRows; off += kCompactThreads) {
+    const int64_t r = r0 + off + threadIdx.x;
+    const bool act = r < N && row_active(g, ids, r);
+    const unsigned bal = __ballot_sync(0xffffffffu, act);
+    __syncthreads();  // wtot is reused
+    if (lane == 0) wtot[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      before += (w < warp) ? wtot[w] : 0;
+      total += wtot[w];
+    }
+    if (act) {
+      const int k = base + before + __popc(bal & ((1u << lane) - 1u));
+      idx[k] = (int)r;
+      pos[r] = k;
+      ids_c[k] = ids[r];
+      lse_c[k] = lse[r];
+      g_c[k] = g[r];
+    } else if (r < N) {
+      pos[r] = -1;
+    }
+    base += total;
+  }
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) *n_act = base;
+}
+
+// h_c[k] = h[idx[k]] for k < n, 16 bytes per thread.
+__global__ void gather_rows_kernel(const uint4* __restrict__ h, const int* __restrict__ idx, int64_t n, int vec_per_row,
+                                   uint4* __restrict__ h_c) {
+  const int64_t total = n * vec_per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = i / vec_per_row;
+    const int c = (int)(i - k * vec_per_row);
+    h_c[i] = h[(int64_t)idx[k] * vec_per_row + c];
+  }
+}
+
+// out[r] = pos[r] >= 0 ? src[pos[r]] : 0 for every row r < N, 16 bytes per thread.
+__global__ void scatter_rows_kernel(const uint4* __restrict__ src, const int* __restrict__ pos, int64_t N,
+                                    int vec_per_row, uint4* __restrict__ out) {
+  const int64_t total = N * vec_per_row;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vec_per_row;
+    const int c = (int)(i - r * vec_per_row);
+    const int k = pos[r];
+    out[i] = k >= 0 ? src[(int64_t)k * vec_per_row + c] : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// Row skipping is on unless INVOKERL_B200_SKIP_ZERO_ROWS=0.
+bool skip_zero_rows_enabled() {
+  const char* e = getenv("INVOKERL_B200_SKIP_ZERO_ROWS");
+  return !(e != nullptr && e[0] == '0');
 }
 
 int check_common(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int H, int V,
@@ -1082,9 +1229,61 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
   uint16_t* dS = reinterpret_cast<uint16_t*>(w + L.ds_off);
   float* dw32 = L.need_dw32 ? reinterpret_cast<float*>(w + L.dw_off) : nullptr;
   IKRL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
-  const uint16_t* h16 = reinterpret_cast<const uint16_t*>(hidden);
   const int n_vt = (int)cdiv64(V, BN);
-  const int64_t nchunks = cdiv64(N, L.chunk);
+
+  // Rows the GEMMs run on: all N, or the compacted active rows.
+  const uint16_t* hsrc = reinterpret_cast<const uint16_t*>(hidden);
+  const int64_t* idsrc = ids;
+  const float* lsesrc = lse;
+  const float* gsrc = dlogp;
+  int64_t Nw = N;
+  uint16_t* dh_out = reinterpret_cast<uint16_t*>(dhidden);  // where the dH GEMMs write
+  const int* pos = nullptr;                                  // set when dH must be scattered back
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  IKRL_CUDA(cudaStreamIsCapturing(s, &cap));
+  if (skip_zero_rows_enabled() && cap == cudaStreamCaptureStatusNone && N <= INT32_MAX) {
+    int* counts = reinterpret_cast<int*>(w + L.cnt_off);
+    int64_t* n_act_d = reinterpret_cast<int64_t*>(w + L.nact_off);
+    int* idx = reinterpret_cast<int*>(w + L.idx_off);
+    int* posw = reinterpret_cast<int*>(w + L.pos_off);
+    int64_t* ids_c = reinterpret_cast<int64_t*>(w + L.idc_off);
+    float* lse_c = reinterpret_cast<float*>(w + L.lsec_off);
+    float* g_c = reinterpret_cast<float*>(w + L.gc_off);
+    uint16_t* h_c = reinterpret_cast<uint16_t*>(w + L.hc_off);
+    const int nb = (int)cdiv64(N, kCompactRows);
+    active_count_kernel<<<nb, kCompactThreads, 0, s>>>(dlogp, ids, N, counts);
+    if ((rc = check_launch("active_count_kernel"))) return rc;
+    compact_rows_kernel<<<nb, kCompactThreads, 0, s>>>(dlogp, ids, lse, N, counts, idx, posw, ids_c, lse_c, g_c,
+                                                        n_act_d);
+    if ((rc = check_launch("compact_rows_kernel"))) return rc;
+    // The chunk plan depends on the active count: read it back (one stream synchronisation).
+    int64_t n_act = 0;
+    IKRL_CUDA(cudaMemcpyAsync(&n_act, n_act_d, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    IKRL_CUDA(cudaStreamSynchronize(s));
+    IKRL_REQUIRE(n_act >= 0 && n_act <= N, IKRL_ERR_DEVICE, "ikrl_lmhead_logprob_bwd: bad active-row count %lld",
+                 (long long)n_act);
+    if (n_act == 0) {
+      if (dhidden) IKRL_CUDA(cudaMemsetAsync(dhidden, 0, (size_t)N * H * 2, s));
+      if (dweight && !accumulate_dweight)
+        IKRL_CUDA(cudaMemsetAsync(dweight, 0, (size_t)V * H * (dweight_dtype == IKRL_DTYPE_F32 ? 4 : 2), s));
+      return IKRL_OK;
+    }
+    if (n_act < N) {
+      const int vpr = H / 8;
+      const int gb = (int)std::min<int64_t>(cdiv64(n_act * vpr, 256), 148ll * 16);
+      gather_rows_kernel<<<gb, 256, 0, s>>>(reinterpret_cast<const uint4*>(hidden), idx, n_act, vpr,
+                                            reinterpret_cast<uint4*>(h_c));
+      if ((rc = check_launch("gather_rows_kernel"))) return rc;
+      hsrc = h_c; idsrc = ids_c; lsesrc = lse_c; gsrc = g_c; Nw = n_act;
+      // dH of a chunk overwrites that chunk's gathered rows once dW has read them.
+      if (dhidden) { dh_out = h_c; pos = posw; }
+    }
+  }
+
+  const BwdLayout Lw = bwd_layout(Nw, H, V, chunk_rows, dweight_dtype, accumulate_dweight);
+  const int64_t chunk = std::min(L.chunk, Lw.chunk);
+  const int64_t nchunks = cdiv64(Nw, chunk);
+  const bool use_dw32 = (dweight_dtype == IKRL_DTYPE_BF16) && nchunks > 1;
 
   CUtensorMap t_w_k, t_w_k2, t_w_mn;
   if ((rc = make_tmap(&t_w_k, weight, H, V, H, BN, "weight"))) return rc;
@@ -1092,10 +1291,10 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
   if ((rc = make_tmap(&t_w_mn, weight, H, V, H, 64, "weight^T"))) return rc;
 
   for (int64_t ci = 0; ci < nchunks; ++ci) {
-    const int64_t c0 = ci * L.chunk;
-    const int64_t rows = std::min<int64_t>(L.chunk, N - c0);
+    const int64_t c0 = ci * chunk;
+    const int64_t rows = std::min<int64_t>(chunk, Nw - c0);
     const int m_tiles = (int)cdiv64(rows, BM);
-    const uint16_t* hc = h16 + c0 * H;
+    const uint16_t* hc = hsrc + c0 * H;
     // 1) dS = g * (onehot - softmax(h W^T)) for this chunk
     {
       CUtensorMap ta;
@@ -1103,22 +1302,12 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       GemmParams p{};
       p.M = (int)rows; p.N = V; p.K = H;
       const int sp = choose_splits(m_tiles, n_vt, H);
-      p.ids = ids + c0; p.lse = lse + c0; p.g = dlogp + c0;
+      p.ids = idsrc + c0; p.lse = lsesrc + c0; p.g = gsrc + c0;
       p.out_bf16 = dS; p.ld_bf16 = L.lds;
       p.err = err;
       if ((rc = launch_k1<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, sp, s))) return rc;
     }
-    // 2) dH[chunk] = dS W
-    if (dhidden) {
-      CUtensorMap ta;
-      if ((rc = make_tmap(&ta, dS, V, rows, L.lds, BM, "dS"))) return rc;
-      GemmParams p{};
-      p.M = (int)rows; p.N = H; p.K = V;
-      p.out_bf16 = reinterpret_cast<uint16_t*>(dhidden) + c0 * H; p.ld_bf16 = H;
-      p.err = err;
-      if ((rc = launch_k1<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, 0, s))) return rc;
-    }
-    // 3) dW (+)= dS^T h[chunk]
+    // 2) dW (+)= dS^T h[chunk]
     if (dweight) {
       CUtensorMap ta, tb;
       if ((rc = make_tmap(&ta, dS, V, rows, L.lds, 64, "dS^T"))) return rc;
@@ -1128,7 +1317,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       p.err = err;
       const int v_tiles = (int)cdiv64(V, BM);
       const bool last = ci == nchunks - 1;
-      if (dweight_dtype == IKRL_DTYPE_BF16 && !L.need_dw32) {
+      if (dweight_dtype == IKRL_DTYPE_BF16 && !use_dw32) {
         p.out_bf16 = reinterpret_cast<uint16_t*>(dweight); p.ld_bf16 = H;
         if ((rc = launch_k1<EPI_STORE_BF16, true, true>(ta, tb, ta, tb, p, v_tiles, 0, s))) return rc;
       } else {
@@ -1144,6 +1333,23 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
         if ((rc = launch_k1<EPI_F32, true, true>(ta, tb, ta, tb, p, v_tiles, 0, s))) return rc;
       }
     }
+    // 3) dH[chunk] = dS W
+    if (dhidden) {
+      CUtensorMap ta;
+      if ((rc = make_tmap(&ta, dS, V, rows, L.lds, BM, "dS"))) return rc;
+      GemmParams p{};
+      p.M = (int)rows; p.N = H; p.K = V;
+      p.out_bf16 = dh_out + c0 * H; p.ld_bf16 = H;
+      p.err = err;
+      if ((rc = launch_k1<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, 0, s))) return rc;
+    }
+  }
+  if (pos != nullptr) {
+    const int vpr = H / 8;
+    const int gb = (int)std::min<int64_t>(cdiv64(N * vpr, 256), 148ll * 16);
+    scatter_rows_kernel<<<gb, 256, 0, s>>>(reinterpret_cast<const uint4*>(dh_out), pos, N, vpr,
+                                           reinterpret_cast<uint4*>(dhidden));
+    if ((rc = check_launch("scatter_rows_kernel"))) return rc;
   }
   return IKRL_OK;
 }

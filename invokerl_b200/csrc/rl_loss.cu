@@ -10,6 +10,7 @@
 // d loss / d new_lp, and the metrics come out of a fixed-order (reproducible) reduction in the
 // same launch; the host reads them with a single copy.
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace ikrl {
 namespace {
@@ -403,6 +404,58 @@ __device__ __forceinline__ void ld4(const float* p, int64_t q, float (&x)[4]) {
   x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
 }
 
+// Per-block sums -> partials; the last block to finish reduces them in a fixed order and adds the
+// batch-level terms.
+__device__ __forceinline__ void finish_loss_sums(const LossArgs& a, double (&v)[kTokenSums], double* scratch,
+                                                 bool* am_last, bool derive_token_loss) {
+  block_sum<double, kTokenSums>(v, scratch);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < kTokenSums; ++i) a.partials[(int64_t)blockIdx.x * IKRL_LOSS_NSUMS + i] = v[i];
+    __threadfence();
+    *am_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (*am_last) {
+    __threadfence();
+    // Fixed-order reduction of the per-block partials by the whole block: thread i takes blocks
+    // i, i + blockDim, ... in order, then the block tree combines the threads.
+    double t[kTokenSums];
+#pragma unroll
+    for (int i = 0; i < kTokenSums; ++i) t[i] = 0.0;
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+#pragma unroll
+      for (int i = 0; i < kTokenSums; ++i) t[i] += __ldcg(a.partials + (int64_t)b * IKRL_LOSS_NSUMS + i);
+    }
+    block_sum<double, kTokenSums>(t, scratch);
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int i = 0; i < kTokenSums; ++i) a.sums[i] = t[i];
+      // GRPO token loss sum(pl*m) + beta*sum(kl*m), when the per-token pass left it out.
+      if (derive_token_loss) a.sums[8] = t[0] + (double)a.p.beta * t[1];
+    }
+    // Batch-level terms: rewards.mean() and the zero-variance group count (dapo.py:132-135).
+    double r[2] = {0.0, 0.0};
+    for (int b = threadIdx.x; b < a.B; b += blockDim.x) r[0] += a.rewards[b];
+    if (a.G > 0) {
+      for (int g = threadIdx.x; g < a.B / a.G; g += blockDim.x) {
+        double mean, sd;
+        group_stats(a.rewards + g * a.G, a.G, mean, sd);
+        if ((float)sd < 1e-8f) r[1] += 1.0;
+      }
+    }
+    block_sum<double, 2>(r, scratch);
+    if (threadIdx.x == 0) {
+      a.sums[9] = r[0];
+      a.sums[10] = (double)a.B;
+      a.sums[11] = r[1];
+      a.sums[12] = a.G > 0 ? (double)(a.B / a.G) : 0.0;
+      a.sums[13] = a.sums[14] = a.sums[15] = 0.0;
+      *a.ticket = 0;
+    }
+  }
+}
+
 // VEC: four tokens per thread per step with 16-byte loads (n % 4 == 0, aligned pointers).
 template <int FAMILY, bool BF16, bool VEC>
 __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kernel(LossArgs a) {
@@ -473,50 +526,236 @@ __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kern
   double v[kTokenSums];
 #pragma unroll
   for (int i = 0; i < kTokenSums; ++i) v[i] = (double)acc[i];
-  block_sum<double, kTokenSums>(v, scratch);
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int i = 0; i < kTokenSums; ++i) a.partials[(int64_t)blockIdx.x * IKRL_LOSS_NSUMS + i] = v[i];
-    __threadfence();
-    am_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  finish_loss_sums(a, v, scratch, &am_last, false);
+}
+
+// Masked sums of the lean GRPO / DAPO pass (grpo.py:103-140): policy loss, KL, clip count,
+// (lp - old)^2, advantages of masked tokens, token count, lp.
+struct GrpoSums {
+  float pl = 0.f, kl = 0.f, clip = 0.f, lr2 = 0.f, adv = 0.f, m = 0.f, lp = 0.f;
+};
+
+// One token of GRPO / DAPO: accumulates the masked sums and returns d loss / d lp.
+// KL: 0 none, 1 k3 (schulman), 2 k1 (simple).
+template <int KL>
+__device__ __forceinline__ float grpo_token(float x, float o, float r, float A, bool mk, float inv_n, float lo,
+                                            float hi, float ceps, float beta, GrpoSums& acc) {
+  const float m = mk ? 1.f : 0.f;
+  const float lr = x - o;
+  // ratio = e^lr as 2^(lr * log2 e) on the MUFU unit: a few ulp, well inside the 1e-4 parity bound.
+  const float rho = fast_exp2(lr * kLog2e);
+  const float s1 = rho * A;
+  const float s2 = torch_clamp(rho, lo, hi) * A;
+  float mn, w1, w2;
+  torch_min2(s1, s2, mn, w1, w2);
+  const float inb = (rho >= lo && rho <= hi) ? 1.f : 0.f;
+  const float dpl = -((w1 * A + w2 * (A * inb)) * rho);
+  float kl = 0.f, dkl = 0.f;
+  if constexpr (KL == 1) {
+    const float lrr = r - x;
+    const float e = fast_exp2(lrr * kLog2e);
+    kl = e - lrr - 1.f;
+    dkl = 1.f - e;
+  } else if constexpr (KL == 2) {
+    kl = -(r - x);
+    dkl = 1.f;
   }
-  __syncthreads();
-  if (am_last) {
-    __threadfence();
-    // Fixed-order reduction of the per-block partials by the whole block: thread i takes blocks
-    // i, i + blockDim, ... in order, then the block tree combines the threads.
-    double t[kTokenSums];
+  const float g = m * inv_n;
+  acc.pl += (-mn) * m;
+  acc.kl += kl * m;
+  acc.clip += (fabsf(rho - 1.f) > ceps ? 1.f : 0.f) * m;
+  acc.lr2 += (lr * lr) * m;
+  if (mk) acc.adv += A;
+  acc.m += m;
+  acc.lp += x * m;
+  return g * dpl + (g * beta) * dkl;
+}
+
+__device__ __forceinline__ void grpo_finish(const LossArgs& a, const GrpoSums& acc, double* scratch, bool* am_last,
+                                            bool aborted = false) {
+  double v[kTokenSums] = {(double)acc.pl, (double)acc.kl, (double)acc.clip, 0.5 * (double)acc.lr2, (double)acc.adv,
+                          (double)acc.m, (double)acc.lp, 0.0, 0.0};
+  if (aborted) v[0] = __longlong_as_double(0x7ff8000000000000ll);  // a gave-up wait poisons the loss
+  finish_loss_sums(a, v, scratch, am_last, true);
+}
+
+// GRPO / DAPO with no value head and no whitening (grpo.py:84-143, dapo.py:90-150): four tokens
+// per thread per step on 16-byte loads, KL form fixed at compile time, and only the sums those
+// losses report.  The token loss sum(pl*m) + beta*sum(kl*m) is formed from its two parts after
+// the reduction instead of per token.
+template <bool BF16, int KL>
+__global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) grpo_loss_kernel(LossArgs a) {
+  __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
+  __shared__ bool am_last;
+  GrpoSums acc;
+  const float inv_n = 1.f / fmaxf((float)(*a.ntok), 1.f);
+  const float lo = a.p.ratio_lo, hi = a.p.ratio_hi, ceps = a.p.clip_metric_eps, beta = a.p.beta;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nq = a.n >> 2;
+  for (int64_t q0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q0 < nq; q0 += stride * kLossUnroll) {
+    float lp[kLossUnroll][4], old[kLossUnroll][4], ref[kLossUnroll][4], adv[kLossUnroll][4];
+    uint32_t mw[kLossUnroll];
 #pragma unroll
-    for (int i = 0; i < kTokenSums; ++i) t[i] = 0.0;
-    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
-#pragma unroll
-      for (int i = 0; i < kTokenSums; ++i) t[i] += __ldcg(a.partials + (int64_t)b * IKRL_LOSS_NSUMS + i);
-    }
-    block_sum<double, kTokenSums>(t, scratch);
-    if (threadIdx.x == 0) {
-#pragma unroll
-      for (int i = 0; i < kTokenSums; ++i) a.sums[i] = t[i];
-    }
-    // Batch-level terms: rewards.mean() and the zero-variance group count (dapo.py:132-135).
-    double r[2] = {0.0, 0.0};
-    for (int b = threadIdx.x; b < a.B; b += blockDim.x) r[0] += a.rewards[b];
-    if (a.G > 0) {
-      for (int g = threadIdx.x; g < a.B / a.G; g += blockDim.x) {
-        double mean, sd;
-        group_stats(a.rewards + g * a.G, a.G, mean, sd);
-        if ((float)sd < 1e-8f) r[1] += 1.0;
+    for (int u = 0; u < kLossUnroll; ++u) {
+      const int64_t q = q0 + u * stride;
+      if (q < nq) {
+        load_lp4<BF16>(a.new_lp, q, lp[u]);
+        ld4(a.old_lp, q, old[u]);
+        if constexpr (KL != 0) ld4(a.ref_lp, q, ref[u]);
+        ld4(a.adv, q, adv[u]);
+        mw[u] = __ldg(reinterpret_cast<const uint32_t*>(a.mask) + q);
       }
     }
-    block_sum<double, 2>(r, scratch);
-    if (threadIdx.x == 0) {
-      a.sums[9] = r[0];
-      a.sums[10] = (double)a.B;
-      a.sums[11] = r[1];
-      a.sums[12] = a.G > 0 ? (double)(a.B / a.G) : 0.0;
-      a.sums[13] = a.sums[14] = a.sums[15] = 0.0;
-      *a.ticket = 0;
+#pragma unroll
+    for (int u = 0; u < kLossUnroll; ++u) {
+      const int64_t q = q0 + u * stride;
+      if (q >= nq) break;
+      float d[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        d[j] = grpo_token<KL>(lp[u][j], old[u][j], KL != 0 ? ref[u][j] : 0.f, adv[u][j],
+                              ((mw[u] >> (8 * j)) & 0xffu) != 0u, inv_n, lo, hi, ceps, beta, acc);
+      if (a.dlp) store_lp4<BF16>(a.dlp, q, d);
     }
   }
+  grpo_finish(a, acc, scratch, &am_last);
+}
+
+// The same pass with the inputs staged through shared memory by bulk copies (cp.async.bulk,
+// completion on an mbarrier): one producer thread keeps kBulkStages tiles of 1024 tokens per
+// block in flight, independent of the registers of the 256 consumer threads, which read their
+// four tokens of a tile from shared memory.  Tiles are dealt to the blocks round-robin; the one
+// partial tile at the end (n % 1024 tokens) is read directly from global memory.
+using namespace sm100;
+
+constexpr int kBulkTile = 1024;
+constexpr int kBulkStages = 4;
+constexpr int kBulkConsumers = 256;
+constexpr int kBulkThreads = kBulkConsumers + 32;
+constexpr int kBulkBlocksPerSM = 2;
+
+template <bool BF16>
+constexpr uint32_t bulk_stage_bytes() {
+  return kBulkTile * ((BF16 ? 2 : 4) + 4 + 4 + 4 + 1);
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+template <bool BF16, int KL>
+__global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk_kernel(LossArgs a) {
+  extern __shared__ __align__(128) uint8_t bulk_smem[];
+  __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
+  __shared__ bool am_last;
+  __shared__ __align__(8) uint64_t full_bar[kBulkStages], empty_bar[kBulkStages];
+  __shared__ int abort_flag;
+  constexpr uint32_t kLpBytes = kBulkTile * (BF16 ? 2 : 4);
+  constexpr uint32_t kOffOld = kLpBytes, kOffRef = kOffOld + 4 * kBulkTile, kOffAdv = kOffRef + 4 * kBulkTile,
+                     kOffMask = kOffAdv + 4 * kBulkTile;
+  constexpr uint32_t kStage = bulk_stage_bytes<BF16>();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n_full = a.n / kBulkTile;
+  const int64_t n_tiles = (a.n + kBulkTile - 1) / kBulkTile;
+  volatile int* abort_v = &abort_flag;
+  int* err = reinterpret_cast<int*>(a.ticket) + 1;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kBulkStages; ++st) {
+      mbar_init(smem_u32(&full_bar[st]), 1);
+      mbar_init(smem_u32(&empty_bar[st]), kBulkConsumers / 32);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t sbase = smem_u32(bulk_smem);
+  GrpoSums acc;
+
+  if (warp == kBulkConsumers / 32) {
+    // ---- producer ----
+    if (lane == 0) {
+      int i = 0;
+      for (int64_t t = blockIdx.x; t < n_full; t += gridDim.x, ++i) {
+        const int st = i % kBulkStages;
+        const uint32_t ph = (uint32_t)(i / kBulkStages) & 1u;
+        if (!mbar_wait(smem_u32(&empty_bar[st]), ph ^ 1u, abort_v, err, kErrTimeoutProducer)) break;
+        const uint32_t fb = smem_u32(&full_bar[st]);
+        const uint32_t dst = sbase + st * kStage;
+        const int64_t t0 = t * kBulkTile;
+        mbar_arrive_expect_tx(fb, KL != 0 ? kStage : kStage - 4 * kBulkTile);
+        bulk_g2s(dst, reinterpret_cast<const uint8_t*>(a.new_lp) + t0 * (BF16 ? 2 : 4), kLpBytes, fb);
+        bulk_g2s(dst + kOffOld, a.old_lp + t0, 4 * kBulkTile, fb);
+        if constexpr (KL != 0) bulk_g2s(dst + kOffRef, a.ref_lp + t0, 4 * kBulkTile, fb);
+        bulk_g2s(dst + kOffAdv, a.adv + t0, 4 * kBulkTile, fb);
+        bulk_g2s(dst + kOffMask, a.mask + t0, kBulkTile, fb);
+      }
+      // Copies still in flight after a gave-up wait land before the block leaves.
+      if (*abort_v) {
+        const int issued = i;
+        for (int j = 0; j < kBulkStages && j < issued; ++j) {
+          const int k = issued - 1 - j;
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(smem_u32(&full_bar[k % kBulkStages]), (uint32_t)(k / kBulkStages) & 1u)) {
+            if (globaltimer() - t0 > kWaitTimeoutNs / 4) break;
+          }
+        }
+      }
+    }
+  } else {
+    // ---- consumers: four tokens each per tile ----
+    const float inv_n = 1.f / fmaxf((float)(*a.ntok), 1.f);
+    const float lo = a.p.ratio_lo, hi = a.p.ratio_hi, ceps = a.p.clip_metric_eps, beta = a.p.beta;
+    int i = 0;
+    for (int64_t t = blockIdx.x; t < n_full; t += gridDim.x, ++i) {
+      const int st = i % kBulkStages;
+      const uint32_t ph = (uint32_t)(i / kBulkStages) & 1u;
+      if (!mbar_wait(smem_u32(&full_bar[st]), ph, abort_v, err, kErrTimeoutEpilogue)) break;
+      const uint8_t* sp = bulk_smem + st * kStage;
+      float x[4], o[4], r[4] = {0.f, 0.f, 0.f, 0.f}, A[4];
+      if constexpr (BF16) {
+        const uint2 w = reinterpret_cast<const uint2*>(sp)[threadIdx.x];
+        x[0] = bf16lo(w.x); x[1] = bf16hi(w.x); x[2] = bf16lo(w.y); x[3] = bf16hi(w.y);
+      } else {
+        const float4 v = reinterpret_cast<const float4*>(sp)[threadIdx.x];
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+      }
+      {
+        const float4 v = reinterpret_cast<const float4*>(sp + kOffOld)[threadIdx.x];
+        o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+      }
+      if constexpr (KL != 0) {
+        const float4 v = reinterpret_cast<const float4*>(sp + kOffRef)[threadIdx.x];
+        r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+      }
+      {
+        const float4 v = reinterpret_cast<const float4*>(sp + kOffAdv)[threadIdx.x];
+        A[0] = v.x; A[1] = v.y; A[2] = v.z; A[3] = v.w;
+      }
+      const uint32_t mw = reinterpret_cast<const uint32_t*>(sp + kOffMask)[threadIdx.x];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty_bar[st]));  // the tile's smem may be refilled
+      float d[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        d[j] = grpo_token<KL>(x[j], o[j], r[j], A[j], ((mw >> (8 * j)) & 0xffu) != 0u, inv_n, lo, hi, ceps, beta,
+                              acc);
+      if (a.dlp) store_lp4<BF16>(a.dlp, t * (kBulkTile / 4) + threadIdx.x, d);
+    }
+    // the partial tile, if any, goes to the block that would have been dealt it
+    if (n_tiles > n_full && (n_full % gridDim.x) == blockIdx.x && !*abort_v) {
+      for (int64_t k = n_full * kBulkTile + threadIdx.x; k < a.n; k += kBulkConsumers) {
+        const float x = load_lp<BF16>(a.new_lp, k);
+        const float d = grpo_token<KL>(x, a.old_lp[k], KL != 0 ? a.ref_lp[k] : 0.f, a.adv[k], a.mask[k] != 0, inv_n,
+                                       lo, hi, ceps, beta, acc);
+        if (a.dlp) store_lp<BF16>(a.dlp, k, d);
+      }
+    }
+  }
+  __syncthreads();
+  grpo_finish(a, acc, scratch, &am_last, *abort_v != 0);
 }
 
 __global__ void clip_loss_finalize_kernel(const double* __restrict__ s, const int64_t* __restrict__ ntok,
@@ -711,6 +950,14 @@ __global__ void dpo_pairs_kernel(const float* __restrict__ lr, const float* __re
   }
 }
 
+// GRPO / DAPO loss kernel: 2 bulk-copy staged, 1 (default) register loads, 0 the general
+// clipped-ratio kernel (INVOKERL_B200_LEAN_LOSS; kept for A/B timing).
+int lean_loss_mode() {
+  const char* e = getenv("INVOKERL_B200_LEAN_LOSS");
+  if (e != nullptr && e[0] >= '0' && e[0] <= '2') return e[0] - '0';
+  return 1;
+}
+
 int loss_grid(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(cdiv(n, 4), kLossThreads), kLossMaxBlocks)); }
 
 }  // namespace
@@ -844,13 +1091,39 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
   a.ticket = reinterpret_cast<unsigned*>(ws);
   a.partials = reinterpret_cast<double*>(reinterpret_cast<char*>(ws) + 256);
   a.sums = sums_out; a.n = n; a.p = *params;
-  IKRL_CUDA(cudaMemsetAsync(a.ticket, 0, sizeof(unsigned), s));
+  IKRL_CUDA(cudaMemsetAsync(a.ticket, 0, 2 * sizeof(unsigned), s));  // ticket and the bulk kernel's error word
   const int grid = loss_grid(n);
   const bool bf = lp_dtype == IKRL_DTYPE_BF16;
   auto al = [](const void* p, uintptr_t m) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
   const bool vec = (n % 4 == 0) && al(new_lp, bf ? 8 : 16) && al(old_lp, 16) && al(ref_lp, 16) && al(adv, 16) &&
                    al(mask, 4) && al(values, 16) && al(old_values, 16) && al(dlp_out, bf ? 8 : 16) &&
                    al(dvalues_out, 16);
+  const bool has_kl = ref_lp != nullptr && params->kl_type != IKRL_KL_NONE;
+  const int lean = lean_loss_mode();
+  if (vec && params->family == IKRL_LOSS_GRPO && values == nullptr && whiten == nullptr && lean != 0) {
+    const int kl = !has_kl ? 0 : params->kl_type == IKRL_KL_SCHULMAN ? 1 : 2;
+    const bool bulk_ok = lean == 2 && n >= kBulkTile && al(new_lp, 16) && al(old_lp, 16) && al(ref_lp, 16) &&
+                         al(adv, 16) && al(mask, 16);
+    if (bulk_ok) {
+      const int bgrid = (int)std::min<int64_t>(cdiv(n, kBulkTile), (int64_t)kNumSMs * kBulkBlocksPerSM);
+      const uint32_t smem = kBulkStages * (bf ? bulk_stage_bytes<true>() : bulk_stage_bytes<false>());
+#define IKRL_LAUNCH_BULK(BF, KLV)                                                                      \
+  do {                                                                                                \
+    IKRL_CUDA(cudaFuncSetAttribute(grpo_loss_bulk_kernel<BF, KLV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)smem));                                                       \
+    grpo_loss_bulk_kernel<BF, KLV><<<bgrid, kBulkThreads, smem, s>>>(a);                              \
+  } while (0)
+      if (bf) { if (kl == 0) IKRL_LAUNCH_BULK(true, 0); else if (kl == 1) IKRL_LAUNCH_BULK(true, 1); else IKRL_LAUNCH_BULK(true, 2); }
+      else { if (kl == 0) IKRL_LAUNCH_BULK(false, 0); else if (kl == 1) IKRL_LAUNCH_BULK(false, 1); else IKRL_LAUNCH_BULK(false, 2); }
+#undef IKRL_LAUNCH_BULK
+      return check_launch("grpo_loss_bulk_kernel");
+    }
+#define IKRL_LAUNCH_LEAN(BF, KLV) grpo_loss_kernel<BF, KLV><<<grid, kLossThreads, 0, s>>>(a)
+    if (bf) { if (kl == 0) IKRL_LAUNCH_LEAN(true, 0); else if (kl == 1) IKRL_LAUNCH_LEAN(true, 1); else IKRL_LAUNCH_LEAN(true, 2); }
+    else { if (kl == 0) IKRL_LAUNCH_LEAN(false, 0); else if (kl == 1) IKRL_LAUNCH_LEAN(false, 1); else IKRL_LAUNCH_LEAN(false, 2); }
+#undef IKRL_LAUNCH_LEAN
+    return check_launch("grpo_loss_kernel");
+  }
 #define IKRL_LAUNCH_LOSS(FAM, BF, VEC) clip_loss_kernel<FAM, BF, VEC><<<grid, kLossThreads, 0, s>>>(a)
   if (params->family == IKRL_LOSS_GRPO) {
     if (bf) { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, true, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, true, false); }

@@ -145,3 +145,63 @@ def test_full_size_properties(N, H, kernel_variant):
     assert rel_fro(dw[vs.to(DEV)], dw_sub) <= 1e-2
     colsum = dw.sum(dim=0)
     assert float(colsum.norm() / dw.norm()) <= 1e-2
+
+
+def _bwd(h, w, t, lse, g, skip: bool, **kw):
+    import os
+
+    prev = os.environ.get("INVOKERL_B200_SKIP_ZERO_ROWS")
+    os.environ["INVOKERL_B200_SKIP_ZERO_ROWS"] = "1" if skip else "0"
+    try:
+        out = ops.lmhead_backward_raw(h, w, t, lse, g, **kw)
+        torch.cuda.synchronize()
+        return out
+    finally:
+        if prev is None:
+            del os.environ["INVOKERL_B200_SKIP_ZERO_ROWS"]
+        else:
+            os.environ["INVOKERL_B200_SKIP_ZERO_ROWS"] = prev
+
+
+@pytest.mark.parametrize("N,H,V,chunk,frac", [
+    (1000, 256, 33000, 256, 0.4),      # several chunks of compacted rows
+    (700, 4096, 151936, None, 0.5),    # Qwen3-8B head shape, one chunk
+    (2500, 64, 5000, 512, 0.02),       # very few active rows (fewer than one chunk)
+])
+def test_zero_gradient_rows_are_skipped_exactly(N, H, V, chunk, frac, kernel_variant):
+    """Rows with zero upstream gradient (masked tokens) and ignore_index rows are left out of the
+    backward GEMMs: dH is identical to the dense computation, dW equal up to fp32 summation order."""
+    li = lmhead_inputs(N, H, V, seed=N + V, w_std=0.05 if H > 512 else 0.3)
+    gen = torch.Generator().manual_seed(9)
+    g = torch.randn(N, generator=gen) * torch.bernoulli(torch.full((N,), frac), generator=gen)
+    t = li.targets.clone()
+    t[torch.bernoulli(torch.full((N,), 0.05), generator=gen).bool()] = -100
+    hd, wd, td, gd = li.hidden.to(DEV), li.weight.to(DEV), t.to(DEV), g.to(DEV)
+    _, lse = ops.lmhead_forward_raw(hd, wd, td)
+    dh_s, dw_s = _bwd(hd, wd, td, lse, gd, True, dw_dtype=torch.float32, chunk_rows=chunk)
+    dh_d, dw_d = _bwd(hd, wd, td, lse, gd, False, dw_dtype=torch.float32, chunk_rows=chunk)
+    assert torch.equal(dh_s, dh_d)
+    torch.testing.assert_close(dw_s, dw_d, rtol=1e-4, atol=1e-6)
+    dead = (g == 0) | (t == -100)
+    assert float(dh_s.cpu()[dead].abs().max()) == 0.0
+    keep = t != -100
+    _, dh_o, dw_o = oracle.lmhead_logprob_grads(li.hidden[keep], li.weight, t[keep], g[keep])
+    assert rel_fro(dh_s.cpu()[keep], dh_o) <= 1e-2
+    assert rel_fro(dw_s.cpu(), dw_o) <= 1e-2
+    # bf16 dW through the fp32 workspace when the compacted rows span several chunks
+    _, dw_b = _bwd(hd, wd, td, lse, gd, True, want_dh=False, dw_dtype=torch.bfloat16, chunk_rows=chunk)
+    assert rel_fro(dw_b.cpu(), dw_o) <= 1e-2
+
+
+def test_all_rows_zero_gradient():
+    N, H, V = 300, 128, 3000
+    li = lmhead_inputs(N, H, V, seed=11, w_std=0.3)
+    hd, wd, td = li.hidden.to(DEV), li.weight.to(DEV), li.targets.to(DEV)
+    _, lse = ops.lmhead_forward_raw(hd, wd, td)
+    g = torch.zeros(N, device=DEV)
+    dh, dw = _bwd(hd, wd, td, lse, g, True, dw_dtype=torch.bfloat16)
+    assert float(dh.abs().max()) == 0.0 and float(dw.abs().max()) == 0.0
+    base = torch.randn(V, H, device=DEV)
+    acc = base.clone()
+    _bwd(hd, wd, td, lse, g, True, want_dh=False, dweight_out=acc)
+    assert torch.equal(acc, base)

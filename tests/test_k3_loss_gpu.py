@@ -129,3 +129,26 @@ def test_group_size_one_gives_nan_like_torch_std():
     m = torch.ones(3, 4, dtype=torch.bool, device=DEV)
     adv = ops.group_advantages(r, m, 1)
     assert torch.isnan(adv).all()
+
+
+@pytest.mark.parametrize("lean", ["2", "1", "0"])
+@pytest.mark.parametrize("kl_type,lp_dtype", [("schulman", torch.float32), ("simple", torch.float32),
+                                             ("schulman", torch.bfloat16)])
+def test_grpo_kernel_variants_agree_with_oracle(lean, kl_type, lp_dtype, monkeypatch):
+    """The three GRPO loss kernels (bulk-copy staged, register loads, general clipped-ratio) on a
+    batch of 23 full 1024-token tiles plus a 448-token partial tile."""
+    monkeypatch.setenv("INVOKERL_B200_LEAN_LOSS", lean)
+    b = rollout_batch(6, 4, 1000, prompt_len=(16, 200), completion_len=(100, 800), seed=77,
+                      lp_dtype=lp_dtype)
+    nl = b.extras["new_log_probs"]
+    adv_o = oracle.group_advantages(b.rewards, b.response_mask, 4)
+    loss_o, met_o, g_o = oracle.clip_ratio_loss(nl.float(), b.old_log_probs, b.ref_log_probs, adv_o,
+                                                b.response_mask, b.rewards, kl_type=kl_type)
+    bd = make_batch(vars(b), DEV)
+    adv, loss, metrics, grad = run(GRPO(kl_type=kl_type), bd, nl.to(DEV))
+    assert abs(float(loss) - float(loss_o)) <= 1e-4 * abs(float(loss_o)) + 1e-6
+    for k in ("kl", "policy_loss", "clip_frac", "approx_kl", "advantages_mean", "reward"):
+        assert abs(metrics[k] - met_o[k]) <= 1e-4 * abs(met_o[k]) + 1e-6, k
+    bf = lp_dtype == torch.bfloat16
+    torch.testing.assert_close(grad.cpu().float(), g_o.to(lp_dtype).float(), rtol=1e-2 if bf else 1e-4,
+                               atol=1e-6 if bf else 1e-8)
