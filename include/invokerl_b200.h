@@ -257,6 +257,21 @@ IKRL_API int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* wei
  * environment variable INVOKERL_B200_CTA_PAIRS=0 sets the initial choice. */
 IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
 
+/* ---- rollout packing ------------------------------------------------------------------------ */
+
+/* Pads B variable-length rollouts into [B, T] tensors; replaces the per-row host loop of
+ * invokerl/generator.py:414-455 (`VLLMGenerator._pack_output`).  Row b's token ids are
+ * ids_flat[id_offsets[b] .. id_offsets[b+1]) and its log-probs lps_flat[lp_offsets[b] ..
+ * lp_offsets[b+1]) (device CSR arrays, offsets int64 [B+1]).  Writes token_ids int64 (pad_id
+ * after the sequence), log_probs fp32 (0 after the row's list), prompt_mask [0, prompt_len),
+ * response_mask [prompt_len, prompt_len + completion_len) and attention_mask [0, seq_len) as
+ * bytes; lengths past T are clipped like Python slices.  B <= 65535. */
+IKRL_API int ikrl_pack_rollouts(const int64_t* ids_flat, const int64_t* id_offsets, const float* lps_flat,
+                                const int64_t* lp_offsets, const int32_t* prompt_lens,
+                                const int32_t* completion_lens, int32_t B, int32_t T, int64_t pad_id,
+                                int64_t* token_ids, float* log_probs, uint8_t* prompt_mask,
+                                uint8_t* response_mask, uint8_t* attention_mask, void* stream);
+
 /* Device status word of the last K1 call that used workspace `ws` (synchronises `stream`):
  * IKRL_OK, or IKRL_ERR_DEVICE with *status_out = the recorded code (a bounded wait expired). */
 IKRL_API int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream);

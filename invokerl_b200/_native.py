@@ -124,6 +124,10 @@ _SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_P, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P],
     ),
+    "ikrl_pack_rollouts": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _P, _P, c_int32, c_int32, c_int64, _P, _P, _P, _P, _P, _P],
+    ),
 }
 
 _lock = threading.Lock()

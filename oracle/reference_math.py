@@ -21,6 +21,7 @@ __all__ = [
     "clip_ratio_loss",
     "simpo_loss",
     "dpo_loss",
+    "pack_rollouts",
 ]
 
 
@@ -249,3 +250,29 @@ def dpo_loss(new_lp, ref_lp, mask, rewards, beta=0.1, label_smoothing=0.0, chose
         )
     loss.backward()
     return loss.detach(), metrics, lp.grad.to(new_lp.dtype)
+
+
+# ---- rollout packing: invokerl/generator.py ------------------------------------------------------
+
+
+def pack_rollouts(all_ids, all_lps, prompt_lens, completion_lens, pad_id):
+    """Padded [B, T] token ids, log-probs and prompt / response / attention masks of ragged
+    rollouts, T = the longest sequence (generator.py:414-455, `_pack_output`)."""
+    B = len(all_ids)
+    T = max((len(x) for x in all_ids), default=0)
+    token_ids = torch.full((B, T), pad_id, dtype=torch.long)
+    log_probs = torch.zeros(B, T, dtype=torch.float32)
+    prompt_mask = torch.zeros(B, T, dtype=torch.bool)
+    response_mask = torch.zeros(B, T, dtype=torch.bool)
+    attention_mask = torch.zeros(B, T, dtype=torch.bool)
+    for i in range(B):
+        n = len(all_ids[i])
+        token_ids[i, :n] = torch.tensor(all_ids[i], dtype=torch.long)
+        m = min(len(all_lps[i]), T)
+        log_probs[i, :m] = torch.tensor(all_lps[i][:m], dtype=torch.float32)
+        p, c = prompt_lens[i], completion_lens[i]
+        prompt_mask[i, :p] = True
+        response_mask[i, p:p + c] = True
+        attention_mask[i, :n] = True
+    return dict(token_ids=token_ids, log_probs=log_probs, prompt_mask=prompt_mask, response_mask=response_mask,
+                attention_mask=attention_mask)

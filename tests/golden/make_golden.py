@@ -225,7 +225,39 @@ def policy_forward_case() -> None:
          attention_mask=am, lp=lp)
 
 
+def rollout_pack_case() -> None:
+    # VLLMGenerator._pack_output (generator.py:414-455) on ragged sequences: prompt + completion
+    # token ids, log-probs 0 on the prompt, one log-prob list shorter than its sequence.
+    from invokerl.generator import VLLMGenerator
+
+    class _Tok:
+        pad_token_id = 151643
+
+    gen = VLLMGenerator.__new__(VLLMGenerator)
+    gen.tokenizer = _Tok()
+    g = torch.Generator().manual_seed(21)
+    all_ids, all_lps, pls, cls, texts = [], [], [], [], []
+    for i in range(7):
+        p = int(torch.randint(1, 40, (1,), generator=g))
+        c = int(torch.randint(0, 60, (1,), generator=g))
+        ids = torch.randint(0, 151936, (p + c,), generator=g).tolist()
+        lps = [0.0] * p + (-torch.empty(c).exponential_(1.0, generator=g)).tolist()
+        if i == 3:
+            lps = lps[: max(0, len(lps) - 5)]
+        all_ids.append(ids)
+        all_lps.append(lps)
+        pls.append(p)
+        cls.append(c)
+        texts.append(f"completion {i}")
+    out = gen._pack_output(all_ids, all_lps, pls, cls, texts)
+    save("rollout_pack", all_ids=all_ids, all_lps=all_lps, prompt_lens=pls, completion_lens=cls, texts=texts,
+         pad_id=_Tok.pad_token_id, token_ids=out.token_ids, log_probs=out.log_probs, prompt_mask=out.prompt_mask,
+         response_mask=out.response_mask, attention_mask=out.attention_mask)
+
+
+CASES = {"algo": algo_cases, "logprob": logprob_cases, "policy": policy_forward_case, "rollout": rollout_pack_case}
+
 if __name__ == "__main__":
-    algo_cases()
-    logprob_cases()
-    policy_forward_case()
+    # no arguments: every case; otherwise the named groups
+    for name in sys.argv[1:] or list(CASES):
+        CASES[name]()

@@ -93,3 +93,11 @@ def test_oracle_matches_reference_chunked_branch():
     li = lmhead_inputs(B * T, H, V, seed=g["seed"], w_std=g["w_std"])
     lp = oracle.lmhead_logprob(li.hidden, li.weight, li.targets).reshape(B, T)
     torch.testing.assert_close(lp, g["lp_fp32"], rtol=0, atol=2e-4)
+
+
+def test_oracle_matches_reference_rollout_packing():
+    g = load("rollout_pack")
+    out = oracle.pack_rollouts(g["all_ids"], g["all_lps"], g["prompt_lens"], g["completion_lens"], g["pad_id"])
+    for k in ("token_ids", "log_probs", "prompt_mask", "response_mask", "attention_mask"):
+        assert out[k].dtype == g[k].dtype, k
+        assert torch.equal(out[k], g[k]), k
