@@ -257,6 +257,31 @@ IKRL_API int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* wei
  * environment variable INVOKERL_B200_CTA_PAIRS=0 sets the initial choice. */
 IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
 
+/* ---- vocab-parallel LM head ---------------------------------------------------------------- */
+/* The LM head with W split along the vocabulary over P ranks (rows replicated), the optional
+ * tensor-parallel layout of the hot path.  No counterpart in the reference, which keeps the whole
+ * W on every rank; the results equal ikrl_lmhead_logprob_fwd/_bwd on the whole W.
+ *
+ * Forward on one rank: weight_shard holds vocabulary rows [vocab_start, vocab_start + V_shard).
+ * Writes lse_shard[N] = logsumexp over the shard and tlogit[N] = the raw logit of ids[r] when the
+ * id falls in the shard, -inf otherwise.  Workspace: ikrl_lmhead_fwd_workspace_bytes(N, H,
+ * V_shard).  The caller gathers every rank's [tlogit; lse_shard] ([2, N] fp32, rank-major
+ * [P, 2, N]) and calls ikrl_vocab_parallel_combine for logp[N] and the global lse[N]. */
+IKRL_API int ikrl_lmhead_shard_fwd(const void* hidden, const void* weight_shard, const int64_t* ids, int64_t N,
+                                   int32_t H, int32_t V_shard, int64_t vocab_start, float* tlogit, float* lse_shard,
+                                   void* ws, size_t ws_bytes, void* stream);
+IKRL_API int ikrl_vocab_parallel_combine(const float* parts, const int64_t* ids, int64_t N, int32_t P,
+                                         int64_t V_total, float* logp, float* lse, void* stream);
+/* Backward on one rank from the global lse: dweight_shard [V_shard, H] is this rank's slice of
+ * dW (no communication), dhidden_partial [N, H] bf16 this rank's term of dH; the caller sums the
+ * terms over ranks (all-reduce).  Same row skipping, workspace and synchronisation as
+ * ikrl_lmhead_logprob_bwd with V = V_shard. */
+IKRL_API int ikrl_lmhead_shard_bwd(const void* hidden, const void* weight_shard, const int64_t* ids,
+                                   const float* lse, const float* dlogp, int64_t N, int32_t H, int32_t V_shard,
+                                   int64_t vocab_start, int64_t chunk_rows, void* dhidden_partial,
+                                   void* dweight_shard, int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
+                                   size_t ws_bytes, void* stream);
+
 /* ---- rollout packing ------------------------------------------------------------------------ */
 
 /* Pads B variable-length rollouts into [B, T] tensors; replaces the per-row host loop of

@@ -124,6 +124,16 @@ _SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_P, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P],
     ),
+    "ikrl_lmhead_shard_fwd": (
+        ctypes.c_int,
+        [_P, _P, _P, c_int64, c_int32, c_int32, c_int64, _P, _P, _P, c_size_t, _P],
+    ),
+    "ikrl_vocab_parallel_combine": (ctypes.c_int, [_P, _P, c_int64, c_int32, c_int64, _P, _P, _P]),
+    "ikrl_lmhead_shard_bwd": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _P, c_int64, c_int32, c_int32, c_int64, c_int64, _P, _P, c_int32, c_int32, _P, c_size_t,
+         _P],
+    ),
     "ikrl_pack_rollouts": (
         ctypes.c_int,
         [_P, _P, _P, _P, _P, _P, c_int32, c_int32, c_int64, _P, _P, _P, _P, _P, _P],

@@ -69,6 +69,8 @@ struct GemmParams {
   int* err;               // device error word
   int part_sets;          // LSE partial sets written (splits x column halves), set by the launcher
   int a_policy, b_policy; // L2 eviction priority of the A / B loads: 0 normal, 1 evict-last, 2 evict-first
+  unsigned* lockstep;     // [npairs] tiles started per pair (zeroed per launch), or null: no pacing
+  int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
@@ -117,6 +119,9 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       if (tgt == -100) gval = 0.f;  // ignore_index rows have zero gradient
     }
   }
+  // Column index of the target in this W (a vocab shard starts at id_offset); ignore_index rows
+  // keep -100, which matches no column.
+  if (tgt != -100) tgt -= p.id_offset;
   float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
   bool found = false;
   for (int j = 0; j < ntiles; ++j) {
@@ -578,6 +583,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Pacing of the persistent pairs: pairs that read the same W tiles through L2 drift apart over a
+// sweep, and a tile read by a leading pair is evicted before the trailing pairs reach it.  Each
+// pair publishes how many tiles it has started; a pair about to start tile j waits until every
+// unfinished pair has started tile j - kPaceLag.  The wait is a heuristic with a short bound:
+// after kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair
+// that is not resident, e.g. on a shared GPU, must not stall the others).
+constexpr int kPaceLag = 1;
+constexpr uint64_t kPaceBoundNs = 20000;
+constexpr unsigned kPaceDone = 0xffffffffu;
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* ptr) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u32(unsigned* ptr, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// Publish "started tile j" (j counted over all of this pair's units) and wait for the laggards.
+__device__ __forceinline__ void pace_tile(unsigned* prog, int pair_id, int npairs, int j, bool& pacing) {
+  st_relaxed_u32(prog + pair_id, (unsigned)j + 1u);
+  if (!pacing || j < kPaceLag) return;
+  const unsigned need = (unsigned)(j + 1 - kPaceLag);
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    unsigned mn = kPaceDone;
+    for (int q = 0; q < npairs; q += 8) {
+      unsigned v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (q + i < npairs) ? ld_relaxed_u32(prog + q + i) : kPaceDone;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mn = min(mn, v[i]);
+    }
+    if (mn >= need) return;
+    if (globaltimer() - t0 > kPaceBoundNs) {
+      pacing = false;
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 // Wide CTA-pair variant for long K: the pair computes a 256 x 512 tile per K step with two
 // N=256 MMAs into all 512 TMEM columns.  Each CTA stages 128 A rows and 256 of the 512 B rows per
 // 64-deep K block (48 KB, 4 stages), so L2 and shared-memory reads per MMA flop are 3/4 of the
@@ -643,12 +691,15 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool pacing = p.lockstep != nullptr && rank == 0;
+      int jt = 0;
       for (int u = pair_id; u < nunits && ok; u += npairs) {
         const int split = u % p.splits;
         const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
         const int t_begin = split * p.tiles_per_split;
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-        for (int t = t_begin; t < t_end && ok; ++t) {
+        for (int t = t_begin; t < t_end && ok; ++t, ++jt) {
+          if (p.lockstep != nullptr && rank == 0) pace_tile(p.lockstep, pair_id, npairs, jt, pacing);
           for (int kb = 0; kb < nk; ++kb) {
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
               ok = false;
@@ -684,6 +735,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
           }
         }
       }
+      if (p.lockstep != nullptr && rank == 0) st_relaxed_u32(p.lockstep + pair_id, kPaceDone);
       if (ok) {
         for (int s = 0; s < kWideStages; ++s) {
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) break;
@@ -792,6 +844,56 @@ __global__ void lse_combine_kernel(const float* __restrict__ part_m, const float
   if (lse_out) lse_out[r] = bad ? __int_as_float(0x7fc00000) : lse;
 }
 
+// Vocab shard of the forward: the shard's own logsumexp and the raw target logit when the target
+// id falls in this shard (-inf otherwise, so that a max over shards picks the owner's value).
+__global__ void lse_shard_combine_kernel(const float* __restrict__ part_m, const float* __restrict__ part_s,
+                                         const float* __restrict__ part_t, const int64_t* __restrict__ ids, int M,
+                                         int64_t vocab_start, int V_shard, int splits, float* __restrict__ tlogit,
+                                         float* __restrict__ lse_out, const int* __restrict__ err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= M) return;
+  const bool bad = *err != 0;
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, part_m[(int64_t)s * M + r]);
+  float sum = 0.f;
+  for (int s = 0; s < splits; ++s) sum += part_s[(int64_t)s * M + r] * fast_exp2(part_m[(int64_t)s * M + r] - mx);
+  const float nan = __int_as_float(0x7fc00000);
+  lse_out[r] = bad ? nan : (mx + log2f(sum)) * kLn2;
+  const int64_t t = ids[r];
+  const bool owned = t != -100 && t >= vocab_start && t < vocab_start + V_shard;
+  tlogit[r] = bad ? nan : (owned ? part_t[r] : -INFINITY);
+}
+
+// log p = t - logsumexp over shards, from each shard's (target logit or -inf, shard logsumexp):
+// parts[q][0][r], parts[q][1][r] for shards q < P.  Ignored rows give -0.0 and ids outside the
+// vocabulary NaN, as the unsharded forward.
+__global__ void vocab_parallel_combine_kernel(const float* __restrict__ parts, const int64_t* __restrict__ ids,
+                                              int64_t N, int P, int64_t V_total, float* __restrict__ logp,
+                                              float* __restrict__ lse_out) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= N) return;
+  float mx = -INFINITY, t = -INFINITY;
+  bool nan_in = false;
+  for (int q = 0; q < P; ++q) {
+    const float lq = parts[((int64_t)q * 2 + 1) * N + r];
+    const float tq = parts[((int64_t)q * 2) * N + r];
+    nan_in |= (lq != lq) || (tq != tq);
+    mx = fmaxf(mx, lq);
+    t = fmaxf(t, tq);
+  }
+  float sum = 0.f;
+  for (int q = 0; q < P; ++q) sum += expf(parts[((int64_t)q * 2 + 1) * N + r] - mx);
+  const float nan = __int_as_float(0x7fc00000);
+  const float lse = nan_in ? nan : mx + logf(sum);
+  const int64_t id = ids[r];
+  float lp;
+  if (id == -100) lp = -0.f;
+  else if (id < 0 || id >= V_total) lp = nan;
+  else lp = t - lse;
+  logp[r] = lp;
+  if (lse_out) lse_out[r] = lse;
+}
+
 // ---- host side ---------------------------------------------------------------------------------
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -843,8 +945,37 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p,
 }
 
 // Pair launch: a persistent 1-D grid of one CTA pair (cluster of 2) per two SMs.
+// Per-pair tile counters of the pacing in the wide kernel: one array per device, zeroed before
+// every launch that paces (launches on one stream are ordered; concurrent launches on other
+// streams would share it, which only weakens the pacing, whose waits are bounded).
+constexpr int kMaxPacedPairs = 512;
+static __device__ unsigned g_pace[kMaxPacedPairs];
+std::mutex g_pace_mu;
+unsigned* g_pace_addr[64] = {nullptr};
+
+int pace_array(unsigned** out) {
+  int dev = 0;
+  IKRL_CUDA(cudaGetDevice(&dev));
+  IKRL_REQUIRE(dev >= 0 && dev < 64, IKRL_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_pace_mu);
+  if (g_pace_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    IKRL_CUDA(cudaGetSymbolAddress(&ptr, g_pace));
+    g_pace_addr[dev] = reinterpret_cast<unsigned*>(ptr);
+  }
+  *out = g_pace_addr[dev];
+  return IKRL_OK;
+}
+
+// Pacing of the wide kernel's pairs: on unless INVOKERL_B200_PACE=0.
+bool pacing_enabled() {
+  const char* e = getenv("INVOKERL_B200_PACE");
+  return !(e != nullptr && e[0] == '0');
+}
+
 template <int EPI, bool A_MN, bool B_MN, bool WIDE>
-int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int m_tiles, cudaStream_t s) {
+int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p_in, int m_tiles, cudaStream_t s) {
+  GemmParams p = p_in;
   auto kern = WIDE ? lmhead_gemm_wide_kernel<EPI, A_MN, B_MN> : lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
   const uint32_t smem_bytes = WIDE ? kWideSmemBytes : kPairSmemBytes;
   IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
@@ -858,6 +989,12 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   const char* pe = getenv("INVOKERL_B200_PERSISTENT");
   const bool persistent = !(pe != nullptr && pe[0] == '0');
   const int64_t npairs = std::max<int64_t>(1, persistent ? std::min<int64_t>(nunits, nsm / 2) : nunits);
+  p.lockstep = nullptr;
+  if (WIDE && persistent && pacing_enabled()) {
+    int rc = pace_array(&p.lockstep);
+    if (rc) return rc;
+    IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * npairs), 1, 1);
   cfg.blockDim = dim3(WIDE ? kWideThreads : kThreads, 1, 1);
@@ -950,9 +1087,9 @@ int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // A tiles in L2 (about 24 MB of hidden rows), and enough CTAs to fill the GPU.
 int choose_splits(int64_t m_tiles, int n_tiles, int H) {
   // L2 share for the A rows of the units in flight.  Long reductions (the wide kernel, whose A
-  // loads are marked evict-last) keep more rows resident and split the vocabulary less: at
-  // H = 4096, 80 MB gives 2 splits and measured 30% less DRAM traffic than 24 MB (7 splits).
-  int64_t budget_mb = H >= 2048 ? 80 : 24;
+  // loads are marked evict-last and whose pairs are paced) keep more rows resident and split the
+  // vocabulary less: at H = 4096, 40 MB gives 4 splits.
+  int64_t budget_mb = H >= 2048 ? 40 : 24;
   if (const char* e = getenv("INVOKERL_B200_L2_BUDGET_MB")) budget_mb = std::max<int64_t>(1, atoll(e));
   const int64_t resident_rows_budget = (budget_mb << 20) / (2ll * H);   // rows whose A tiles fit the budget
   const int64_t blocks_resident = std::max<int64_t>(1, resident_rows_budget / BM);
@@ -1152,25 +1289,18 @@ int check_common(const void* hidden, const void* weight, const int64_t* ids, int
 
 using namespace ikrl;
 
-extern "C" {
-
-size_t ikrl_lmhead_fwd_workspace_bytes(int64_t N, int32_t H, int32_t V) {
-  if (N <= 0 || H <= 0 || V <= 0) return 256;
-  return fwd_layout(N, H, V).total;
-}
-
-int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
-                            int32_t V, float* logp, float* lse, void* ws, size_t ws_bytes, void* stream) {
-  clear_error();
-  int rc = check_common(hidden, weight, ids, N, H, V, "ikrl_lmhead_logprob_fwd");
+static int lmhead_fwd_impl(const char* what, const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
+                    int32_t V, int64_t vocab_start, bool shard, float* logp, float* lse, void* ws, size_t ws_bytes,
+                    void* stream) {
+  int rc = check_common(hidden, weight, ids, N, H, V, what);
   if (rc) return rc;
   if (N == 0) return IKRL_OK;
-  IKRL_REQUIRE(logp != nullptr, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_logprob_fwd: logp is NULL");
+  IKRL_REQUIRE(logp != nullptr, IKRL_ERR_INVALID_ARGUMENT, "%s: output is NULL", what);
   const FwdLayout L = fwd_layout(N, H, V);
   IKRL_REQUIRE(ws != nullptr && ws_bytes >= L.total, IKRL_ERR_WORKSPACE,
-               "ikrl_lmhead_logprob_fwd: workspace %zu < %zu bytes", ws_bytes, L.total);
+               "%s: workspace %zu < %zu bytes", what, ws_bytes, L.total);
   IKRL_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, IKRL_ERR_ALIGNMENT,
-               "ikrl_lmhead_logprob_fwd: workspace must be 256-byte aligned");
+               "%s: workspace must be 256-byte aligned", what);
   cudaStream_t s = as_stream(stream);
   char* w = reinterpret_cast<char*>(ws);
   int* err = reinterpret_cast<int*>(w + L.err_off);
@@ -1183,46 +1313,46 @@ int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_
   GemmParams p{};
   p.M = (int)N; p.N = V; p.K = H;
   p.ids = ids;
+  p.id_offset = vocab_start;
   p.part_m = reinterpret_cast<float*>(w + L.pm_off);
   p.part_s = reinterpret_cast<float*>(w + L.ps_off);
   p.part_t = reinterpret_cast<float*>(w + L.pt_off);
   p.err = err;
   const int m_tiles = (int)cdiv64(N, BM);
   if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s))) return rc;
+  if (shard) {
+    lse_shard_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N,
+                                                                      vocab_start, V, p.part_sets, logp, lse, err);
+    return check_launch("lse_shard_combine_kernel");
+  }
   lse_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N, V,
                                                               p.part_sets, logp, lse, err);
   return check_launch("lse_combine_kernel");
 }
 
-size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows, int32_t dweight_dtype,
-                                       int32_t accumulate_dweight) {
-  if (N <= 0 || H <= 0 || V <= 0) return 256;
-  return bwd_layout(N, H, V, chunk_rows, dweight_dtype, accumulate_dweight).total;
-}
 
-int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids, const float* lse,
-                            const float* dlogp, int64_t N, int32_t H, int32_t V, int64_t chunk_rows, void* dhidden,
-                            void* dweight, int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
-                            size_t ws_bytes, void* stream) {
-  clear_error();
-  int rc = check_common(hidden, weight, ids, N, H, V, "ikrl_lmhead_logprob_bwd");
+static int lmhead_bwd_impl(const char* what, const void* hidden, const void* weight, const int64_t* ids,
+                           const float* lse, const float* dlogp, int64_t N, int32_t H, int32_t V, int64_t vocab_start,
+                           int64_t chunk_rows, void* dhidden, void* dweight, int32_t dweight_dtype,
+                           int32_t accumulate_dweight, void* ws, size_t ws_bytes, void* stream) {
+  int rc = check_common(hidden, weight, ids, N, H, V, what);
   if (rc) return rc;
   IKRL_REQUIRE(dweight_dtype == IKRL_DTYPE_F32 || dweight_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
-               "ikrl_lmhead_logprob_bwd: dweight dtype %d unsupported", dweight_dtype);
+               "%s: dweight dtype %d unsupported", what, dweight_dtype);
   IKRL_REQUIRE(!(accumulate_dweight && dweight_dtype == IKRL_DTYPE_BF16), IKRL_ERR_UNSUPPORTED,
-               "ikrl_lmhead_logprob_bwd: accumulating into a bf16 dweight is not supported; use fp32");
+               "%s: accumulating into a bf16 dweight is not supported; use fp32", what);
   if (N == 0) return IKRL_OK;
   IKRL_REQUIRE(lse && dlogp && (dhidden || dweight), IKRL_ERR_INVALID_ARGUMENT,
-               "ikrl_lmhead_logprob_bwd: null pointer");
+               "%s: null pointer", what);
   const BwdLayout L = bwd_layout(N, H, V, chunk_rows, dweight_dtype, accumulate_dweight);
   IKRL_REQUIRE(ws != nullptr && ws_bytes >= L.total, IKRL_ERR_WORKSPACE,
-               "ikrl_lmhead_logprob_bwd: workspace %zu < %zu bytes", ws_bytes, L.total);
+               "%s: workspace %zu < %zu bytes", what, ws_bytes, L.total);
   IKRL_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0, IKRL_ERR_ALIGNMENT,
-               "ikrl_lmhead_logprob_bwd: workspace must be 256-byte aligned");
+               "%s: workspace must be 256-byte aligned", what);
   IKRL_REQUIRE(dweight == nullptr || (reinterpret_cast<uintptr_t>(dweight) & 15) == 0, IKRL_ERR_ALIGNMENT,
-               "ikrl_lmhead_logprob_bwd: dweight must be 16-byte aligned");
+               "%s: dweight must be 16-byte aligned", what);
   IKRL_REQUIRE(dhidden == nullptr || (reinterpret_cast<uintptr_t>(dhidden) & 15) == 0, IKRL_ERR_ALIGNMENT,
-               "ikrl_lmhead_logprob_bwd: dhidden must be 16-byte aligned");
+               "%s: dhidden must be 16-byte aligned", what);
   cudaStream_t s = as_stream(stream);
   char* w = reinterpret_cast<char*>(ws);
   int* err = reinterpret_cast<int*>(w + L.err_off);
@@ -1260,7 +1390,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
     int64_t n_act = 0;
     IKRL_CUDA(cudaMemcpyAsync(&n_act, n_act_d, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     IKRL_CUDA(cudaStreamSynchronize(s));
-    IKRL_REQUIRE(n_act >= 0 && n_act <= N, IKRL_ERR_DEVICE, "ikrl_lmhead_logprob_bwd: bad active-row count %lld",
+    IKRL_REQUIRE(n_act >= 0 && n_act <= N, IKRL_ERR_DEVICE, "%s: bad active-row count %lld", what,
                  (long long)n_act);
     if (n_act == 0) {
       if (dhidden) IKRL_CUDA(cudaMemsetAsync(dhidden, 0, (size_t)N * H * 2, s));
@@ -1303,6 +1433,7 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
       p.M = (int)rows; p.N = V; p.K = H;
       const int sp = choose_splits(m_tiles, n_vt, H);
       p.ids = idsrc + c0; p.lse = lsesrc + c0; p.g = gsrc + c0;
+      p.id_offset = vocab_start;
       p.out_bf16 = dS; p.ld_bf16 = L.lds;
       p.err = err;
       if ((rc = launch_k1<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, sp, s))) return rc;
@@ -1352,6 +1483,71 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
     if ((rc = check_launch("scatter_rows_kernel"))) return rc;
   }
   return IKRL_OK;
+}
+
+
+extern "C" {
+
+size_t ikrl_lmhead_fwd_workspace_bytes(int64_t N, int32_t H, int32_t V) {
+  if (N <= 0 || H <= 0 || V <= 0) return 256;
+  return fwd_layout(N, H, V).total;
+}
+
+int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
+                            int32_t V, float* logp, float* lse, void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  return lmhead_fwd_impl("ikrl_lmhead_logprob_fwd", hidden, weight, ids, N, H, V, 0, false, logp, lse, ws, ws_bytes,
+                         stream);
+}
+
+int ikrl_lmhead_shard_fwd(const void* hidden, const void* weight_shard, const int64_t* ids, int64_t N, int32_t H,
+                          int32_t V_shard, int64_t vocab_start, float* tlogit, float* lse_shard, void* ws,
+                          size_t ws_bytes, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(vocab_start >= 0, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_shard_fwd: vocab_start %lld < 0",
+               (long long)vocab_start);
+  IKRL_REQUIRE(N == 0 || lse_shard != nullptr, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_shard_fwd: lse_shard is NULL");
+  return lmhead_fwd_impl("ikrl_lmhead_shard_fwd", hidden, weight_shard, ids, N, H, V_shard, vocab_start, true, tlogit,
+                         lse_shard, ws, ws_bytes, stream);
+}
+
+int ikrl_vocab_parallel_combine(const float* parts, const int64_t* ids, int64_t N, int32_t P, int64_t V_total,
+                                float* logp, float* lse, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(N >= 0 && P >= 1 && V_total > 0, IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_vocab_parallel_combine: bad sizes N=%lld P=%d V=%lld", (long long)N, P, (long long)V_total);
+  if (N == 0) return IKRL_OK;
+  IKRL_REQUIRE(parts && ids && logp, IKRL_ERR_INVALID_ARGUMENT, "ikrl_vocab_parallel_combine: null pointer");
+  vocab_parallel_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, as_stream(stream)>>>(parts, ids, N, P, V_total,
+                                                                                        logp, lse);
+  return check_launch("vocab_parallel_combine_kernel");
+}
+
+size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows, int32_t dweight_dtype,
+                                       int32_t accumulate_dweight) {
+  if (N <= 0 || H <= 0 || V <= 0) return 256;
+  return bwd_layout(N, H, V, chunk_rows, dweight_dtype, accumulate_dweight).total;
+}
+
+int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids, const float* lse,
+                            const float* dlogp, int64_t N, int32_t H, int32_t V, int64_t chunk_rows, void* dhidden,
+                            void* dweight, int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
+                            size_t ws_bytes, void* stream) {
+  clear_error();
+  return lmhead_bwd_impl("ikrl_lmhead_logprob_bwd", hidden, weight, ids, lse, dlogp, N, H, V, 0, chunk_rows, dhidden,
+                         dweight, dweight_dtype, accumulate_dweight, ws, ws_bytes, stream);
+}
+
+int ikrl_lmhead_shard_bwd(const void* hidden, const void* weight_shard, const int64_t* ids, const float* lse,
+                          const float* dlogp, int64_t N, int32_t H, int32_t V_shard, int64_t vocab_start,
+                          int64_t chunk_rows, void* dhidden_partial, void* dweight_shard, int32_t dweight_dtype,
+                          int32_t accumulate_dweight, void* ws, size_t ws_bytes, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(vocab_start >= 0, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_shard_bwd: vocab_start %lld < 0",
+               (long long)vocab_start);
+  return lmhead_bwd_impl("ikrl_lmhead_shard_bwd", hidden, weight_shard, ids, lse, dlogp, N, H, V_shard, vocab_start,
+                         chunk_rows, dhidden_partial, dweight_shard, dweight_dtype, accumulate_dweight, ws, ws_bytes,
+                         stream);
 }
 
 int ikrl_lmhead_set_cta_pairs(int32_t enable) {

@@ -97,3 +97,57 @@ def test_two_rank_row_sharding_matches_full_batch():
     rel = lambda a, c: float((a.float() - c.float()).norm() / c.float().norm())  # noqa: E731
     assert rel(dh, dh_o) <= 1e-2
     assert rel(dw, dw_o) <= 1e-2
+
+
+def _vp_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from invokerl_b200.synthetic import lmhead_inputs
+    from invokerl_b200.vocab_parallel import lmhead_logprob_vocab_parallel, shard_bounds
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        n, h_dim, v = 384, 256, 33000
+        li = lmhead_inputs(n, h_dim, v, seed=12, w_std=0.3)
+        s, e = shard_bounds(v, world, rank)
+        h = li.hidden.to(dev).requires_grad_(True)
+        w = li.weight[s:e].contiguous().to(dev).requires_grad_(True)
+        up = torch.randn(n, generator=torch.Generator().manual_seed(13)).to(dev)
+        lp = lmhead_logprob_vocab_parallel(h, w, li.targets.to(dev), s, v)
+        (lp * up).sum().backward()
+        dws = [None] * world
+        dist.all_gather_object(dws, w.grad.float().cpu())
+        if rank == 0:
+            q.put((lp.detach().cpu(), h.grad.float().cpu(), torch.cat(dws)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_vocab_parallel_head_matches_oracle():
+    import oracle
+    from invokerl_b200.synthetic import lmhead_inputs
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_vp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    lp, dh, dw = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    li = lmhead_inputs(384, 256, 33000, seed=12, w_std=0.3)
+    up = torch.randn(384, generator=torch.Generator().manual_seed(13))
+    lp_o, dh_o, dw_o = oracle.lmhead_logprob_grads(li.hidden, li.weight, li.targets, up)
+    assert float((lp - lp_o).abs().max()) <= 2e-3
+    rel = lambda a, c: float((a.float() - c.float()).norm() / c.float().norm())  # noqa: E731
+    assert rel(dh, dh_o) <= 1e-2
+    assert rel(dw, dw_o) <= 1e-2
