@@ -93,7 +93,10 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 // arrive on when a tile is consumed (this CTA's, or the pair leader's when cluster_arrive).
 // tile_base: number of tiles this CTA consumed before this unit (accumulator ring position).
 // Returns false when a wait gave up (abort).
-template <int EPI, int TILE_N = BN, int NBUF = 2, int HALVES = 1>
+// SPLIT (wide tile, one accumulator): every warp drains its 128 columns of the first 256-column
+// half, releases that half (acc_empty[0]) so the next tile's first-half MMAs can start, then
+// drains its 128 columns of the second half and releases it (acc_empty[1]).
+template <int EPI, int TILE_N = BN, int NBUF = 2, int HALVES = 1, bool SPLIT = false>
 __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
                                               int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
                                               const uint32_t (&acc_empty)[2], bool cluster_arrive,
@@ -102,6 +105,9 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   bool ok = true;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
   constexpr int kCols = TILE_N / HALVES;  // columns of the tile this warp drains
+  static_assert(!SPLIT || (HALVES == 2 && NBUF == 1), "split drain needs two column groups, one accumulator");
+  constexpr int kSegs = SPLIT ? 2 : 1;                      // column segments, drained in order
+  constexpr int kSegCols = SPLIT ? TILE_N / 4 : kCols;
   const int half = HALVES == 1 ? 0 : (warp - 2) / 4;
   const int c_lo = half * kCols;
   const int r = q * 32 + lane;
@@ -131,12 +137,15 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       // Pull this row's slice of the fp32 accumulator into L2 while the MMAs run, so the
       // read-modify-write below hits L2.
       if (row_ok && p.f32_mode != F32_STORE) {
-        const int n0p = (t_begin + j) * TILE_N + c_lo;
-        const int ncols = min(kCols, p.N - n0p);
-        if (ncols > 0)
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
-                       "r"((uint32_t)ncols * 4u)
-                       : "memory");
+#pragma unroll
+        for (int sg = 0; sg < kSegs; ++sg) {
+          const int n0p = (t_begin + j) * TILE_N + (SPLIT ? sg * (TILE_N / 2) + half * kSegCols : c_lo);
+          const int ncols = min(kSegCols, p.N - n0p);
+          if (ncols > 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
+                         "r"((uint32_t)ncols * 4u)
+                         : "memory");
+        }
       }
     }
     if (!mbar_wait(acc_full[acc], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) {
@@ -146,8 +155,10 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
     tc_fence_after();
     const int n0 = (t_begin + j) * TILE_N;
     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
+    for (int sg = 0; sg < kSegs; ++sg) {
+    const int cs = SPLIT ? sg * (TILE_N / 2) + half * kSegCols : c_lo;
 #pragma unroll 1
-    for (int c = c_lo; c < c_lo + kCols; c += 32) {
+    for (int c = cs; c < cs + kSegCols; c += 32) {
       const int col0 = n0 + c;
       if (col0 >= p.N) break;  // warp-uniform
       float v[32];
@@ -227,11 +238,18 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
         }
       }
     }
+    if (SPLIT && sg == 0) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty[0]);  // first half drained
+    }
+    }  // column segments
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
-      if (cluster_arrive) mbar_arrive_cluster(acc_empty[acc]);
-      else mbar_arrive(acc_empty[acc]);
+      const int rel = SPLIT ? 1 : acc;
+      if (cluster_arrive) mbar_arrive_cluster(acc_empty[rel]);
+      else mbar_arrive(acc_empty[rel]);
     }
   }
   if constexpr (EPI == EPI_LSE) {
@@ -757,31 +775,60 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         const int split = u % p.splits;
         const int t_begin = split * p.tiles_per_split;
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
+        // MMAs of one K block into accumulator half h (TMEM columns [256h, 256h + 256)).
+        auto issue_half = [&](int st, int kb, int h) {
+          const uint32_t a_addr = smem_base + st * kWideStageBytes;
+          const uint32_t bh = a_addr + kTileA + h * ((BN / 2) * BK * 2);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
+                                     : smem_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc(bh + k * 2048, kMnAtomBytes, 1024) : smem_desc(bh + k * 32, 16, 1024);
+            mma_bf16_pair(tmem_base + (uint32_t)(h * BN), ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+        };
+        auto release_stage = [&](int st) {
+          const uint32_t eb = smem_u32(&empty_bar[st]);
+          mma_commit_pair(mapa_shared(eb, 0));
+          mma_commit_pair(mapa_shared(eb, 1));
+        };
         for (int t = t_begin; t < t_end && ok; ++t, ++j) {
-          if (!mbar_wait(smem_u32(&acc_empty[0]), ((uint32_t)j & 1u) ^ 1u, abort_v, p.err, kErrTimeoutMma)) {
+          const uint32_t epar = ((uint32_t)j & 1u) ^ 1u;
+          if (!mbar_wait(smem_u32(&acc_empty[0]), epar, abort_v, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          for (int kb = 0; kb < nk; ++kb) {
+          // The first half of the accumulator is free: run its MMAs over the K blocks already
+          // staged while the epilogue still drains the second half.
+          const int look = min(kWideStages, nk);
+          {
+            int st = stage;
+            uint32_t ph = phase;
+            for (int kb = 0; kb < look; ++kb) {
+              if (!mbar_wait(smem_u32(&full_bar[st]), ph, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+              tc_fence_after();
+              issue_half(st, kb, 0);
+              if (++st == kWideStages) { st = 0; ph ^= 1u; }
+            }
+          }
+          if (!ok) break;
+          if (!mbar_wait(smem_u32(&acc_empty[1]), epar, abort_v, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int kb = 0; kb < look; ++kb) {
+            issue_half(stage, kb, 1);
+            release_stage(stage);
+            if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
+          }
+          for (int kb = look; kb < nk; ++kb) {
             if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t a_addr = smem_base + stage * kWideStageBytes;
-            const uint32_t b_addr = a_addr + kTileA;
-#pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, kMnAtomBytes, 1024)
-                                       : smem_desc(a_addr + k * 32, 16, 1024);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const uint32_t bh = b_addr + h * ((BN / 2) * BK * 2);
-                const uint64_t bd = B_MN ? smem_desc(bh + k * 2048, kMnAtomBytes, 1024) : smem_desc(bh + k * 32, 16, 1024);
-                mma_bf16_pair(tmem_base + (uint32_t)(h * BN), ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-              }
-            }
-            const uint32_t eb = smem_u32(&empty_bar[stage]);
-            mma_commit_pair(mapa_shared(eb, 0));
-            mma_commit_pair(mapa_shared(eb, 1));
+            issue_half(stage, kb, 0);
+            issue_half(stage, kb, 1);
+            release_stage(stage);
             if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
           }
           if (ok) {
@@ -806,7 +853,8 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
       const int t_begin = split * p.tiles_per_split;
       const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-      if (!epilogue_role<EPI, WN, 1, 2>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v, jb))
+      if (!epilogue_role<EPI, WN, 1, 2, true>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v,
+                                              jb))
         break;
       jb += t_end - t_begin;
     }

@@ -56,8 +56,10 @@ def test_emulated_shards_match_unsharded(N, H, V, P):
     assert float(dh.cpu()[~keep].abs().max()) == 0.0
     assert rel_fro(dw.cpu(), dw_o) <= 1e-2
     dh_u, dw_u = ops.lmhead_backward_raw(h, w, td, lse_u, gd, dw_dtype=torch.float32)
+    # dH: the unsharded result is one bf16 rounding of the sum, the sharded one a sum of P bf16
+    # terms; dW: the shards' dS uses the merged lse, so a few bf16 dS values round the other way
     assert rel_fro(dh, dh_u) <= 1e-2
-    torch.testing.assert_close(dw, dw_u, rtol=1e-3, atol=1e-5)
+    assert rel_fro(dw, dw_u) <= 1e-3
 
 
 def test_single_rank_autograd_equals_fused_head():
