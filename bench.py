@@ -193,15 +193,17 @@ class LMHeadGRPO:
         H, B, T, G = self.H, self.B, self.T, self.G
         batch = rollout_batch(B // G, G, T, prompt_len=self.p["prompt"], completion_len=self.p["completion"],
                               vocab=V, seed=0)
-        local = shard_batch(batch, rank, world)
+        # Ranks take whole groups balanced by work (rows for the forward, response tokens for the
+        # backward), not by count.
+        local = shard_batch(batch, rank, world, balance=world > 1)
         local.extras = {}
         Bl = local.token_ids.shape[0]
-        first_group = int(local.group_ids[0])
+        gids = [int(local.group_ids[j * G]) for j in range(Bl // G)]
         # Hidden rows and W are generated on the device per prompt group, so the global data is
         # the same for any number of ranks.
         hidden = torch.empty(Bl * T, H, dtype=torch.bfloat16, device=device)
-        for j in range(Bl // G):
-            gen = torch.Generator(device=device).manual_seed(1000 + first_group + j)
+        for j, gid in enumerate(gids):
+            gen = torch.Generator(device=device).manual_seed(1000 + gid)
             hidden[j * G * T:(j + 1) * G * T] = torch.randn(G * T, H, device=device, generator=gen).to(torch.bfloat16)
         gw = torch.Generator(device=device).manual_seed(7)
         weight = (0.02 * torch.randn(V, H, device=device, generator=gw)).to(torch.bfloat16)
@@ -209,10 +211,16 @@ class LMHeadGRPO:
         # Rollout-time log-probs of the same policy: old = lp + N(0, 0.05), ref = lp + N(0, 0.1), so
         # ratios and KL terms have realistic sizes for this random-init head.
         lp, _ = ops.lmhead_forward_raw(hidden, weight, ids)
-        gr = torch.Generator(device=device).manual_seed(11 + first_group)
-        local.old_log_probs = (lp.view(Bl, T) + 0.05 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
-        local.ref_log_probs = (lp.view(Bl, T) + 0.1 * torch.randn(Bl, T, device=device, generator=gr)).cpu()
-        del lp
+        lp = lp.view(Bl, T)
+        old = torch.empty_like(lp)
+        ref = torch.empty_like(lp)
+        for j, gid in enumerate(gids):
+            gr = torch.Generator(device=device).manual_seed(11 + gid)
+            rows = slice(j * G, (j + 1) * G)
+            old[rows] = lp[rows] + 0.05 * torch.randn(G, T, device=device, generator=gr)
+            ref[rows] = lp[rows] + 0.1 * torch.randn(G, T, device=device, generator=gr)
+        local.old_log_probs, local.ref_log_probs = old.cpu(), ref.cpu()
+        del lp, old, ref
         self.local, self.Bl = local, Bl
         self.dev_batch = to_device_batch(local, device)
         self.hidden = hidden.requires_grad_(True)
@@ -272,7 +280,8 @@ class LMHeadGRPO:
             "hidden": self.H,
             "vocab": V,
             "group_size": self.G,
-            "parallelism": f"dp{world} (row shards of whole groups; scalar NCCL all-reduce)",
+            "parallelism": f"dp{world} (whole groups per rank, balanced by rows + response tokens; "
+                           "scalar NCCL all-reduces)",
             "l2": f"inputs larger than L2 (hidden {self.B * self.T * self.H * 2 / 1e9:.1f} GB per step), no flush",
         }
 

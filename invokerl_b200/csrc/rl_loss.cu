@@ -292,8 +292,7 @@ struct LossArgs {
   int B, G;
   void* dlp;
   float* dvalues;
-  double* partials;
-  unsigned* ticket;
+  double* partials;  // [grid + 1][IKRL_LOSS_NSUMS]: per-block sums, then the batch-level slot
   double* sums;
   int64_t n;
   ikrl_loss_params p;
@@ -404,55 +403,91 @@ __device__ __forceinline__ void ld4(const float* p, int64_t q, float (&x)[4]) {
   x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
 }
 
-// Per-block sums -> partials; the last block to finish reduces them in a fixed order and adds the
-// batch-level terms.
-__device__ __forceinline__ void finish_loss_sums(const LossArgs& a, double (&v)[kTokenSums], double* scratch,
-                                                 bool* am_last, bool derive_token_loss) {
-  block_sum<double, kTokenSums>(v, scratch);
-  if (threadIdx.x == 0) {
+// The loss kernels run one block more than they give tokens to: block 0 computes the batch-level
+// reward terms (they take a few µs of dependent loads) while blocks 1.. process the tokens, so no
+// token block finishes late.  With a one-block grid, block 0 does both.
+struct TokenGrid {
+  int tb;  // this block's index among the token blocks (-1: the batch-terms block)
+  int nb;  // number of token blocks
+};
+__device__ __forceinline__ TokenGrid token_grid() {
+  const int tok0 = gridDim.x > 1 ? 1 : 0;
+  return {(int)blockIdx.x - tok0, (int)gridDim.x - tok0};
+}
+__host__ __device__ inline int token_blocks(int grid) { return grid > 1 ? grid - 1 : 1; }
+
+// Per-block sums -> partials[slot] (fixed order: float warp sums, then a double sum over the
+// warps).  The token blocks' sums are combined afterwards, in a fixed order, by
+// loss_sums_reduce_kernel (a separate launch, so no block waits on the others and no counter has
+// to be reset between calls).
+__device__ __forceinline__ void write_block_sums(const LossArgs& a, const float (&v)[kTokenSums], double* scratch,
+                                                 int slot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  float w[kTokenSums];
 #pragma unroll
-    for (int i = 0; i < kTokenSums; ++i) a.partials[(int64_t)blockIdx.x * IKRL_LOSS_NSUMS + i] = v[i];
-    __threadfence();
-    *am_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  for (int i = 0; i < kTokenSums; ++i) w[i] = warp_sum(v[i]);
+  __syncthreads();  // scratch may still be read by an earlier block-wide reduction
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < kTokenSums; ++i) scratch[i * 32 + warp] = (double)w[i];
   }
   __syncthreads();
-  if (*am_last) {
-    __threadfence();
-    // Fixed-order reduction of the per-block partials by the whole block: thread i takes blocks
-    // i, i + blockDim, ... in order, then the block tree combines the threads.
-    double t[kTokenSums];
+  if (warp == 0) {
 #pragma unroll
-    for (int i = 0; i < kTokenSums; ++i) t[i] = 0.0;
-    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+    for (int i = 0; i < kTokenSums; ++i) {
+      double t = lane < nw ? scratch[i * 32 + lane] : 0.0;
+      t = warp_sum(t);
+      if (lane == 0) a.partials[(int64_t)slot * IKRL_LOSS_NSUMS + i] = t;
+    }
+  }
+}
+
+// Batch-level terms: rewards.sum() (for rewards.mean()) and the zero-variance group count
+// (dapo.py:132-135), into the slot after the nb token blocks' partials.
+__device__ __forceinline__ void write_batch_terms(const LossArgs& a, double* scratch, int nb) {
+  double r[2] = {0.0, 0.0};
+  for (int b = threadIdx.x; b < a.B; b += blockDim.x) r[0] += a.rewards[b];
+  if (a.G > 0) {
+    for (int g = threadIdx.x; g < a.B / a.G; g += blockDim.x) {
+      double mean, sd;
+      group_stats(a.rewards + g * a.G, a.G, mean, sd);
+      if ((float)sd < 1e-8f) r[1] += 1.0;
+    }
+  }
+  block_sum<double, 2>(r, scratch);
+  if (threadIdx.x == 0) {
+    a.partials[(int64_t)nb * IKRL_LOSS_NSUMS + 0] = r[0];
+    a.partials[(int64_t)nb * IKRL_LOSS_NSUMS + 1] = r[1];
+  }
+}
+
+// sums[0..8] = fixed-order sum of the nblocks per-block partials (thread i takes blocks i,
+// i + 256, ..., then the block tree combines the threads); sums[9..12] the batch-level terms.
+// derive_token_loss: sums[8] = sums[0] + beta * sums[1] (the lean GRPO kernels leave it out).
+__global__ void __launch_bounds__(256) loss_sums_reduce_kernel(const double* __restrict__ partials, int nblocks,
+                                                               int derive_token_loss, float beta, int B, int G,
+                                                               double* __restrict__ sums) {
+  __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
+  // Launched as a programmatic dependent of the loss kernel: it may start while that kernel runs
+  // and waits here until it has completed and its partials are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  double t[kTokenSums];
 #pragma unroll
-      for (int i = 0; i < kTokenSums; ++i) t[i] += __ldcg(a.partials + (int64_t)b * IKRL_LOSS_NSUMS + i);
-    }
-    block_sum<double, kTokenSums>(t, scratch);
-    if (threadIdx.x == 0) {
+  for (int i = 0; i < kTokenSums; ++i) t[i] = 0.0;
+  for (int b = threadIdx.x; b < nblocks; b += blockDim.x) {
 #pragma unroll
-      for (int i = 0; i < kTokenSums; ++i) a.sums[i] = t[i];
-      // GRPO token loss sum(pl*m) + beta*sum(kl*m), when the per-token pass left it out.
-      if (derive_token_loss) a.sums[8] = t[0] + (double)a.p.beta * t[1];
-    }
-    // Batch-level terms: rewards.mean() and the zero-variance group count (dapo.py:132-135).
-    double r[2] = {0.0, 0.0};
-    for (int b = threadIdx.x; b < a.B; b += blockDim.x) r[0] += a.rewards[b];
-    if (a.G > 0) {
-      for (int g = threadIdx.x; g < a.B / a.G; g += blockDim.x) {
-        double mean, sd;
-        group_stats(a.rewards + g * a.G, a.G, mean, sd);
-        if ((float)sd < 1e-8f) r[1] += 1.0;
-      }
-    }
-    block_sum<double, 2>(r, scratch);
-    if (threadIdx.x == 0) {
-      a.sums[9] = r[0];
-      a.sums[10] = (double)a.B;
-      a.sums[11] = r[1];
-      a.sums[12] = a.G > 0 ? (double)(a.B / a.G) : 0.0;
-      a.sums[13] = a.sums[14] = a.sums[15] = 0.0;
-      *a.ticket = 0;
-    }
+    for (int i = 0; i < kTokenSums; ++i) t[i] += partials[(int64_t)b * IKRL_LOSS_NSUMS + i];
+  }
+  block_sum<double, kTokenSums>(t, scratch);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < kTokenSums; ++i) sums[i] = t[i];
+    if (derive_token_loss) sums[8] = t[0] + (double)beta * t[1];
+    sums[9] = partials[(int64_t)nblocks * IKRL_LOSS_NSUMS + 0];
+    sums[10] = (double)B;
+    sums[11] = partials[(int64_t)nblocks * IKRL_LOSS_NSUMS + 1];
+    sums[12] = G > 0 ? (double)(B / G) : 0.0;
+    sums[13] = sums[14] = sums[15] = 0.0;
   }
 }
 
@@ -460,7 +495,11 @@ __device__ __forceinline__ void finish_loss_sums(const LossArgs& a, double (&v)[
 template <int FAMILY, bool BF16, bool VEC>
 __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kernel(LossArgs a) {
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
-  __shared__ bool am_last;
+  // Every block has started: the sums-reduce kernel may be scheduled now (it waits for this grid).
+  asm volatile("griddepcontrol.launch_dependents;");
+  const TokenGrid tg = token_grid();
+  if (blockIdx.x == 0) write_batch_terms(a, scratch, tg.nb);
+  if (tg.tb < 0) return;
   float acc[kTokenSums];
 #pragma unroll
   for (int i = 0; i < kTokenSums; ++i) acc[i] = 0.f;
@@ -468,11 +507,11 @@ __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kern
   const float inv_n = 1.f / fmaxf((float)(*a.ntok), 1.f);
   const bool whiten_on = a.whiten != nullptr && a.whiten[3] != 0.f;
   const float wmean = whiten_on ? a.whiten[0] : 0.f, wstd = whiten_on ? a.whiten[1] : 0.f;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t stride = (int64_t)tg.nb * blockDim.x;
   if constexpr (VEC) {
     // kLossUnroll quads per thread per step, all loads issued before any compute.
     const int64_t nq = a.n >> 2;
-    for (int64_t q0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q0 < nq; q0 += stride * kLossUnroll) {
+    for (int64_t q0 = (int64_t)tg.tb * blockDim.x + threadIdx.x; q0 < nq; q0 += stride * kLossUnroll) {
       float lp[kLossUnroll][4], old[kLossUnroll][4], ref[kLossUnroll][4], adv[kLossUnroll][4];
       float vv[kLossUnroll][4], ov[kLossUnroll][4];
       uint32_t mw[kLossUnroll];
@@ -507,7 +546,7 @@ __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kern
       }
     }
   } else {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    for (int64_t i = (int64_t)tg.tb * blockDim.x + threadIdx.x; i < a.n; i += stride) {
       const float lp = load_lp<BF16>(a.new_lp, i);
       const float old = __ldg(a.old_lp + i);
       const float ref = a.ref_lp ? __ldg(a.ref_lp + i) : 0.f;
@@ -523,10 +562,7 @@ __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kern
     }
   }
 
-  double v[kTokenSums];
-#pragma unroll
-  for (int i = 0; i < kTokenSums; ++i) v[i] = (double)acc[i];
-  finish_loss_sums(a, v, scratch, &am_last, false);
+  write_block_sums(a, acc, scratch, tg.tb);
 }
 
 // Masked sums of the lean GRPO / DAPO pass (grpo.py:103-140): policy loss, KL, clip count,
@@ -571,12 +607,11 @@ __device__ __forceinline__ float grpo_token(float x, float o, float r, float A, 
   return g * dpl + (g * beta) * dkl;
 }
 
-__device__ __forceinline__ void grpo_finish(const LossArgs& a, const GrpoSums& acc, double* scratch, bool* am_last,
+__device__ __forceinline__ void grpo_finish(const LossArgs& a, const GrpoSums& acc, double* scratch, int slot,
                                             bool aborted = false) {
-  double v[kTokenSums] = {(double)acc.pl, (double)acc.kl, (double)acc.clip, 0.5 * (double)acc.lr2, (double)acc.adv,
-                          (double)acc.m, (double)acc.lp, 0.0, 0.0};
-  if (aborted) v[0] = __longlong_as_double(0x7ff8000000000000ll);  // a gave-up wait poisons the loss
-  finish_loss_sums(a, v, scratch, am_last, true);
+  float v[kTokenSums] = {acc.pl, acc.kl, acc.clip, 0.5f * acc.lr2, acc.adv, acc.m, acc.lp, 0.f, 0.f};
+  if (aborted) v[0] = __int_as_float(0x7fc00000);  // a gave-up wait poisons the loss
+  write_block_sums(a, v, scratch, slot);
 }
 
 // GRPO / DAPO with no value head and no whitening (grpo.py:84-143, dapo.py:90-150): four tokens
@@ -586,13 +621,17 @@ __device__ __forceinline__ void grpo_finish(const LossArgs& a, const GrpoSums& a
 template <bool BF16, int KL>
 __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) grpo_loss_kernel(LossArgs a) {
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
-  __shared__ bool am_last;
+  // Every block has started: the sums-reduce kernel may be scheduled now (it waits for this grid).
+  asm volatile("griddepcontrol.launch_dependents;");
+  const TokenGrid tg = token_grid();
+  if (blockIdx.x == 0) write_batch_terms(a, scratch, tg.nb);
+  if (tg.tb < 0) return;
   GrpoSums acc;
   const float inv_n = 1.f / fmaxf((float)(*a.ntok), 1.f);
   const float lo = a.p.ratio_lo, hi = a.p.ratio_hi, ceps = a.p.clip_metric_eps, beta = a.p.beta;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t stride = (int64_t)tg.nb * blockDim.x;
   const int64_t nq = a.n >> 2;
-  for (int64_t q0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q0 < nq; q0 += stride * kLossUnroll) {
+  for (int64_t q0 = (int64_t)tg.tb * blockDim.x + threadIdx.x; q0 < nq; q0 += stride * kLossUnroll) {
     float lp[kLossUnroll][4], old[kLossUnroll][4], ref[kLossUnroll][4], adv[kLossUnroll][4];
     uint32_t mw[kLossUnroll];
 #pragma unroll
@@ -618,7 +657,7 @@ __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) grpo_loss_kern
       if (a.dlp) store_lp4<BF16>(a.dlp, q, d);
     }
   }
-  grpo_finish(a, acc, scratch, &am_last);
+  grpo_finish(a, acc, scratch, tg.tb);
 }
 
 // The same pass with the inputs staged through shared memory by bulk copies (cp.async.bulk,
@@ -649,18 +688,19 @@ template <bool BF16, int KL>
 __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk_kernel(LossArgs a) {
   extern __shared__ __align__(128) uint8_t bulk_smem[];
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
-  __shared__ bool am_last;
   __shared__ __align__(8) uint64_t full_bar[kBulkStages], empty_bar[kBulkStages];
-  __shared__ int abort_flag;
+  __shared__ int abort_flag, err_word;
   constexpr uint32_t kLpBytes = kBulkTile * (BF16 ? 2 : 4);
   constexpr uint32_t kOffOld = kLpBytes, kOffRef = kOffOld + 4 * kBulkTile, kOffAdv = kOffRef + 4 * kBulkTile,
                      kOffMask = kOffAdv + 4 * kBulkTile;
   constexpr uint32_t kStage = bulk_stage_bytes<BF16>();
+  // Every block has started: the sums-reduce kernel may be scheduled now (it waits for this grid).
+  asm volatile("griddepcontrol.launch_dependents;");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_full = a.n / kBulkTile;
   const int64_t n_tiles = (a.n + kBulkTile - 1) / kBulkTile;
   volatile int* abort_v = &abort_flag;
-  int* err = reinterpret_cast<int*>(a.ticket) + 1;
+  int* err = &err_word;
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < kBulkStages; ++st) {
@@ -668,9 +708,13 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
       mbar_init(smem_u32(&empty_bar[st]), kBulkConsumers / 32);
     }
     abort_flag = 0;
+    err_word = 0;
     fence_barrier_init();
   }
   __syncthreads();
+  const TokenGrid tg = token_grid();
+  if (blockIdx.x == 0) write_batch_terms(a, scratch, tg.nb);
+  if (tg.tb < 0) return;
   const uint32_t sbase = smem_u32(bulk_smem);
   GrpoSums acc;
 
@@ -678,7 +722,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
     // ---- producer ----
     if (lane == 0) {
       int i = 0;
-      for (int64_t t = blockIdx.x; t < n_full; t += gridDim.x, ++i) {
+      for (int64_t t = tg.tb; t < n_full; t += tg.nb, ++i) {
         const int st = i % kBulkStages;
         const uint32_t ph = (uint32_t)(i / kBulkStages) & 1u;
         if (!mbar_wait(smem_u32(&empty_bar[st]), ph ^ 1u, abort_v, err, kErrTimeoutProducer)) break;
@@ -709,7 +753,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
     const float inv_n = 1.f / fmaxf((float)(*a.ntok), 1.f);
     const float lo = a.p.ratio_lo, hi = a.p.ratio_hi, ceps = a.p.clip_metric_eps, beta = a.p.beta;
     int i = 0;
-    for (int64_t t = blockIdx.x; t < n_full; t += gridDim.x, ++i) {
+    for (int64_t t = tg.tb; t < n_full; t += tg.nb, ++i) {
       const int st = i % kBulkStages;
       const uint32_t ph = (uint32_t)(i / kBulkStages) & 1u;
       if (!mbar_wait(smem_u32(&full_bar[st]), ph, abort_v, err, kErrTimeoutEpilogue)) break;
@@ -745,7 +789,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
       if (a.dlp) store_lp4<BF16>(a.dlp, t * (kBulkTile / 4) + threadIdx.x, d);
     }
     // the partial tile, if any, goes to the block that would have been dealt it
-    if (n_tiles > n_full && (n_full % gridDim.x) == blockIdx.x && !*abort_v) {
+    if (n_tiles > n_full && (n_full % tg.nb) == tg.tb && !*abort_v) {
       for (int64_t k = n_full * kBulkTile + threadIdx.x; k < a.n; k += kBulkConsumers) {
         const float x = load_lp<BF16>(a.new_lp, k);
         const float d = grpo_token<KL>(x, a.old_lp[k], KL != 0 ? a.ref_lp[k] : 0.f, a.adv[k], a.mask[k] != 0, inv_n,
@@ -755,7 +799,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
     }
   }
   __syncthreads();
-  grpo_finish(a, acc, scratch, &am_last, *abort_v != 0);
+  grpo_finish(a, acc, scratch, tg.tb, *abort_v != 0);
 }
 
 __global__ void clip_loss_finalize_kernel(const double* __restrict__ s, const int64_t* __restrict__ ntok,
@@ -958,6 +1002,28 @@ int lean_loss_mode() {
   return 1;
 }
 
+// The fixed-order combine of the loss kernel's per-block partials (and its batch-level slot).
+int launch_sums_reduce(const LossArgs& a, int nblocks, bool derive_token_loss, cudaStream_t s) {
+  // Programmatic dependent launch: the one-block reduce is scheduled while the loss kernel still
+  // runs (hiding its launch latency) and waits in-kernel for the loss kernel to finish.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const double* partials = a.partials;
+  const int derive = derive_token_loss ? 1 : 0;
+  const float beta = a.p.beta;
+  const int B = a.B, G = a.G;
+  double* sums = a.sums;
+  IKRL_CUDA(cudaLaunchKernelEx(&cfg, loss_sums_reduce_kernel, partials, nblocks, derive, beta, B, G, sums));
+  return check_launch("loss_sums_reduce_kernel");
+}
+
 int loss_grid(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(cdiv(n, 4), kLossThreads), kLossMaxBlocks)); }
 
 }  // namespace
@@ -1058,7 +1124,8 @@ int ikrl_gae_advantages(const float* rewards_b, const float* rewards_bt, const f
 }
 
 size_t ikrl_clip_loss_workspace_bytes(int64_t n_tokens) {
-  return 256 + (size_t)loss_grid(n_tokens) * IKRL_LOSS_NSUMS * sizeof(double);
+  // per-block partials plus one slot for the batch-level terms
+  return 256 + (size_t)(loss_grid(n_tokens) + 1) * IKRL_LOSS_NSUMS * sizeof(double);
 }
 
 int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp, const float* ref_lp,
@@ -1088,10 +1155,8 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
   a.new_lp = new_lp; a.old_lp = old_lp; a.ref_lp = ref_lp; a.adv = adv; a.mask = mask; a.ntok = ntok;
   a.rewards = rewards; a.B = B; a.G = G;
   a.whiten = whiten; a.values = values; a.old_values = old_values; a.dlp = dlp_out; a.dvalues = dvalues_out;
-  a.ticket = reinterpret_cast<unsigned*>(ws);
   a.partials = reinterpret_cast<double*>(reinterpret_cast<char*>(ws) + 256);
   a.sums = sums_out; a.n = n; a.p = *params;
-  IKRL_CUDA(cudaMemsetAsync(a.ticket, 0, 2 * sizeof(unsigned), s));  // ticket and the bulk kernel's error word
   const int grid = loss_grid(n);
   const bool bf = lp_dtype == IKRL_DTYPE_BF16;
   auto al = [](const void* p, uintptr_t m) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0; };
@@ -1105,7 +1170,8 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
     const bool bulk_ok = lean == 2 && n >= kBulkTile && al(new_lp, 16) && al(old_lp, 16) && al(ref_lp, 16) &&
                          al(adv, 16) && al(mask, 16);
     if (bulk_ok) {
-      const int bgrid = (int)std::min<int64_t>(cdiv(n, kBulkTile), (int64_t)kNumSMs * kBulkBlocksPerSM);
+      // one block more than tiles (block 0 takes the batch-level terms), at most two per SM
+      const int bgrid = (int)std::min<int64_t>(cdiv(n, kBulkTile) + 1, (int64_t)kNumSMs * kBulkBlocksPerSM);
       const uint32_t smem = kBulkStages * (bf ? bulk_stage_bytes<true>() : bulk_stage_bytes<false>());
 #define IKRL_LAUNCH_BULK(BF, KLV)                                                                      \
   do {                                                                                                \
@@ -1116,13 +1182,15 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
       if (bf) { if (kl == 0) IKRL_LAUNCH_BULK(true, 0); else if (kl == 1) IKRL_LAUNCH_BULK(true, 1); else IKRL_LAUNCH_BULK(true, 2); }
       else { if (kl == 0) IKRL_LAUNCH_BULK(false, 0); else if (kl == 1) IKRL_LAUNCH_BULK(false, 1); else IKRL_LAUNCH_BULK(false, 2); }
 #undef IKRL_LAUNCH_BULK
-      return check_launch("grpo_loss_bulk_kernel");
+      int rc = check_launch("grpo_loss_bulk_kernel");
+      return rc ? rc : launch_sums_reduce(a, token_blocks(bgrid), true, s);
     }
 #define IKRL_LAUNCH_LEAN(BF, KLV) grpo_loss_kernel<BF, KLV><<<grid, kLossThreads, 0, s>>>(a)
     if (bf) { if (kl == 0) IKRL_LAUNCH_LEAN(true, 0); else if (kl == 1) IKRL_LAUNCH_LEAN(true, 1); else IKRL_LAUNCH_LEAN(true, 2); }
     else { if (kl == 0) IKRL_LAUNCH_LEAN(false, 0); else if (kl == 1) IKRL_LAUNCH_LEAN(false, 1); else IKRL_LAUNCH_LEAN(false, 2); }
 #undef IKRL_LAUNCH_LEAN
-    return check_launch("grpo_loss_kernel");
+    int rc = check_launch("grpo_loss_kernel");
+    return rc ? rc : launch_sums_reduce(a, token_blocks(grid), true, s);
   }
 #define IKRL_LAUNCH_LOSS(FAM, BF, VEC) clip_loss_kernel<FAM, BF, VEC><<<grid, kLossThreads, 0, s>>>(a)
   if (params->family == IKRL_LOSS_GRPO) {
@@ -1133,7 +1201,8 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
     else { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, false, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, false, false); }
   }
 #undef IKRL_LAUNCH_LOSS
-  return check_launch("clip_loss_kernel");
+  int rc = check_launch("clip_loss_kernel");
+  return rc ? rc : launch_sums_reduce(a, token_blocks(grid), false, s);
 }
 
 int ikrl_clip_loss_finalize(const double* sums, const int64_t* ntok, const ikrl_loss_params* params,

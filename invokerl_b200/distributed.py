@@ -27,15 +27,86 @@ def group_shard_bounds(B: int, G: int, rank: int, world: int) -> tuple[int, int]
     return g0 * G, g1 * G
 
 
+def balanced_groups(response_mask: torch.Tensor, G: int, world: int, row_cost: float = 1.0,
+                    token_cost: float = 3.0) -> list[list[int]]:
+    """Whole groups per rank, balanced by estimated work instead of by count.
+
+    A group costs `row_cost` per row (the LM-head forward runs every row) plus `token_cost` per
+    response token (the backward runs only rows with a nonzero upstream gradient; 3 = its three
+    GEMMs against the forward's one).  Groups are placed largest first on the least-loaded rank
+    (ties: lower rank), then single moves and swaps off the most loaded rank are applied while
+    they lower its load; each rank's groups are returned in increasing order.  Deterministic, so
+    every rank computes the same assignment from the same masks."""
+    B, T = response_mask.shape
+    if G <= 0 or B % G:
+        raise ValueError(f"B={B} is not a multiple of group_size={G}")
+    ngroups = B // G
+    tok = response_mask.reshape(ngroups, G * T).sum(dim=1).tolist()
+    cost = [row_cost * G * T + token_cost * t for t in tok]
+    order = sorted(range(ngroups), key=lambda g: (-cost[g], g))
+    load = [0.0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for g in order:
+        r = min(range(world), key=lambda q: (load[q], q))
+        out[r].append(g)
+        load[r] += cost[g]
+    # Local search: move or swap a group between the most loaded rank and another while that lowers
+    # the larger of the two loads.
+    for _ in range(4 * ngroups):
+        hi = max(range(world), key=lambda q: (load[q], -q))
+        best = None
+        for lo in range(world):
+            if lo == hi:
+                continue
+            for g in out[hi]:
+                cand = [(max(load[hi] - cost[g], load[lo] + cost[g]), g, None)]
+                cand += [(max(load[hi] - cost[g] + cost[h], load[lo] - cost[h] + cost[g]), g, h) for h in out[lo]]
+                for m, a, b in cand:
+                    if m < load[hi] - 1e-9 and (best is None or m < best[0]):
+                        best = (m, lo, a, b)
+        if best is None:
+            break
+        _, lo, a, b = best
+        out[hi].remove(a)
+        out[lo].append(a)
+        load[hi] -= cost[a]
+        load[lo] += cost[a]
+        if b is not None:
+            out[lo].remove(b)
+            out[hi].append(b)
+            load[lo] -= cost[b]
+            load[hi] += cost[b]
+    return [sorted(x) for x in out]
+
+
 def shard_rows(x, start: int, end: int, B: int):
     if isinstance(x, torch.Tensor) and x.dim() >= 1 and x.shape[0] == B:
         return x[start:end]
     return x
 
 
-def shard_batch(batch: RolloutBatch, rank: int, world: int) -> RolloutBatch:
-    """This rank's whole groups of `batch` (views, no copies)."""
+def shard_batch(batch: RolloutBatch, rank: int, world: int, balance: bool = False) -> RolloutBatch:
+    """This rank's whole groups of `batch`: contiguous (views, no copies), or with balance=True the
+    groups `balanced_groups` assigns to it (copies, in group order)."""
     B = batch.token_ids.shape[0]
+    if balance:
+        G = batch.group_size
+        groups = balanced_groups(batch.response_mask, G, world)[rank]
+        idx = torch.tensor([g * G + j for g in groups for j in range(G)], dtype=torch.long)
+
+        def take(x):
+            if isinstance(x, torch.Tensor) and x.dim() >= 1 and x.shape[0] == B:
+                return x.index_select(0, idx.to(x.device))
+            return x
+
+        return RolloutBatch(
+            token_ids=take(batch.token_ids), prompt_mask=take(batch.prompt_mask),
+            response_mask=take(batch.response_mask), attention_mask=take(batch.attention_mask),
+            rewards=take(batch.rewards), token_rewards=take(batch.token_rewards),
+            old_log_probs=take(batch.old_log_probs), ref_log_probs=take(batch.ref_log_probs),
+            group_ids=take(batch.group_ids), group_size=G, weight_version=batch.weight_version,
+            extras={k: take(v) for k, v in batch.extras.items()},
+        )
     s, e = group_shard_bounds(B, batch.group_size, rank, world)
     return RolloutBatch(
         token_ids=batch.token_ids[s:e],

@@ -161,3 +161,33 @@ def test_scatter_batch_sends_each_rank_its_groups(world):
         assert torch.equal(ids, ref.token_ids) and torch.equal(rew, ref.rewards)
         assert torch.equal(rm, ref.response_mask) and torch.equal(tr, ref.extras["truncated"])
         assert note == "kept" and torch.equal(scale, torch.tensor([2.0, 3.0])) and G == 4
+
+
+def test_balanced_groups_cover_every_group_once_and_balance_work():
+    from invokerl_b200.distributed import balanced_groups
+
+    b = rollout_batch(16, 8, 512, prompt_len=(16, 64), completion_len=(32, 448), seed=5)
+    G, T = 8, 512
+    for world in (1, 2, 3, 8):
+        parts = balanced_groups(b.response_mask, G, world)
+        assert sorted(g for p in parts for g in p) == list(range(16))
+        assert parts == balanced_groups(b.response_mask, G, world)  # deterministic
+        tok = b.response_mask.reshape(16, G * T).sum(1).tolist()
+        load = [sum(G * T + 3 * tok[g] for g in p) for p in parts]
+        contiguous = [sum(G * T + 3 * tok[g] for g in range(r * 16 // world, (r + 1) * 16 // world))
+                      for r in range(world)]
+        assert max(load) <= max(contiguous) + 1e-9
+
+
+def test_balanced_shard_batch_rows_match_their_groups():
+    from invokerl_b200.distributed import balanced_groups
+
+    b = rollout_batch(6, 4, 64, prompt_len=(4, 20), completion_len=(8, 40), seed=9)
+    parts = balanced_groups(b.response_mask, 4, 2)
+    for r in range(2):
+        loc = shard_batch(b, r, 2, balance=True)
+        rows = [g * 4 + j for g in parts[r] for j in range(4)]
+        assert torch.equal(loc.token_ids, b.token_ids[rows])
+        assert torch.equal(loc.response_mask, b.response_mask[rows])
+        assert torch.equal(loc.rewards, b.rewards[rows])
+        assert loc.group_size == 4
