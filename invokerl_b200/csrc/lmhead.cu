@@ -603,11 +603,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Pacing of the persistent pairs: pairs that read the same W tiles through L2 drift apart over a
 // sweep, and a tile read by a leading pair is evicted before the trailing pairs reach it.  Each
-// pair publishes how many tiles it has started; a pair about to start tile j waits until every
-// unfinished pair has started tile j - kPaceLag.  The wait is a heuristic with a short bound:
+// pair publishes how many checkpoints it has passed (one per kPaceKb K blocks, so a long
+// reduction such as dH over the vocabulary has many per tile); a pair about to pass checkpoint j
+// waits until every unfinished pair has passed checkpoint j - kPaceLag.  The wait is a heuristic with a short bound:
 // after kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair
 // that is not resident, e.g. on a shared GPU, must not stall the others).
 constexpr int kPaceLag = 1;
+constexpr int kPaceKb = 64;  // K blocks between checkpoints (one per tile at K = 4096)
 constexpr uint64_t kPaceBoundNs = 20000;
 constexpr unsigned kPaceDone = 0xffffffffu;
 
@@ -620,8 +622,8 @@ __device__ __forceinline__ void st_relaxed_u32(unsigned* ptr, unsigned v) {
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 
-// Publish "started tile j" (j counted over all of this pair's units) and wait for the laggards.
-__device__ __forceinline__ void pace_tile(unsigned* prog, int pair_id, int npairs, int j, bool& pacing) {
+// Publish "passed checkpoint j" (counted over all of this pair's units) and wait for the laggards.
+__device__ __forceinline__ void pace_checkpoint(unsigned* prog, int pair_id, int npairs, int j, bool& pacing) {
   st_relaxed_u32(prog + pair_id, (unsigned)j + 1u);
   if (!pacing || j < kPaceLag) return;
   const unsigned need = (unsigned)(j + 1 - kPaceLag);
@@ -710,6 +712,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       bool pacing = p.lockstep != nullptr && rank == 0;
+      const int pace_steps = (nk + kPaceKb - 1) / kPaceKb;  // checkpoints per tile
       int jt = 0;
       for (int u = pair_id; u < nunits && ok; u += npairs) {
         const int split = u % p.splits;
@@ -717,8 +720,10 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         const int t_begin = split * p.tiles_per_split;
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
         for (int t = t_begin; t < t_end && ok; ++t, ++jt) {
-          if (p.lockstep != nullptr && rank == 0) pace_tile(p.lockstep, pair_id, npairs, jt, pacing);
           for (int kb = 0; kb < nk; ++kb) {
+            // pacing checkpoints: every kPaceKb K blocks (once per tile when K <= 64 * kPaceKb)
+            if (p.lockstep != nullptr && rank == 0 && kb % kPaceKb == 0)
+              pace_checkpoint(p.lockstep, pair_id, npairs, jt * pace_steps + kb / kPaceKb, pacing);
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
               ok = false;
               break;
