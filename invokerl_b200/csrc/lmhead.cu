@@ -425,6 +425,51 @@ constexpr uint32_t kPairTileB = (BN / 2) * BK * 2;  // 16 KB: this CTA's half of
 constexpr uint32_t kPairStageBytes = kTileA + kPairTileB;
 constexpr uint32_t kPairSmemBytes = kPairStages * kPairStageBytes + 1024;
 
+// Pacing of the persistent pairs: pairs that read the same W tiles through L2 drift apart over a
+// sweep, and a tile read by a leading pair is evicted before the trailing pairs reach it.  Each
+// pair publishes how many checkpoints it has passed (one per kPaceKb K blocks, so a long
+// reduction such as dH over the vocabulary has many per tile); a pair about to pass checkpoint j
+// waits until every unfinished pair has passed checkpoint j - kPaceLag.  The wait is a heuristic with a short bound:
+// after kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair
+// that is not resident, e.g. on a shared GPU, must not stall the others).
+constexpr int kPaceLag = 1;
+constexpr int kPaceKb = 64;  // K blocks between checkpoints (one per tile at K = 4096, 4 tiles at K = 1024)
+constexpr uint64_t kPaceBoundNs = 20000;
+constexpr unsigned kPaceDone = 0xffffffffu;
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* ptr) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u32(unsigned* ptr, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// Publish "passed checkpoint j" (counted over all of this pair's units) and wait for the laggards.
+__device__ __forceinline__ void pace_checkpoint(unsigned* prog, int pair_id, int npairs, int j, bool& pacing) {
+  st_relaxed_u32(prog + pair_id, (unsigned)j + 1u);
+  if (!pacing || j < kPaceLag) return;
+  const unsigned need = (unsigned)(j + 1 - kPaceLag);
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    unsigned mn = kPaceDone;
+    for (int q = 0; q < npairs; q += 8) {
+      unsigned v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (q + i < npairs) ? ld_relaxed_u32(prog + q + i) : kPaceDone;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mn = min(mn, v[i]);
+    }
+    if (mn >= need) return;
+    if (globaltimer() - t0 > kPaceBoundNs) {
+      pacing = false;
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     lmhead_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -482,14 +527,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool pacing = p.lockstep != nullptr && rank == 0;
+      int jt = 0;
       for (int u = pair_id; u < nunits && ok; u += npairs) {
         const int split = u % p.splits;
         const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
         const int t_begin = split * p.tiles_per_split;
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-        for (int t = t_begin; t < t_end && ok; ++t) {
+        for (int t = t_begin; t < t_end && ok; ++t, ++jt) {
           const int nb = t * BN + (int)rank * (BN / 2);  // this CTA's half of the N tile
           for (int kb = 0; kb < nk; ++kb) {
+            const int gkb = jt * nk + kb;
+            if (p.lockstep != nullptr && rank == 0 && gkb % kPaceKb == 0)
+              pace_checkpoint(p.lockstep, pair_id, npairs, gkb / kPaceKb, pacing);
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
               ok = false;
               break;
@@ -518,6 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (p.lockstep != nullptr && rank == 0) st_relaxed_u32(p.lockstep + pair_id, kPaceDone);
       if (ok) {
         for (int s = 0; s < kPairStages; ++s) {
           if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) break;
@@ -601,51 +652,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Pacing of the persistent pairs: pairs that read the same W tiles through L2 drift apart over a
-// sweep, and a tile read by a leading pair is evicted before the trailing pairs reach it.  Each
-// pair publishes how many checkpoints it has passed (one per kPaceKb K blocks, so a long
-// reduction such as dH over the vocabulary has many per tile); a pair about to pass checkpoint j
-// waits until every unfinished pair has passed checkpoint j - kPaceLag.  The wait is a heuristic with a short bound:
-// after kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair
-// that is not resident, e.g. on a shared GPU, must not stall the others).
-constexpr int kPaceLag = 1;
-constexpr int kPaceKb = 64;  // K blocks between checkpoints (one per tile at K = 4096)
-constexpr uint64_t kPaceBoundNs = 20000;
-constexpr unsigned kPaceDone = 0xffffffffu;
-
-__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* ptr) {
-  unsigned v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_relaxed_u32(unsigned* ptr, unsigned v) {
-  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
-}
-
-// Publish "passed checkpoint j" (counted over all of this pair's units) and wait for the laggards.
-__device__ __forceinline__ void pace_checkpoint(unsigned* prog, int pair_id, int npairs, int j, bool& pacing) {
-  st_relaxed_u32(prog + pair_id, (unsigned)j + 1u);
-  if (!pacing || j < kPaceLag) return;
-  const unsigned need = (unsigned)(j + 1 - kPaceLag);
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    unsigned mn = kPaceDone;
-    for (int q = 0; q < npairs; q += 8) {
-      unsigned v[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = (q + i < npairs) ? ld_relaxed_u32(prog + q + i) : kPaceDone;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mn = min(mn, v[i]);
-    }
-    if (mn >= need) return;
-    if (globaltimer() - t0 > kPaceBoundNs) {
-      pacing = false;
-      return;
-    }
-    __nanosleep(256);
-  }
-}
-
 // Wide CTA-pair variant for long K: the pair computes a 256 x 512 tile per K step with two
 // N=256 MMAs into all 512 TMEM columns.  Each CTA stages 128 A rows and 256 of the 512 B rows per
 // 64-deep K block (48 KB, 4 stages), so L2 and shared-memory reads per MMA flop are 3/4 of the
@@ -712,7 +718,6 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       bool pacing = p.lockstep != nullptr && rank == 0;
-      const int pace_steps = (nk + kPaceKb - 1) / kPaceKb;  // checkpoints per tile
       int jt = 0;
       for (int u = pair_id; u < nunits && ok; u += npairs) {
         const int split = u % p.splits;
@@ -721,9 +726,10 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
         for (int t = t_begin; t < t_end && ok; ++t, ++jt) {
           for (int kb = 0; kb < nk; ++kb) {
-            // pacing checkpoints: every kPaceKb K blocks (once per tile when K <= 64 * kPaceKb)
-            if (p.lockstep != nullptr && rank == 0 && kb % kPaceKb == 0)
-              pace_checkpoint(p.lockstep, pair_id, npairs, jt * pace_steps + kb / kPaceKb, pacing);
+            // pacing checkpoint every kPaceKb K blocks of this pair's work
+            const int gkb = jt * nk + kb;
+            if (p.lockstep != nullptr && rank == 0 && gkb % kPaceKb == 0)
+              pace_checkpoint(p.lockstep, pair_id, npairs, gkb / kPaceKb, pacing);
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
               ok = false;
               break;
@@ -1043,6 +1049,8 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   const bool persistent = !(pe != nullptr && pe[0] == '0');
   const int64_t npairs = std::max<int64_t>(1, persistent ? std::min<int64_t>(nunits, nsm / 2) : nunits);
   p.lockstep = nullptr;
+  // Pacing helps the wide kernel (long tiles, W re-read across pairs); on the 256 x 256 pair
+  // kernel at K = 1024 it measured 7% slower (checkpoints every 4 short tiles stall the producer).
   if (WIDE && persistent && pacing_enabled()) {
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
