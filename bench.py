@@ -756,6 +756,28 @@ def run_native(args, rank, world, device) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, kms = float(t[0]), float(t[1])
 
+    # Outside the timed region: the data-parallel reduction of the LM-head weight gradient that a
+    # DP / FSDP layer would add per step (one NCCL all-reduce of dW in its dtype), reported apart.
+    dw_allreduce = None
+    if world > 1 and isinstance(wl, LMHeadGRPO) and wl.weight.grad is not None:
+        gw = wl.weight.grad
+        for _ in range(2):
+            dist.all_reduce(gw)
+        torch.cuda.synchronize()
+        dist.barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(5):
+            dist.all_reduce(gw)
+        s1.record()
+        torch.cuda.synchronize()
+        ta = torch.tensor([s0.elapsed_time(s1) / 5], dtype=torch.float64, device=device)
+        dist.all_reduce(ta, op=dist.ReduceOp.MAX)
+        nbytes = gw.numel() * gw.element_size()
+        dw_allreduce = {"ms": float(ta[0]), "bytes": int(nbytes), "dtype": str(gw.dtype).replace("torch.", ""),
+                        "bus_gbs": 2 * (world - 1) / world * nbytes / (float(ta[0]) / 1e3) / 1e9,
+                        "note": "NCCL all-reduce of dW per step, not in the timed region"}
+
     e2e = None
     if not args.no_e2e:
         one, h2d, d2h = wl.e2e()
@@ -798,6 +820,7 @@ def run_native(args, rank, world, device) -> dict | None:
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clocks,
+        "dw_allreduce": dw_allreduce,
         "loss": loss,
     }
     if world == 1 and not args.no_cpu_baseline and not isinstance(wl, E2EGRPO):
