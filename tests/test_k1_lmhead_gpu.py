@@ -205,3 +205,30 @@ def test_all_rows_zero_gradient():
     acc = base.clone()
     _bwd(hd, wd, td, lse, g, True, want_dh=False, dweight_out=acc)
     assert torch.equal(acc, base)
+
+
+def test_forward_and_backward_capture_into_a_cuda_graph(monkeypatch):
+    """Both K1 calls can be captured into a CUDA graph: inside a capture the backward runs all
+    rows (no host read of the active count) and the replay equals the eager results."""
+    monkeypatch.setattr(ops, "_CHECK_DEVICE_STATUS", False)  # the status read synchronises
+    N, H, V = 512, 4096, 20000
+    li = lmhead_inputs(N, H, V, seed=21, w_std=0.05)
+    h, w, t = li.hidden.to(DEV), li.weight.to(DEV), li.targets.to(DEV)
+    g = (torch.randn(N, generator=torch.Generator().manual_seed(22)) * (torch.arange(N) % 2)).to(DEV)
+    lp_e, lse_e = ops.lmhead_forward_raw(h, w, t)
+    dh_e, dw_e = ops.lmhead_backward_raw(h, w, t, lse_e, g, dw_dtype=torch.float32)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):  # warm-up on the capture stream
+        ops.lmhead_forward_raw(h, w, t)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        lp_c, lse_c = ops.lmhead_forward_raw(h, w, t)
+        dh_c, dw_c = ops.lmhead_backward_raw(h, w, t, lse_c, g, dw_dtype=torch.float32)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(lp_c, lp_e) and torch.equal(lse_c, lse_e)
+    assert torch.equal(dh_c, dh_e)
+    torch.testing.assert_close(dw_c, dw_e, rtol=1e-4, atol=1e-6)
