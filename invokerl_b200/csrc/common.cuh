@@ -73,6 +73,14 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Programmatic dependent launch (sm_90+): a kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may be scheduled while the previous kernel
+// of its stream still runs; griddep_wait() blocks until that kernel has finished and its writes
+// are visible (a no-op for an ordinary launch).  griddep_launch_dependents() lets the next such
+// kernel be scheduled once every block of this grid has called it or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 

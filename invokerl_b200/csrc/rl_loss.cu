@@ -96,6 +96,8 @@ __global__ void group_adv_kernel(const float* __restrict__ rewards, const uint8_
                                  const uint8_t* __restrict__ truncated, int B, int T, int G,
                                  int filter_zero_var, float overlong_penalty, float* __restrict__ adv,
                                  float* __restrict__ row_adv) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.x;
   __shared__ float s_adv;
   // Touch this row's mask early so its loads overlap the group statistics below.
@@ -470,7 +472,8 @@ __global__ void __launch_bounds__(256) loss_sums_reduce_kernel(const double* __r
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
   // Launched as a programmatic dependent of the loss kernel: it may start while that kernel runs
   // and waits here until it has completed and its partials are visible.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  griddep_wait();
+  griddep_launch_dependents();
   double t[kTokenSums];
 #pragma unroll
   for (int i = 0; i < kTokenSums; ++i) t[i] = 0.0;
@@ -495,8 +498,10 @@ __global__ void __launch_bounds__(256) loss_sums_reduce_kernel(const double* __r
 template <int FAMILY, bool BF16, bool VEC>
 __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) clip_loss_kernel(LossArgs a) {
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
+  // Inputs may come from the previous kernel of the stream (programmatic dependent launch).
+  griddep_wait();
   // Every block has started: the sums-reduce kernel may be scheduled now (it waits for this grid).
-  asm volatile("griddepcontrol.launch_dependents;");
+  griddep_launch_dependents();
   const TokenGrid tg = token_grid();
   if (blockIdx.x == 0) write_batch_terms(a, scratch, tg.nb);
   if (tg.tb < 0) return;
@@ -621,8 +626,10 @@ __device__ __forceinline__ void grpo_finish(const LossArgs& a, const GrpoSums& a
 template <bool BF16, int KL>
 __global__ void __launch_bounds__(kLossThreads, kLossBlocksPerSM) grpo_loss_kernel(LossArgs a) {
   __shared__ double scratch[IKRL_LOSS_NSUMS * 32];
+  // Inputs may come from the previous kernel of the stream (programmatic dependent launch).
+  griddep_wait();
   // Every block has started: the sums-reduce kernel may be scheduled now (it waits for this grid).
-  asm volatile("griddepcontrol.launch_dependents;");
+  griddep_launch_dependents();
   const TokenGrid tg = token_grid();
   if (blockIdx.x == 0) write_batch_terms(a, scratch, tg.nb);
   if (tg.tb < 0) return;
@@ -694,8 +701,10 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
   constexpr uint32_t kOffOld = kLpBytes, kOffRef = kOffOld + 4 * kBulkTile, kOffAdv = kOffRef + 4 * kBulkTile,
                      kOffMask = kOffAdv + 4 * kBulkTile;
   constexpr uint32_t kStage = bulk_stage_bytes<BF16>();
+  // Inputs may come from the previous kernel of the stream (programmatic dependent launch).
+  griddep_wait();
   // Every block has started: the sums-reduce kernel may be scheduled now (it waits for this grid).
-  asm volatile("griddepcontrol.launch_dependents;");
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_full = a.n / kBulkTile;
   const int64_t n_tiles = (a.n + kBulkTile - 1) / kBulkTile;
@@ -805,6 +814,8 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkBlocksPerSM) grpo_loss_bulk
 __global__ void clip_loss_finalize_kernel(const double* __restrict__ s, const int64_t* __restrict__ ntok,
                                           ikrl_loss_params p, float* __restrict__ loss_out,
                                           float* __restrict__ metrics) {
+  griddep_wait();
+  griddep_launch_dependents();
   if (threadIdx.x != 0) return;
   const double n = fmax((double)(float)(*ntok), 1.0);
   const float nf = (float)n;
@@ -837,6 +848,8 @@ __global__ void clip_loss_finalize_kernel(const double* __restrict__ s, const in
 
 template <bool BF16>
 __global__ void scale_grad_kernel(void* g, int64_t n, const float* __restrict__ scale) {
+  griddep_wait();
+  griddep_launch_dependents();
   const float s = *scale;
   if (s == 1.f) return;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -1002,26 +1015,31 @@ int lean_loss_mode() {
   return 1;
 }
 
-// The fixed-order combine of the loss kernel's per-block partials (and its batch-level slot).
-int launch_sums_reduce(const LossArgs& a, int nblocks, bool derive_token_loss, cudaStream_t s) {
-  // Programmatic dependent launch: the one-block reduce is scheduled while the loss kernel still
-  // runs (hiding its launch latency) and waits in-kernel for the loss kernel to finish.
+// Launch with programmatic stream serialization: the kernel may be scheduled while the previous
+// kernel of the stream runs (its launch latency overlaps that kernel's tail); it calls
+// griddep_wait() before touching memory.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, const char* name,
+               Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1, 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const double* partials = a.partials;
-  const int derive = derive_token_loss ? 1 : 0;
-  const float beta = a.p.beta;
-  const int B = a.B, G = a.G;
-  double* sums = a.sums;
-  IKRL_CUDA(cudaLaunchKernelEx(&cfg, loss_sums_reduce_kernel, partials, nblocks, derive, beta, B, G, sums));
-  return check_launch("loss_sums_reduce_kernel");
+  IKRL_CUDA(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+  return check_launch(name);
+}
+
+// The fixed-order combine of the loss kernel's per-block partials (and its batch-level slot).
+int launch_sums_reduce(const LossArgs& a, int nblocks, bool derive_token_loss, cudaStream_t s) {
+  // The one-block reduce is scheduled while the loss kernel still runs and waits in-kernel for it.
+  return launch_pdl(loss_sums_reduce_kernel, dim3(1), dim3(256), 0, s, "loss_sums_reduce_kernel",
+                    (const double*)a.partials, nblocks, derive_token_loss ? 1 : 0, a.p.beta, a.B, a.G, a.sums);
 }
 
 int loss_grid(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(cdiv(n, 4), kLossThreads), kLossMaxBlocks)); }
@@ -1066,9 +1084,8 @@ int ikrl_group_advantages(const float* rewards, const uint8_t* response_mask, co
   if (B == 0) return IKRL_OK;
   IKRL_REQUIRE(rewards && response_mask && adv_out, IKRL_ERR_INVALID_ARGUMENT,
                "ikrl_group_advantages: null pointer");
-  group_adv_kernel<<<B, 256, 0, as_stream(stream)>>>(rewards, response_mask, truncated, B, T, G,
-                                                    filter_zero_var, overlong_penalty, adv_out, row_adv_out);
-  return check_launch("group_adv_kernel");
+  return launch_pdl(group_adv_kernel, dim3(B), dim3(256), 0, as_stream(stream), "group_adv_kernel", rewards,
+                    response_mask, truncated, B, T, G, filter_zero_var, overlong_penalty, adv_out, row_adv_out);
 }
 
 int ikrl_token_group_advantages(const float* token_rewards, const uint8_t* response_mask, int32_t B,
@@ -1173,26 +1190,30 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
       // one block more than tiles (block 0 takes the batch-level terms), at most two per SM
       const int bgrid = (int)std::min<int64_t>(cdiv(n, kBulkTile) + 1, (int64_t)kNumSMs * kBulkBlocksPerSM);
       const uint32_t smem = kBulkStages * (bf ? bulk_stage_bytes<true>() : bulk_stage_bytes<false>());
+      int rc = 0;
 #define IKRL_LAUNCH_BULK(BF, KLV)                                                                      \
   do {                                                                                                \
     IKRL_CUDA(cudaFuncSetAttribute(grpo_loss_bulk_kernel<BF, KLV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                    (int)smem));                                                       \
-    grpo_loss_bulk_kernel<BF, KLV><<<bgrid, kBulkThreads, smem, s>>>(a);                              \
+    rc = launch_pdl(grpo_loss_bulk_kernel<BF, KLV>, dim3(bgrid), dim3(kBulkThreads), smem, s,          \
+                    "grpo_loss_bulk_kernel", a);                                                      \
   } while (0)
       if (bf) { if (kl == 0) IKRL_LAUNCH_BULK(true, 0); else if (kl == 1) IKRL_LAUNCH_BULK(true, 1); else IKRL_LAUNCH_BULK(true, 2); }
       else { if (kl == 0) IKRL_LAUNCH_BULK(false, 0); else if (kl == 1) IKRL_LAUNCH_BULK(false, 1); else IKRL_LAUNCH_BULK(false, 2); }
 #undef IKRL_LAUNCH_BULK
-      int rc = check_launch("grpo_loss_bulk_kernel");
       return rc ? rc : launch_sums_reduce(a, token_blocks(bgrid), true, s);
     }
-#define IKRL_LAUNCH_LEAN(BF, KLV) grpo_loss_kernel<BF, KLV><<<grid, kLossThreads, 0, s>>>(a)
+    int rc = 0;
+#define IKRL_LAUNCH_LEAN(BF, KLV) \
+  rc = launch_pdl(grpo_loss_kernel<BF, KLV>, dim3(grid), dim3(kLossThreads), 0, s, "grpo_loss_kernel", a)
     if (bf) { if (kl == 0) IKRL_LAUNCH_LEAN(true, 0); else if (kl == 1) IKRL_LAUNCH_LEAN(true, 1); else IKRL_LAUNCH_LEAN(true, 2); }
     else { if (kl == 0) IKRL_LAUNCH_LEAN(false, 0); else if (kl == 1) IKRL_LAUNCH_LEAN(false, 1); else IKRL_LAUNCH_LEAN(false, 2); }
 #undef IKRL_LAUNCH_LEAN
-    int rc = check_launch("grpo_loss_kernel");
     return rc ? rc : launch_sums_reduce(a, token_blocks(grid), true, s);
   }
-#define IKRL_LAUNCH_LOSS(FAM, BF, VEC) clip_loss_kernel<FAM, BF, VEC><<<grid, kLossThreads, 0, s>>>(a)
+  int rc = 0;
+#define IKRL_LAUNCH_LOSS(FAM, BF, VEC) \
+  rc = launch_pdl(clip_loss_kernel<FAM, BF, VEC>, dim3(grid), dim3(kLossThreads), 0, s, "clip_loss_kernel", a)
   if (params->family == IKRL_LOSS_GRPO) {
     if (bf) { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, true, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, true, false); }
     else { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, false, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_GRPO, false, false); }
@@ -1201,7 +1222,6 @@ int ikrl_clip_loss_fwd(const void* new_lp, int32_t lp_dtype, const float* old_lp
     else { if (vec) IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, false, true); else IKRL_LAUNCH_LOSS(IKRL_LOSS_PPO, false, false); }
   }
 #undef IKRL_LAUNCH_LOSS
-  int rc = check_launch("clip_loss_kernel");
   return rc ? rc : launch_sums_reduce(a, token_blocks(grid), false, s);
 }
 
@@ -1210,8 +1230,8 @@ int ikrl_clip_loss_finalize(const double* sums, const int64_t* ntok, const ikrl_
   clear_error();
   IKRL_REQUIRE(sums && ntok && params && loss_out && metrics_out, IKRL_ERR_INVALID_ARGUMENT,
                "ikrl_clip_loss_finalize: bad arguments");
-  clip_loss_finalize_kernel<<<1, 32, 0, as_stream(stream)>>>(sums, ntok, *params, loss_out, metrics_out);
-  return check_launch("clip_loss_finalize_kernel");
+  return launch_pdl(clip_loss_finalize_kernel, dim3(1), dim3(32), 0, as_stream(stream), "clip_loss_finalize_kernel",
+                    sums, ntok, *params, loss_out, metrics_out);
 }
 
 int ikrl_scale_grad(void* g, int32_t dtype, int64_t n, const float* scale, void* stream) {
@@ -1221,9 +1241,11 @@ int ikrl_scale_grad(void* g, int32_t dtype, int64_t n, const float* scale, void*
                "ikrl_scale_grad: dtype %d unsupported", dtype);
   if (n == 0) return IKRL_OK;
   const int grid = (int)std::min<int64_t>(kNumSMs * 8, cdiv(n, 256));
-  if (dtype == IKRL_DTYPE_BF16) scale_grad_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(g, n, scale);
-  else scale_grad_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(g, n, scale);
-  return check_launch("scale_grad_kernel");
+  if (dtype == IKRL_DTYPE_BF16)
+    return launch_pdl(scale_grad_kernel<true>, dim3(grid), dim3(256), 0, as_stream(stream), "scale_grad_kernel", g, n,
+                      scale);
+  return launch_pdl(scale_grad_kernel<false>, dim3(grid), dim3(256), 0, as_stream(stream), "scale_grad_kernel", g, n,
+                    scale);
 }
 
 size_t ikrl_simpo_workspace_bytes(int32_t B) { return (size_t)(B > 0 ? B : 0) * 2 * sizeof(float) + 256; }
