@@ -1051,7 +1051,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   p.lockstep = nullptr;
   // Pacing helps the wide kernel (long tiles, W re-read across pairs); on the 256 x 256 pair
   // kernel at K = 1024 it measured 7% slower (checkpoints every 4 short tiles stall the producer).
-  if (WIDE && persistent && pacing_enabled()) {
+  if (WIDE && persistent && npairs <= kMaxPacedPairs && pacing_enabled()) {
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
     IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));
