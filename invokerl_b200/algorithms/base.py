@@ -73,6 +73,30 @@ class BaseAlgorithm(ABC):
             torch.distributed.all_reduce(sums, group=self.process_group)
         return sums
 
+    def _global_moments(self, w: Tensor) -> Tensor:
+        """[mean, unbiased std, count, enabled] over the whole batch from each rank's own
+        (`ops.masked_moments`): one all-gather of (count, count * mean, M2) per rank, combined with
+        the pairwise update of Chan et al. (M2 = sum M2_r + sum n_r (mean_r - mean)^2) in fp64."""
+        if not self._sharded():
+            return w
+        import torch.distributed as dist
+
+        w64 = w.double()
+        n = w64[2]
+        mean = torch.where(n > 0, w64[0], torch.zeros_like(n))
+        m2 = torch.where(n > 1, w64[1] * w64[1] * (n - 1), torch.zeros_like(n))
+        local = torch.stack([n, n * mean, m2])
+        parts = [torch.empty_like(local) for _ in range(dist.get_world_size(self.process_group))]
+        dist.all_gather(parts, local, group=self.process_group)
+        allp = torch.stack(parts)
+        nt = allp[:, 0].sum()
+        mean_g = allp[:, 1].sum() / nt.clamp(min=1.0)
+        means = torch.where(allp[:, 0] > 0, allp[:, 1] / allp[:, 0].clamp(min=1.0), mean_g)
+        m2_g = allp[:, 2].sum() + (allp[:, 0] * (means - mean_g) ** 2).sum()
+        on = nt > 1
+        std_g = torch.where(on, torch.sqrt(m2_g / (nt - 1).clamp(min=1.0)), torch.full_like(nt, float("nan")))
+        return torch.stack([mean_g, std_g, nt, on.double()]).float()
+
     # -- credit assignment -------------------------------------------------------------------
 
     def compute_advantages(self, batch: RolloutBatch) -> Tensor:

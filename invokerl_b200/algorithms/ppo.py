@@ -39,8 +39,6 @@ class PPO(BaseAlgorithm):
         self.gae_gamma = gae_gamma
         self.gae_lambda = gae_lambda
         self.beta = beta
-        if self.row_sharded:
-            raise NotImplementedError("PPO row sharding needs global whitening moments; not provided")
 
     def compute_advantages(self, batch: RolloutBatch) -> Tensor:
         values = batch.extras.get("values")
@@ -62,7 +60,8 @@ class PPO(BaseAlgorithm):
     def compute_loss(self, new_log_probs: Tensor, batch: RolloutBatch, advantages: Tensor):
         params = self._params()
         ntok = self._global_token_count(batch.response_mask)
-        whiten = ops.masked_moments(advantages, batch.response_mask)
+        # advantage whitening over the whole batch's masked tokens (all ranks when row-sharded)
+        whiten = self._global_moments(ops.masked_moments(advantages, batch.response_mask))
         values = batch.extras.get("values")
         old_values = batch.extras.get("old_values")
         if values is None or old_values is None:
@@ -72,7 +71,7 @@ class PPO(BaseAlgorithm):
             batch.response_mask, batch.rewards, 0, params, ntok=ntok, whiten=whiten, values=values,
             old_values=old_values,
         )
-        _, mt = ops.clip_loss_finalize(sums, ntok, params)
+        _, mt = ops.clip_loss_finalize(self._global_sums(sums), ntok, params)
         m = mt.tolist()
         metrics = {
             "loss": m[0],

@@ -191,3 +191,55 @@ def test_balanced_shard_batch_rows_match_their_groups():
         assert torch.equal(loc.response_mask, b.response_mask[rows])
         assert torch.equal(loc.rewards, b.rewards[rows])
         assert loc.group_size == 4
+
+
+# ---- PPO whitening moments over gloo ranks ----------------------------------------------------
+
+
+def _moments_worker(rank, world, port, q, counts):
+    import datetime
+
+    from invokerl_b200.algorithms import PPO
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(100 + rank)
+        x = 3.0 + 2.0 * torch.randn(max(counts) + 5, generator=g)
+        m = torch.zeros_like(x, dtype=torch.bool)
+        m[: counts[rank]] = True
+        xm = x[m]
+        n = xm.numel()
+        # what ops.masked_moments returns on the device: [mean, unbiased std, count, enabled]
+        w = torch.tensor([xm.mean() if n else 0.0, xm.std() if n > 1 else float("nan"), float(n),
+                          1.0 if n > 1 else 0.0], dtype=torch.float32)
+        out = PPO(row_sharded=True)._global_moments(w)
+        alls = [torch.zeros(max(counts) + 5) for _ in counts]
+        dist.all_gather(alls, x)
+        if rank == 0:
+            q.put((out, torch.cat([a[:c] for a, c in zip(alls, counts)])))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("counts", [(37, 55), (1, 80), (0, 12), (1, 0)])
+def test_ppo_whitening_moments_combine_over_ranks_gloo(counts):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_moments_worker, args=(r, world, port, q, counts)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out, allx = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n = allx.numel()
+    assert float(out[2]) == n
+    if n > 1:
+        assert float(out[3]) == 1.0
+        torch.testing.assert_close(out[0], allx.double().mean().float(), rtol=1e-6, atol=1e-6)
+        torch.testing.assert_close(out[1], allx.double().std().float(), rtol=1e-5, atol=1e-6)
+    else:
+        assert float(out[3]) == 0.0

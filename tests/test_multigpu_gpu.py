@@ -151,3 +151,65 @@ def test_two_rank_vocab_parallel_head_matches_oracle():
     rel = lambda a, c: float((a.float() - c.float()).norm() / c.float().norm())  # noqa: E731
     assert rel(dh, dh_o) <= 1e-2
     assert rel(dw, dw_o) <= 1e-2
+
+
+def _ppo_worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from helpers import load, make_batch
+    from invokerl_b200.algorithms import PPO
+    from invokerl_b200.distributed import shard_batch
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        g = load("ppo_values")
+        b = make_batch(g["batch"], dev)
+        local = shard_batch(b, rank, world)
+        nl = shard_batch(type(b)(**{**vars(b), "extras": {"nl": g["new_lp"].to(dev)}}), rank, world).extras["nl"]
+        algo = PPO(row_sharded=True, **g["kwargs"])
+        adv = algo.compute_advantages(local)
+        lp = nl.clone().requires_grad_(True)
+        loss, metrics = algo.compute_loss(lp, local, adv)
+        loss.backward()
+        tot = loss.detach().clone()
+        dist.all_reduce(tot)
+        grads = [torch.empty_like(lp.grad) for _ in range(world)]
+        dist.all_gather(grads, lp.grad.contiguous())
+        if rank == 0:
+            q.put((float(tot), metrics, torch.cat(grads).cpu()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_ppo_with_global_whitening_matches_reference_golden():
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from helpers import assert_metrics_close, load
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_ppo_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    tot, metrics, grad = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    out = load("ppo_values")["out"]
+    assert abs(tot - float(out["loss"])) <= 1e-4 * abs(float(out["loss"])) + 1e-6
+    assert_metrics_close(metrics, out["metrics"], rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(grad, out["grad"].float(), rtol=1e-4, atol=1e-7)
