@@ -73,6 +73,22 @@ class BaseAlgorithm(ABC):
             torch.distributed.all_reduce(sums, group=self.process_group)
         return sums
 
+    def _pair_share(self, loss: Tensor, metrics: Tensor, rows: int) -> tuple[Tensor, Tensor]:
+        """Pairwise losses (SimPO, DPO) over row shards of whole pairs: the loss and every metric are
+        means over pairs, so this rank's loss becomes its share (local mean x local pairs / global
+        pairs, which scales its gradient the same way) and the metrics become the global means
+        (one all-reduce of the pair count, one of the pair-weighted metrics)."""
+        if not self._sharded():
+            return loss, metrics
+        import torch.distributed as dist
+
+        p_local = rows // 2
+        p = torch.tensor([float(p_local)], dtype=torch.float64, device=metrics.device)
+        dist.all_reduce(p, group=self.process_group)
+        mt = metrics.double() * p_local
+        dist.all_reduce(mt, group=self.process_group)
+        return loss * (p_local / float(p.item())), (mt / p).float()
+
     def _global_moments(self, w: Tensor) -> Tensor:
         """[mean, unbiased std, count, enabled] over the whole batch from each rank's own
         (`ops.masked_moments`): one all-gather of (count, count * mean, M2) per rank, combined with

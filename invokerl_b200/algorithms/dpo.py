@@ -25,6 +25,7 @@ class DPO(BaseAlgorithm):
     def compute_loss(self, new_log_probs: Tensor, batch: RolloutBatch, advantages: Tensor):
         loss, mt = ops.dpo_loss(new_log_probs, batch.ref_log_probs, batch.response_mask, batch.rewards, self.beta,
                                 self.label_smoothing, self.chosen_first)
+        loss, mt = self._pair_share(loss, mt, new_log_probs.shape[0])
         m = mt.tolist()
         metrics = {
             "loss": m[0],
