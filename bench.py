@@ -40,6 +40,12 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# Keep stdout to the one JSON line: NCCL prints its version banner to stdout at the VERSION and
+# WARN debug levels, so those (and an unset level) become NONE; INFO / TRACE are left for
+# debugging.  Set before torch loads NCCL.
+if os.environ.get("NCCL_DEBUG", "VERSION").upper() in ("VERSION", "WARN"):
+    os.environ["NCCL_DEBUG"] = "NONE"
+
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
@@ -561,6 +567,18 @@ class GRPOHooks:
 
 
 
+def init_single_rank_group(device) -> None:
+    """A one-rank NCCL process group (FSDP needs one) when not launched under torchrun."""
+    if dist.is_initialized():
+        return
+    import socket
+
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1, device_id=device)
+
+
 class E2EGRPO:
     """One GRPO training step of a random-init Qwen3-0.6B (28 layers, H=1024, 16 q / 8 kv heads of
     128, SwiGLU 3072, V=151936, tied, bf16, sdpa attention, gradient checkpointing as the
@@ -573,6 +591,7 @@ class E2EGRPO:
 
     def __init__(self, key, args):
         self.key = key
+        self.fsdp = bool(getattr(args, "fsdp", False))
         if args.batch:
             if args.batch % self.G:
                 raise SystemExit(f"--batch must be a multiple of the group size {self.G}")
@@ -607,6 +626,21 @@ class E2EGRPO:
         return model
 
     @staticmethod
+    def wrap_fsdp(model, device):
+        """FSDP as invokerl's PolicyModel.fsdp() / distributed.wrap_fsdp set it up
+        (distributed.py:100-160): FULL_SHARD, one unit per decoder layer, original parameters."""
+        import functools
+
+        from torch.distributed.fsdp import FullyShardedDataParallel as FSDP
+        from torch.distributed.fsdp import ShardingStrategy
+        from torch.distributed.fsdp.wrap import transformer_auto_wrap_policy
+        from transformers.models.qwen3.modeling_qwen3 import Qwen3DecoderLayer
+
+        policy = functools.partial(transformer_auto_wrap_policy, transformer_layer_cls={Qwen3DecoderLayer})
+        return FSDP(model, sharding_strategy=ShardingStrategy.FULL_SHARD, auto_wrap_policy=policy,
+                    device_id=device, use_orig_params=True)
+
+    @staticmethod
     def model_flops_per_token(cfg, T) -> float:
         """6 x matmul parameters (LM head included) + causal attention (QK^T and AV, fwd + bwd);
         the checkpointing recompute is not counted."""
@@ -624,7 +658,11 @@ class E2EGRPO:
         from invokerl_b200.synthetic import rollout_batch
 
         self.model = self.build_model(device)
-        self.policy = PolicyModel.from_model(self.model, device=device)
+        self.cfg = self.model.config
+        if self.fsdp:
+            init_single_rank_group(device)
+            self.model = self.wrap_fsdp(self.model, device)
+        self.policy = PolicyModel.from_model(self.model, device=device, fsdp_wrapped=self.fsdp)
         b = rollout_batch(self.B // self.G, self.G, self.T, prompt_len=(64, 256), completion_len=(32, 256),
                           vocab=V, seed=0)
         local = shard_batch(b, rank, world)
@@ -657,8 +695,10 @@ class E2EGRPO:
         adv = self.algo.compute_advantages(batch)
         lp = self.policy.forward(batch.token_ids, batch.attention_mask)
         loss, metrics = self.algo.compute_loss(lp, batch, adv)
-        loss.backward()
-        if self.world > 1:
+        # Row-sharded losses are shares of the global loss, so the rank gradients must be summed;
+        # FSDP averages them over the ranks, hence the factor.
+        (loss * self.world if (self.fsdp and self.world > 1) else loss).backward()
+        if self.world > 1 and not self.fsdp:
             self._reduce_grads()
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
@@ -674,11 +714,11 @@ class E2EGRPO:
         return {}
 
     def step_roofline(self, ms_per_step, kernel_ms_per_step, peaks, peak_src):
-        fpt = self.model_flops_per_token(self.model.config, self.T)
+        fpt = self.model_flops_per_token(self.cfg, self.T)
         flops = fpt * self.B * self.T / max(1, self.world)
         achieved = flops / (ms_per_step / 1e3) / 1e12
         peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-        H = self.model.config.hidden_size
+        H = self.cfg.hidden_size
         n_rows = self.dev_batch.token_ids.numel()
         head_tf = 6.0 * n_rows * H * V / (kernel_ms_per_step / 1e3) / 1e12 if kernel_ms_per_step > 0 else None
         return {"kernel": "whole GRPO step (HF transformer + fused LM-head log-prob + K3 loss + AdamW); MFU",
@@ -694,7 +734,9 @@ class E2EGRPO:
         return {"workload": "GRPO train step, random-init Qwen3-0.6B (28 layers, H=1024, tied V=151936, bf16, "
                             "sdpa, gradient checkpointing) + AdamW; log-probs via the fused LM-head kernel",
                 "global_batch": self.B, "seq_len": self.T, "group_size": self.G,
-                "parallelism": f"dp{world} (row shards of whole groups; gradient all-reduce)",
+                "parallelism": (f"fsdp{world} (FULL_SHARD per decoder layer; materialised logits + the "
+                                "logits kernel, as invokerl's FSDP branch)") if self.fsdp else
+                               f"dp{world} (row shards of whole groups; gradient all-reduce)",
                 "l2": "activations and weights far larger than L2, no flush"}
 
     def e2e(self):
@@ -936,9 +978,13 @@ def run_reference_gpu_e2e(args, device) -> dict:
 
     wl = E2EGRPO(args.workload, args)
     model = E2EGRPO.build_model(device)
+    cfg = model.config
+    if wl.fsdp:
+        init_single_rank_group(device)
+        model = E2EGRPO.wrap_fsdp(model, device)
     pm = RefPolicy.__new__(RefPolicy)
     pm.model, pm.device, pm.dtype = model, device, torch.bfloat16
-    pm.master_weights_fp32, pm._autocast_dtype, pm._fsdp_wrapped = False, None, False
+    pm.master_weights_fp32, pm._autocast_dtype, pm._fsdp_wrapped = False, None, wl.fsdp
     b = rollout_batch(wl.B // wl.G, wl.G, wl.T, prompt_len=(64, 256), completion_len=(32, 256), vocab=V, seed=0)
     ids, am = b.token_ids.to(device), b.attention_mask.to(device)
     with torch.no_grad():
@@ -961,9 +1007,15 @@ def run_reference_gpu_e2e(args, device) -> dict:
         opt.step()
         opt.zero_grad(set_to_none=True)
 
-    for _ in range(max(1, args.warmup - 1)):
-        step()
-    torch.cuda.synchronize()
+    try:
+        for _ in range(max(1, args.warmup - 1)):
+            step()
+        torch.cuda.synchronize()
+    except torch.cuda.OutOfMemoryError as e:
+        return {"metric": METRIC, "impl": "reference-gpu", "value": None, "unit": UNIT,
+                "unavailable": f"OOM in invokerl's own step ({'FSDP materialised logits' if wl.fsdp else 'chunked'}"
+                               f" path): {str(e).splitlines()[0][:160]}",
+                "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = max(1, min(args.steps, 3))
     s.record()
@@ -972,7 +1024,7 @@ def run_reference_gpu_e2e(args, device) -> dict:
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / n
-    fpt = E2EGRPO.model_flops_per_token(model.config, wl.T)
+    fpt = E2EGRPO.model_flops_per_token(cfg, wl.T)
     peaks, _ = load_peaks()
     achieved = fpt * wl.B * wl.T / (ms / 1e3) / 1e12
     return {"metric": METRIC, "impl": "reference-gpu", "value": wl.B * wl.T / (ms / 1e3), "unit": UNIT,
@@ -995,6 +1047,9 @@ def main() -> int:
     ap.add_argument("--rows", type=int, default=0, help="override the rows of the logits workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fsdp", action="store_true",
+                    help="e2e-0.6b: wrap the model in FSDP as invokerl's PolicyModel.fsdp() does (per-layer "
+                         "FULL_SHARD); the log-prob path then takes the materialised-logits branch")
     ap.add_argument("--reference-gpu", action="store_true",
                     help="time the reference's own GPU path (baseline/_ref) instead; one extra JSON line")
     args = ap.parse_args()
@@ -1011,10 +1066,9 @@ def main() -> int:
     if args.reference_gpu:
         if rank == 0:
             print(json.dumps(run_reference_gpu(args, device)), flush=True)
+        if dist.is_initialized():
+            dist.destroy_process_group()
         return 0
-    # Keep stdout to the one JSON line: NCCL's version banner would otherwise precede it.
-    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-        os.environ["NCCL_DEBUG"] = "WARN"
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
@@ -1022,7 +1076,7 @@ def main() -> int:
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:
-        if world > 1:
+        if dist.is_initialized():  # torchrun ranks, or the one-rank group of --fsdp
             dist.barrier()
             dist.destroy_process_group()
     return 0

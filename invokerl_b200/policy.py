@@ -65,10 +65,14 @@ class PolicyModel:
                else contextlib.nullcontext())
         with ctx:
             if self._fsdp_wrapped:
-                logits = self.model(input_ids=token_ids, attention_mask=attention_mask).logits[:, :-1, :]
+                logits = self.model(input_ids=token_ids, attention_mask=attention_mask).logits
                 if logits.dtype != torch.bfloat16:
                     logits = logits.to(torch.bfloat16)
-                log_probs = ops.logits_logprob(logits, token_ids[:, 1:])
+                # All T positions as rows of the [B*T, V] logits (a view, no copy of the slice
+                # logits[:, :-1]); the last position has no target (-100, log-prob -0.0, no gradient).
+                targets = torch.full_like(token_ids, -100)
+                targets[:, :-1] = token_ids[:, 1:]
+                log_probs = ops.logits_logprob(logits, targets)[:, :-1]
                 pad = torch.zeros(token_ids.shape[0], 1, device=log_probs.device, dtype=log_probs.dtype)
                 return torch.cat([pad, log_probs], dim=1)
             hidden = self.model.model(input_ids=token_ids, attention_mask=attention_mask).last_hidden_state
