@@ -528,6 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       bool pacing = p.lockstep != nullptr && rank == 0;
+      const uint64_t pol_a = l2_policy(p.a_policy);
+      const uint64_t pol_b = l2_policy(p.b_policy);
       int jt = 0;
       for (int u = pair_id; u < nunits && ok; u += npairs) {
         const int split = u % p.splits;
@@ -551,18 +553,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_dst = a_dst + kTileA;
             const int k0 = kb * BK;
             if constexpr (!A_MN) {
-              tma_load_2d_pair(a_dst, &tmA, fb_leader, k0, m0);
+              tma_load_2d_pair_hint(a_dst, &tmA, fb_leader, k0, m0, pol_a);
             } else {
 #pragma unroll
               for (int c = 0; c < BM / 64; ++c)
-                tma_load_2d_pair(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0);
+                tma_load_2d_pair_hint(a_dst + c * kMnAtomBytes, &tmA, fb_leader, m0 + 64 * c, k0, pol_a);
             }
             if constexpr (!B_MN) {
-              tma_load_2d_pair(b_dst, &tmB, fb_leader, k0, nb);
+              tma_load_2d_pair_hint(b_dst, &tmB, fb_leader, k0, nb, pol_b);
             } else {
 #pragma unroll
               for (int c = 0; c < BN / 128; ++c)
-                tma_load_2d_pair(b_dst + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0);
+                tma_load_2d_pair_hint(b_dst + c * kMnAtomBytes, &tmB, fb_leader, nb + 64 * c, k0, pol_b);
             }
             if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
           }
@@ -1131,7 +1133,8 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
     // 2 evict-first).  Default "10": A (re-read by every tile of a unit) evict-last, B normal;
     // evict-first on B measured 40% more DRAM traffic.
     const char* e = getenv("INVOKERL_B200_L2_HINT");
-    p.a_policy = 1; p.b_policy = 0;
+    p.a_policy = kind == 2 ? 1 : 0;
+    p.b_policy = 0;
     if (e != nullptr && e[0] >= '0' && e[0] <= '2') {
       p.a_policy = e[0] - '0';
       if (e[1] >= '0' && e[1] <= '2') p.b_policy = e[1] - '0';
