@@ -71,6 +71,7 @@ struct GemmParams {
   int a_policy, b_policy; // L2 eviction priority of the A / B loads: 0 normal, 1 evict-last, 2 evict-first
   unsigned* lockstep;     // [npairs] tiles started per pair (zeroed per launch), or null: no pacing
   int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
+  int pace_kb, pace_lag;  // pacing: K blocks between checkpoints, checkpoints a pair may lead by
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
@@ -447,10 +448,11 @@ __device__ __forceinline__ void st_relaxed_u32(unsigned* ptr, unsigned v) {
 }
 
 // Publish "passed checkpoint j" (counted over all of this pair's units) and wait for the laggards.
-__device__ __forceinline__ void pace_checkpoint(unsigned* prog, int pair_id, int npairs, int j, bool& pacing) {
+__device__ __forceinline__ void pace_checkpoint(unsigned* prog, int pair_id, int npairs, int j, int lag,
+                                                bool& pacing) {
   st_relaxed_u32(prog + pair_id, (unsigned)j + 1u);
-  if (!pacing || j < kPaceLag) return;
-  const unsigned need = (unsigned)(j + 1 - kPaceLag);
+  if (!pacing || j < lag) return;
+  const unsigned need = (unsigned)(j + 1 - lag);
   const uint64_t t0 = globaltimer();
   while (true) {
     unsigned mn = kPaceDone;
@@ -540,8 +542,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nb = t * BN + (int)rank * (BN / 2);  // this CTA's half of the N tile
           for (int kb = 0; kb < nk; ++kb) {
             const int gkb = jt * nk + kb;
-            if (p.lockstep != nullptr && rank == 0 && gkb % kPaceKb == 0)
-              pace_checkpoint(p.lockstep, pair_id, npairs, gkb / kPaceKb, pacing);
+            if (p.lockstep != nullptr && rank == 0 && gkb % p.pace_kb == 0)
+              pace_checkpoint(p.lockstep, pair_id, npairs, gkb / p.pace_kb, p.pace_lag, pacing);
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
               ok = false;
               break;
@@ -730,8 +732,8 @@ __global__ void __launch_bounds__(kWideThreads, 1)
           for (int kb = 0; kb < nk; ++kb) {
             // pacing checkpoint every kPaceKb K blocks of this pair's work
             const int gkb = jt * nk + kb;
-            if (p.lockstep != nullptr && rank == 0 && gkb % kPaceKb == 0)
-              pace_checkpoint(p.lockstep, pair_id, npairs, gkb / kPaceKb, pacing);
+            if (p.lockstep != nullptr && rank == 0 && gkb % p.pace_kb == 0)
+              pace_checkpoint(p.lockstep, pair_id, npairs, gkb / p.pace_kb, p.pace_lag, pacing);
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
               ok = false;
               break;
@@ -1057,6 +1059,10 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
     IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));
+    p.pace_kb = kPaceKb;
+    p.pace_lag = kPaceLag;
+    if (const char* e = getenv("INVOKERL_B200_PACE_KB")) p.pace_kb = std::max(1, atoi(e));
+    if (const char* e = getenv("INVOKERL_B200_PACE_LAG")) p.pace_lag = std::max(0, atoi(e));
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * npairs), 1, 1);
