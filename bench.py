@@ -915,11 +915,13 @@ def run_reference_gpu(args, device) -> dict:
     ref_root = ROOT / "baseline" / "_ref"
     if not (ref_root / "invokerl" / "policy.py").exists():
         return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
-    if args.workload not in LMHeadGRPO.PRESETS and args.workload != "e2e-0.6b":
+    if args.workload not in LMHeadGRPO.PRESETS and args.workload not in ("e2e-0.6b", "grpo", "grpo-hbm"):
         return {"impl": "reference-gpu", "unavailable": f"no GPU reference leg for workload {args.workload}"}
     sys.path.insert(0, str(ref_root))
     if args.workload == "e2e-0.6b":
         return run_reference_gpu_e2e(args, device)
+    if args.workload in ("grpo", "grpo-hbm"):
+        return run_reference_gpu_hooks(args, device)
     from invokerl.algorithms import GRPO as RefGRPO
     from invokerl.algorithms import RolloutBatch as RefBatch
     from invokerl.policy import PolicyModel as RefPolicy
@@ -965,6 +967,44 @@ def run_reference_gpu(args, device) -> dict:
             "steps": n, "config": {"workload": LMHeadGRPO.PRESETS[args.workload]["name"] + ", invokerl's own "
                                    "chunked F.linear + cross_entropy path and GRPO on the same GPU"},
             "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
+
+
+def run_reference_gpu_hooks(args, device) -> dict:
+    """invokerl's own GRPO compute_advantages + compute_loss + backward (its eager ATen ops and
+    metric .item() calls) on the same device batch as the grpo workloads."""
+    from invokerl.algorithms import GRPO as RefGRPO
+    from invokerl.algorithms import RolloutBatch as RefBatch
+
+    wl = GRPOHooks(args.workload, args)
+    wl.setup(0, 1, device)
+    db = wl.dev_batch
+    rb = RefBatch(token_ids=db.token_ids, prompt_mask=db.prompt_mask, response_mask=db.response_mask,
+                  attention_mask=db.attention_mask, rewards=db.rewards, token_rewards=None,
+                  old_log_probs=db.old_log_probs, ref_log_probs=db.ref_log_probs, group_ids=db.group_ids,
+                  group_size=db.group_size)
+    algo = RefGRPO(clip_eps=0.2, beta=0.04)
+    lp0 = wl.lp.detach()
+
+    def step():
+        lp = lp0.clone().requires_grad_(True)
+        adv = algo.compute_advantages(rb)
+        loss, _ = algo.compute_loss(lp, rb, adv)
+        loss.backward()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    n = max(5, args.steps)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    tokens = wl.tokens_per_step()
+    return {"metric": METRIC, "impl": "reference-gpu", "value": tokens / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+            "steps": n, "config": {"workload": wl.config(1)["workload"] + ", invokerl's own GRPO on the same GPU"}}
 
 
 def run_reference_gpu_e2e(args, device) -> dict:
