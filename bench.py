@@ -915,13 +915,15 @@ def run_reference_gpu(args, device) -> dict:
     ref_root = ROOT / "baseline" / "_ref"
     if not (ref_root / "invokerl" / "policy.py").exists():
         return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
-    if args.workload not in LMHeadGRPO.PRESETS and args.workload not in ("e2e-0.6b", "grpo", "grpo-hbm"):
+    if args.workload not in LMHeadGRPO.PRESETS and args.workload not in ("e2e-0.6b", "grpo", "grpo-hbm", "logits"):
         return {"impl": "reference-gpu", "unavailable": f"no GPU reference leg for workload {args.workload}"}
     sys.path.insert(0, str(ref_root))
     if args.workload == "e2e-0.6b":
         return run_reference_gpu_e2e(args, device)
     if args.workload in ("grpo", "grpo-hbm"):
         return run_reference_gpu_hooks(args, device)
+    if args.workload == "logits":
+        return run_reference_gpu_logits(args, device)
     from invokerl.algorithms import GRPO as RefGRPO
     from invokerl.algorithms import RolloutBatch as RefBatch
     from invokerl.policy import PolicyModel as RefPolicy
@@ -1005,6 +1007,37 @@ def run_reference_gpu_hooks(args, device) -> dict:
     tokens = wl.tokens_per_step()
     return {"metric": METRIC, "impl": "reference-gpu", "value": tokens / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
             "steps": n, "config": {"workload": wl.config(1)["workload"] + ", invokerl's own GRPO on the same GPU"}}
+
+
+def run_reference_gpu_logits(args, device) -> dict:
+    """The reference's materialised-logits log-prob (policy.py:100-104: -F.cross_entropy over
+    [N, V] bf16 logits, reduction="none") forward + backward on the logits workload's inputs."""
+    import torch.nn.functional as F
+
+    wl = LogitsLogProb(args.workload, args)
+    wl.setup(0, 1, device)
+    x = wl.logits.detach().requires_grad_(True)
+
+    def step():
+        x.grad = None
+        lp = -F.cross_entropy(x, wl.t, reduction="none")
+        (lp * wl.up).sum().backward()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    n = max(5, args.steps)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    return {"metric": METRIC, "impl": "reference-gpu", "value": wl.N / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+            "steps": n, "config": {"workload": "logits bf16 [%d, %d]: -F.cross_entropy fwd + autograd bwd on the same "
+                                               "GPU" % (wl.N, V)},
+            "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
 
 
 def run_reference_gpu_e2e(args, device) -> dict:
