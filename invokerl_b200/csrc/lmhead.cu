@@ -659,8 +659,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Wide CTA-pair variant for long K: the pair computes a 256 x 512 tile per K step with two
 // N=256 MMAs into all 512 TMEM columns.  Each CTA stages 128 A rows and 256 of the 512 B rows per
 // 64-deep K block (48 KB, 4 stages), so L2 and shared-memory reads per MMA flop are 3/4 of the
-// 256 x 256 pair kernel.  The single accumulator is not double-buffered: the epilogue of tile j
-// delays the first MMA of tile j+1, which costs a few percent when K is long (H = 4096, dH, dW).
+// 256 x 256 pair kernel.  The single accumulator is not double-buffered; it is drained in two
+// 256-column halves, and the next tile's first-half MMAs start as soon as the first half is
+// drained, so only that half's drain delays the tensor pipe.
 constexpr int WN = 512;
 constexpr int kWideStages = 4;
 constexpr uint32_t kWideTileB = (WN / 2) * BK * 2;  // 32 KB: this CTA's half of the B tile
