@@ -243,3 +243,38 @@ def test_ppo_whitening_moments_combine_over_ranks_gloo(counts):
         torch.testing.assert_close(out[1], allx.double().std().float(), rtol=1e-5, atol=1e-6)
     else:
         assert float(out[3]) == 0.0
+
+
+@pytest.mark.parametrize("V,world", [(151936, 1), (151936, 2), (151936, 8), (5000, 3), (8, 4)])
+def test_vocab_shard_bounds_cover_the_vocabulary(V, world):
+    from invokerl_b200.vocab_parallel import shard_bounds
+
+    bounds = [shard_bounds(V, world, r) for r in range(world)]
+    assert bounds[0][0] == 0 and bounds[-1][1] == V
+    for (s0, e0), (s1, e1) in zip(bounds, bounds[1:]):
+        assert e0 == s1
+    for s, e in bounds:
+        assert s % 8 == 0 and 0 <= s <= e <= V  # 16-byte aligned slices of a bf16 [V, H] weight
+
+
+def test_vocab_parallel_combine_restated():
+    """The combine rule of the vocab-parallel forward: logsumexp over the slices' logsumexps and
+    the owner's target logit give the unsharded log-prob (restated in torch on the CPU)."""
+    from invokerl_b200.vocab_parallel import shard_bounds
+
+    g = torch.Generator().manual_seed(0)
+    N, V, P = 37, 1000, 3
+    logits = 3 * torch.randn(N, V, generator=g, dtype=torch.float64)
+    t = torch.randint(0, V, (N,), generator=g)
+    want = torch.log_softmax(logits, dim=1).gather(1, t[:, None]).squeeze(1)
+    lse_parts, t_parts = [], []
+    for r in range(P):
+        s, e = shard_bounds(V, P, r)
+        lse_parts.append(torch.logsumexp(logits[:, s:e], dim=1))
+        own = (t >= s) & (t < e)
+        tl = torch.full((N,), float("-inf"), dtype=torch.float64)
+        tl[own] = logits[own, t[own]]
+        t_parts.append(tl)
+    lse = torch.logsumexp(torch.stack(lse_parts), dim=0)
+    got = torch.stack(t_parts).max(dim=0).values - lse
+    torch.testing.assert_close(got, want, rtol=0, atol=1e-12)
