@@ -232,7 +232,7 @@ IKRL_API int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, con
  * is scattered back with zero rows elsewhere.  Choosing the chunks then needs the active-row
  * count on the host: the call synchronises `stream` once.  Inside a stream capture, or with
  * INVOKERL_B200_SKIP_ZERO_ROWS=0 in the environment, all rows are processed and the call does
- * not synchronise. */
+ * not synchronise.  With N = 0 a non-accumulated dweight is zeroed and nothing else runs. */
 IKRL_API size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows,
                                                 int32_t dweight_dtype, int32_t accumulate_dweight);
 IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids,

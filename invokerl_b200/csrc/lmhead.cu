@@ -1360,12 +1360,19 @@ int check_common(const void* hidden, const void* weight, const int64_t* ids, int
 
 using namespace ikrl;
 
+// With no rows no kernel runs; the status word at the start of the workspace is still cleared so
+// that ikrl_lmhead_status reads 0 after the call.
+static int clear_status_word(void* ws, size_t ws_bytes, void* stream) {
+  if (ws != nullptr && ws_bytes >= sizeof(int)) IKRL_CUDA(cudaMemsetAsync(ws, 0, sizeof(int), as_stream(stream)));
+  return IKRL_OK;
+}
+
 static int lmhead_fwd_impl(const char* what, const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
                     int32_t V, int64_t vocab_start, bool shard, float* logp, float* lse, void* ws, size_t ws_bytes,
                     void* stream) {
   int rc = check_common(hidden, weight, ids, N, H, V, what);
   if (rc) return rc;
-  if (N == 0) return IKRL_OK;
+  if (N == 0) return clear_status_word(ws, ws_bytes, stream);
   IKRL_REQUIRE(logp != nullptr, IKRL_ERR_INVALID_ARGUMENT, "%s: output is NULL", what);
   const FwdLayout L = fwd_layout(N, H, V);
   IKRL_REQUIRE(ws != nullptr && ws_bytes >= L.total, IKRL_ERR_WORKSPACE,
@@ -1412,7 +1419,12 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
                "%s: dweight dtype %d unsupported", what, dweight_dtype);
   IKRL_REQUIRE(!(accumulate_dweight && dweight_dtype == IKRL_DTYPE_BF16), IKRL_ERR_UNSUPPORTED,
                "%s: accumulating into a bf16 dweight is not supported; use fp32", what);
-  if (N == 0) return IKRL_OK;
+  if (N == 0) {  // no rows: dW is zero, or left as it is when accumulating
+    if (dweight && !accumulate_dweight)
+      IKRL_CUDA(cudaMemsetAsync(dweight, 0, (size_t)V * H * (dweight_dtype == IKRL_DTYPE_F32 ? 4 : 2),
+                                as_stream(stream)));
+    return clear_status_word(ws, ws_bytes, stream);
+  }
   IKRL_REQUIRE(lse && dlogp && (dhidden || dweight), IKRL_ERR_INVALID_ARGUMENT,
                "%s: null pointer", what);
   const BwdLayout L = bwd_layout(N, H, V, chunk_rows, dweight_dtype, accumulate_dweight);

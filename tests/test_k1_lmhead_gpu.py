@@ -232,3 +232,26 @@ def test_forward_and_backward_capture_into_a_cuda_graph(monkeypatch):
     assert torch.equal(lp_c, lp_e) and torch.equal(lse_c, lse_e)
     assert torch.equal(dh_c, dh_e)
     torch.testing.assert_close(dw_c, dw_e, rtol=1e-4, atol=1e-6)
+
+
+def test_empty_batch():
+    """No rows: empty outputs, a zero weight gradient (unchanged when accumulating), status 0."""
+    H, V = 128, 3000
+    w = lmhead_inputs(1, H, V, seed=5, w_std=0.3).weight.to(DEV)
+    h = torch.empty(0, H, dtype=torch.bfloat16, device=DEV)
+    t = torch.empty(0, dtype=torch.int64, device=DEV)
+    lp, lse = ops.lmhead_forward_raw(h, w, t)
+    assert lp.shape == (0,) and lse.shape == (0,)
+    g = torch.empty(0, device=DEV)
+    for dw_dtype in (torch.bfloat16, torch.float32):
+        dh, dw = ops.lmhead_backward_raw(h, w, t, lse, g, dw_dtype=dw_dtype)
+        assert dh.shape == (0, H) and dw.dtype == dw_dtype and float(dw.abs().max()) == 0.0
+    base = torch.randn(V, H, device=DEV)
+    acc = base.clone()
+    ops.lmhead_backward_raw(h, w, t, lse, g, want_dh=False, dweight_out=acc)
+    assert torch.equal(acc, base)
+    hr = h.requires_grad_(True)
+    wr = w.float().requires_grad_(True)
+    out = ops.lmhead_logprob(hr, wr, t)
+    out.sum().backward()
+    assert out.shape == (0,) and float(wr.grad.abs().max()) == 0.0

@@ -74,3 +74,11 @@ def test_ignore_index_and_out_of_range():
     logp = logp.cpu()
     assert logp[1].item() == 0.0 and torch.isnan(logp[2])
     assert torch.isfinite(logp[[0, 3]]).all()
+
+
+def test_empty_batch():
+    x = torch.empty(0, 1000, dtype=torch.bfloat16, device=DEV, requires_grad=True)
+    t = torch.empty(0, dtype=torch.int64, device=DEV)
+    lp = ops.logits_logprob(x, t)
+    lp.sum().backward()
+    assert lp.shape == (0,) and x.grad.shape == (0, 1000)
