@@ -127,8 +127,14 @@ def lmhead_logprob_vocab_parallel(hidden: torch.Tensor, weight_shard: torch.Tens
 
 
 def shard_bounds(vocab_size: int, world: int, rank: int) -> tuple[int, int]:
-    """[start, end) of rank's vocabulary slice: contiguous, sizes differing by at most 8 rows,
-    starts multiples of 8 (16-byte aligned W rows)."""
-    per = -(-vocab_size // (8 * world)) * 8
-    start = min(vocab_size, rank * per)
-    return start, min(vocab_size, start + per)
+    """[start, end) of rank's vocabulary slice.  The vocabulary is cut into blocks of 8 rows
+    (16-byte aligned W rows); the blocks are dealt out contiguously and as evenly as possible, so
+    slice sizes differ by at most 15 rows (8 from the uneven deal, 7 from a vocabulary that is not
+    a multiple of 8).  A slice is empty only when vocab_size < 8 * world."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} out of range for world size {world}")
+    blocks = -(-vocab_size // 8)
+    base, extra = divmod(blocks, world)
+    start = 8 * (rank * base + min(rank, extra))
+    end = 8 * ((rank + 1) * base + min(rank + 1, extra))
+    return min(vocab_size, start), min(vocab_size, end)

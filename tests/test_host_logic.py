@@ -245,7 +245,8 @@ def test_ppo_whitening_moments_combine_over_ranks_gloo(counts):
         assert float(out[3]) == 0.0
 
 
-@pytest.mark.parametrize("V,world", [(151936, 1), (151936, 2), (151936, 8), (5000, 3), (8, 4)])
+@pytest.mark.parametrize("V,world", [(151936, 1), (151936, 2), (151936, 8), (151936, 3), (5000, 3),
+                                     (1000, 7), (777, 8), (8, 4), (64, 8)])
 def test_vocab_shard_bounds_cover_the_vocabulary(V, world):
     from invokerl_b200.vocab_parallel import shard_bounds
 
@@ -255,6 +256,10 @@ def test_vocab_shard_bounds_cover_the_vocabulary(V, world):
         assert e0 == s1
     for s, e in bounds:
         assert s % 8 == 0 and 0 <= s <= e <= V  # 16-byte aligned slices of a bf16 [V, H] weight
+    sizes = [e - s for s, e in bounds]
+    assert max(sizes) - min(sizes) <= 15
+    if V >= 8 * world:
+        assert min(sizes) > 0
 
 
 def test_vocab_parallel_combine_restated():
