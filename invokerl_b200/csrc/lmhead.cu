@@ -1117,6 +1117,52 @@ bool use_wide(int K) {
 
 int64_t cdiv64(int64_t a, int64_t b);
 
+// Busiest pair's work, in tiles, when m_pairs row pairs x ceil(n_tiles / tps) column ranges of
+// tps tiles (the last range shorter) are dealt round-robin, range fastest, to npairs persistent
+// pairs: the order of the pair kernels' unit loop.
+int64_t pair_makespan(int64_t m_pairs, int n_tiles, int tps, int64_t npairs) {
+  const int splits = (int)cdiv64(n_tiles, tps);
+  const int64_t nunits = m_pairs * splits;
+  const int64_t np = std::max<int64_t>(1, std::min<int64_t>(nunits, npairs));
+  int64_t worst = 0;
+  for (int64_t pr = 0; pr < np; ++pr) {
+    int64_t tiles = 0;
+    for (int64_t u = pr; u < nunits; u += np) {
+      const int sp = (int)(u % splits);
+      tiles += std::min(tps, n_tiles - sp * tps);
+    }
+    worst = std::max(worst, tiles);
+  }
+  return worst;
+}
+
+// Balance of the persistent pairs: the L2 rule's split count can leave a last round of units on
+// a few pairs only (14 m-pairs x 11 splits = 154 units over 74 pairs runs 3 rounds where the mean
+// is 2.1).  Up to 3x the hinted count, take a larger count when it shortens the busiest pair's
+// work by at least 5%; more splits mean more W re-reads, so near-balanced hints stay.  Used for
+// the backward's dS launches, which have no per-split workspace.  INVOKERL_B200_BALANCE_SPLITS=0
+// keeps the hint.
+bool balance_splits_enabled() {
+  const char* e = getenv("INVOKERL_B200_BALANCE_SPLITS");
+  return !(e != nullptr && e[0] == '0');
+}
+
+int balanced_tiles_per_split(int64_t m_tiles, int n_tiles, int splits_hint, int64_t npairs) {
+  const int64_t m_pairs = (m_tiles + 1) / 2;
+  int best_tps = (int)cdiv64(n_tiles, splits_hint);
+  int64_t best = pair_makespan(m_pairs, n_tiles, best_tps, npairs);
+  for (int sp = splits_hint + 1; sp <= std::min(3 * splits_hint, n_tiles); ++sp) {
+    const int tps = (int)cdiv64(n_tiles, sp);
+    if (tps == best_tps) continue;
+    const int64_t ms = pair_makespan(m_pairs, n_tiles, tps, npairs);
+    if (ms * 20 < best * 19) {
+      best = ms;
+      best_tps = tps;
+    }
+  }
+  return best_tps;
+}
+
 // Launch one K1 GEMM with the kernel the configuration selects, filling in the tile ranges:
 // splits_hint > 0 asks for that many N ranges of 256-column tiles (fewer if the tiles run out);
 // splits_hint <= 0 gives every N tile its own unit.  p.splits holds the count actually used.
@@ -1131,6 +1177,13 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
     p.splits = p.n_tiles;
   } else {
     p.tiles_per_split = (int)cdiv64(p.n_tiles, splits_hint);
+    const char* pe = getenv("INVOKERL_B200_PERSISTENT");
+    if (EPI == EPI_DLOGITS && kind != 0 && !(pe != nullptr && pe[0] == '0') && balance_splits_enabled()) {
+      int dev = 0, nsm = kNumSMs;
+      IKRL_CUDA(cudaGetDevice(&dev));
+      IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+      p.tiles_per_split = balanced_tiles_per_split(m_tiles, p.n_tiles, splits_hint, std::max(1, nsm / 2));
+    }
     p.splits = (int)cdiv64(p.n_tiles, p.tiles_per_split);
   }
   p.split_major = 1;
