@@ -58,6 +58,14 @@ def test_argument_errors_need_no_gpu(lib):
     with pytest.raises(N.IkrlError, match="workspace"):
         N.call("ikrl_masked_moments", N.c_void_p(16), N.c_void_p(16), N.i64(10), N.c_void_p(16), None,
                N.sz(0), None)
+    p = N.c_void_p(256)
+    with pytest.raises(N.IkrlError, match="multiple of 8"):  # hidden rows must be 16-byte aligned
+        N.call("ikrl_lmhead_logprob_fwd", p, p, p, N.i64(4), N.i32(12), N.i32(100), p, p, p, N.sz(1 << 20), None)
+    with pytest.raises(N.IkrlError, match="bad sizes"):
+        N.call("ikrl_lmhead_logprob_fwd", p, p, p, N.i64(-1), N.i32(64), N.i32(100), p, p, p, N.sz(1 << 20), None)
+    with pytest.raises(N.IkrlError, match="bf16 dweight"):  # accumulation needs an fp32 dW
+        N.call("ikrl_lmhead_logprob_bwd", p, p, p, p, p, N.i64(4), N.i32(64), N.i32(100), N.i64(0), p, p,
+               N.i32(N.IKRL_DTYPE_BF16), N.i32(1), p, N.sz(1 << 20), None)
 
 
 def test_cpu_tensors_are_rejected():
