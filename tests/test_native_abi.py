@@ -75,3 +75,26 @@ def test_cpu_tensors_are_rejected():
 
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.mask_count(torch.ones(4, dtype=torch.bool))
+
+
+def test_product_package_never_reaches_the_oracle():
+    """The oracle is the checker only: no module of the package imports or names it."""
+    pkg = ROOT / "invokerl_b200"
+    offenders = []
+    for f in sorted(pkg.rglob("*.py")):
+        text = f.read_text()
+        if re.search(r"^\s*(import oracle|from oracle\b)", text, re.M) or "oracle." in text:
+            offenders.append(str(f.relative_to(ROOT)))
+    assert not offenders, offenders
+
+
+def test_importing_the_package_loads_no_oracle():
+    import subprocess
+    import sys
+
+    code = ("import sys, invokerl_b200, invokerl_b200.ops, invokerl_b200.policy, invokerl_b200.algorithms, "
+            "invokerl_b200.vocab_parallel, invokerl_b200.rollout, invokerl_b200.distributed; "
+            "print(any(m == 'oracle' or m.startswith('oracle.') for m in sys.modules))")
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "False"
