@@ -1170,7 +1170,24 @@ int balanced_tiles_per_split(int64_t m_tiles, int n_tiles, int splits_hint, int6
 template <int EPI, bool A_MN, bool B_MN>
 int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CUtensorMap& a_pair,
               const CUtensorMap& b_pair, GemmParams& p, int m_tiles, int splits_hint, cudaStream_t s) {
-  const int kind = !use_pairs() ? 0 : (use_wide(p.K) ? 2 : 1);
+  int kind = !use_pairs() ? 0 : (use_wide(p.K) ? 2 : 1);
+  const char* pers = getenv("INVOKERL_B200_PERSISTENT");
+  const bool persistent = !(pers != nullptr && pers[0] == '0');
+  if (EPI == EPI_STORE_BF16 && kind == 2 && splits_hint <= 0 && persistent && balance_splits_enabled() &&
+      getenv("INVOKERL_B200_WIDE") == nullptr) {
+    // dH: every column tile is a unit reducing over the whole vocabulary, so a narrow H leaves few
+    // units (H = 1024: 2 wide tiles per row pair; 40 row pairs give 80 units, two rounds on 74
+    // pairs where the mean is 1.08).  256-column tiles halve the unit: take the 256 x 256 pair
+    // kernel when its busiest pair finishes at least 5% sooner, counting its measured ~13% lower
+    // rate per flop.
+    int dev = 0, nsm = kNumSMs;
+    IKRL_CUDA(cudaGetDevice(&dev));
+    IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t np = std::max(1, nsm / 2), m_pairs = (m_tiles + 1) / 2;
+    const double wide_cost = 2.0 * (double)pair_makespan(m_pairs, (int)cdiv64(p.N, WN), 1, np);
+    const double pair_cost = 1.13 * (double)pair_makespan(m_pairs, (int)cdiv64(p.N, BN), 1, np);
+    if (pair_cost < 0.95 * wide_cost) kind = 1;
+  }
   const int tile_n = kind == 2 ? WN : BN;
   p.n_tiles = (int)cdiv64(p.N, tile_n);
   if (splits_hint <= 0) {
@@ -1178,8 +1195,7 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
     p.splits = p.n_tiles;
   } else {
     p.tiles_per_split = (int)cdiv64(p.n_tiles, splits_hint);
-    const char* pe = getenv("INVOKERL_B200_PERSISTENT");
-    if (EPI == EPI_DLOGITS && kind != 0 && !(pe != nullptr && pe[0] == '0') && balance_splits_enabled()) {
+    if (EPI == EPI_DLOGITS && kind != 0 && persistent && balance_splits_enabled()) {
       int dev = 0, nsm = kNumSMs;
       IKRL_CUDA(cudaGetDevice(&dev));
       IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
