@@ -257,6 +257,15 @@ IKRL_API int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* wei
  * environment variable INVOKERL_B200_CTA_PAIRS=0 sets the initial choice. */
 IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
 
+/* The launch plan the K1 calls would use, for inspection and tests; makes no CUDA call.  gemm:
+ * 0 the forward over `rows` rows, 1 the dS recompute of a backward chunk of `rows` rows, 2 its
+ * dW (fp32 accumulator), 3 its dH.  num_sms: SMs of the GPU (148 on B200; one persistent CTA
+ * pair per two).  plan_out[4] = kernel (0 single CTAs 128 x 256, 1 CTA pairs 256 x 256, 2 wide
+ * CTA pairs 256 x 512), column tiles, tiles per work unit, work units per row pair.  It follows
+ * the same environment settings as the launches.  No counterpart in the reference. */
+IKRL_API int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t num_sms,
+                              int32_t* plan_out);
+
 /* ---- vocab-parallel LM head ---------------------------------------------------------------- */
 /* The LM head with W split along the vocabulary over P ranks (rows replicated), the optional
  * tensor-parallel layout of the hot path.  No counterpart in the reference, which keeps the whole

@@ -120,6 +120,7 @@ _SIGNATURES: dict[str, tuple] = {
     ),
     "ikrl_lmhead_status": (ctypes.c_int, [_P, POINTER(c_int32), _P]),
     "ikrl_lmhead_set_cta_pairs": (ctypes.c_int, [c_int32]),
+    "ikrl_lmhead_plan": (ctypes.c_int, [c_int32, c_int64, c_int32, c_int32, c_int32, POINTER(c_int32)]),
     "ikrl_lmhead_logprob_fwd_noalloc": (
         ctypes.c_int,
         [_P, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P],

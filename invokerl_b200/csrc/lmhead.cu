@@ -1164,45 +1164,57 @@ int balanced_tiles_per_split(int64_t m_tiles, int n_tiles, int splits_hint, int6
   return best_tps;
 }
 
-// Launch one K1 GEMM with the kernel the configuration selects, filling in the tile ranges:
-// splits_hint > 0 asks for that many N ranges of 256-column tiles (fewer if the tiles run out);
-// splits_hint <= 0 gives every N tile its own unit.  p.splits holds the count actually used.
+// Kernel and column ranges of one K1 GEMM launch: host arithmetic only, no CUDA call.
+// kind: 0 single CTAs (128 x 256), 1 CTA pairs (256 x 256), 2 wide CTA pairs (256 x 512).
+// splits_hint > 0 asks for that many column ranges (fewer if the tiles run out); splits_hint <= 0
+// gives every column tile its own unit.  nsm: SMs of the GPU (one persistent pair per two).
+struct K1Plan {
+  int kind, n_tiles, tiles_per_split, splits;
+};
+
+K1Plan plan_k1(int epi, int64_t m_tiles, int N, int K, int splits_hint, int nsm) {
+  K1Plan pl{};
+  pl.kind = !use_pairs() ? 0 : (use_wide(K) ? 2 : 1);
+  const char* pers = getenv("INVOKERL_B200_PERSISTENT");
+  const bool persistent = !(pers != nullptr && pers[0] == '0');
+  const int64_t npairs = std::max(1, nsm / 2);
+  if (epi == EPI_STORE_BF16 && pl.kind == 2 && splits_hint <= 0 && persistent && balance_splits_enabled() &&
+      getenv("INVOKERL_B200_WIDE") == nullptr) {
+    // bf16-store launches (dH; a one-chunk bf16 dW): every column tile is a unit reducing over the
+    // whole K, so a narrow N leaves few units (dH at H = 1024: 2 wide tiles per row pair; 40 row
+    // pairs give 80 units, two rounds on 74 pairs where the mean is 1.08).  256-column tiles halve
+    // the unit: take the 256 x 256 pair kernel when its busiest pair finishes at least 5% sooner,
+    // counting its measured ~13% lower rate per flop.
+    const int64_t m_pairs = (m_tiles + 1) / 2;
+    const double wide_cost = 2.0 * (double)pair_makespan(m_pairs, (int)cdiv64(N, WN), 1, npairs);
+    const double pair_cost = 1.13 * (double)pair_makespan(m_pairs, (int)cdiv64(N, BN), 1, npairs);
+    if (pair_cost < 0.95 * wide_cost) pl.kind = 1;
+  }
+  pl.n_tiles = (int)cdiv64(N, pl.kind == 2 ? WN : BN);
+  if (splits_hint <= 0) {
+    pl.tiles_per_split = 1;
+  } else {
+    pl.tiles_per_split = (int)cdiv64(pl.n_tiles, splits_hint);
+    if (epi == EPI_DLOGITS && pl.kind != 0 && persistent && balance_splits_enabled())
+      pl.tiles_per_split = balanced_tiles_per_split(m_tiles, pl.n_tiles, splits_hint, npairs);
+  }
+  pl.splits = (int)cdiv64(pl.n_tiles, pl.tiles_per_split);
+  return pl;
+}
+
+// Launch one K1 GEMM with the kernel plan_k1 selects, filling in the tile ranges; p.splits holds
+// the count actually used.
 template <int EPI, bool A_MN, bool B_MN>
 int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CUtensorMap& a_pair,
               const CUtensorMap& b_pair, GemmParams& p, int m_tiles, int splits_hint, cudaStream_t s) {
-  int kind = !use_pairs() ? 0 : (use_wide(p.K) ? 2 : 1);
-  const char* pers = getenv("INVOKERL_B200_PERSISTENT");
-  const bool persistent = !(pers != nullptr && pers[0] == '0');
-  if (EPI == EPI_STORE_BF16 && kind == 2 && splits_hint <= 0 && persistent && balance_splits_enabled() &&
-      getenv("INVOKERL_B200_WIDE") == nullptr) {
-    // dH: every column tile is a unit reducing over the whole vocabulary, so a narrow H leaves few
-    // units (H = 1024: 2 wide tiles per row pair; 40 row pairs give 80 units, two rounds on 74
-    // pairs where the mean is 1.08).  256-column tiles halve the unit: take the 256 x 256 pair
-    // kernel when its busiest pair finishes at least 5% sooner, counting its measured ~13% lower
-    // rate per flop.
-    int dev = 0, nsm = kNumSMs;
-    IKRL_CUDA(cudaGetDevice(&dev));
-    IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-    const int64_t np = std::max(1, nsm / 2), m_pairs = (m_tiles + 1) / 2;
-    const double wide_cost = 2.0 * (double)pair_makespan(m_pairs, (int)cdiv64(p.N, WN), 1, np);
-    const double pair_cost = 1.13 * (double)pair_makespan(m_pairs, (int)cdiv64(p.N, BN), 1, np);
-    if (pair_cost < 0.95 * wide_cost) kind = 1;
-  }
-  const int tile_n = kind == 2 ? WN : BN;
-  p.n_tiles = (int)cdiv64(p.N, tile_n);
-  if (splits_hint <= 0) {
-    p.tiles_per_split = 1;
-    p.splits = p.n_tiles;
-  } else {
-    p.tiles_per_split = (int)cdiv64(p.n_tiles, splits_hint);
-    if (EPI == EPI_DLOGITS && kind != 0 && persistent && balance_splits_enabled()) {
-      int dev = 0, nsm = kNumSMs;
-      IKRL_CUDA(cudaGetDevice(&dev));
-      IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-      p.tiles_per_split = balanced_tiles_per_split(m_tiles, p.n_tiles, splits_hint, std::max(1, nsm / 2));
-    }
-    p.splits = (int)cdiv64(p.n_tiles, p.tiles_per_split);
-  }
+  int dev = 0, nsm = kNumSMs;
+  IKRL_CUDA(cudaGetDevice(&dev));
+  IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  const K1Plan pl = plan_k1(EPI, m_tiles, p.N, p.K, splits_hint, nsm);
+  const int kind = pl.kind;
+  p.n_tiles = pl.n_tiles;
+  p.tiles_per_split = pl.tiles_per_split;
+  p.splits = pl.splits;
   p.split_major = 1;
   p.part_sets = p.splits * (kind == 2 ? 2 : 1);
   {
@@ -1707,6 +1719,28 @@ int ikrl_lmhead_set_cta_pairs(int32_t enable) {
   const int prev = use_pairs() ? 1 : 0;
   g_pairs.store(enable ? 1 : 0, std::memory_order_relaxed);
   return prev;
+}
+
+int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t num_sms, int32_t* plan_out) {
+  clear_error();
+  IKRL_REQUIRE(gemm >= 0 && gemm <= 3, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_plan: gemm %d not in 0..3", gemm);
+  IKRL_REQUIRE(rows > 0 && rows <= (int64_t)65535 * BM && H > 0 && V > 0 && num_sms >= 2 && plan_out,
+               IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_plan: bad arguments");
+  const int64_t row_tiles = cdiv64(rows, BM);
+  K1Plan pl{};
+  if (gemm == 0)  // forward: the hint is the workspace's split count
+    pl = plan_k1(EPI_LSE, row_tiles, V, H, fwd_layout(rows, H, V).splits, num_sms);
+  else if (gemm == 1)  // dS recompute of one backward chunk of `rows` rows
+    pl = plan_k1(EPI_DLOGITS, row_tiles, V, H, choose_splits(row_tiles, (int)cdiv64(V, BN), H), num_sms);
+  else if (gemm == 2)  // dW += dS^T h over the chunk, fp32 accumulator
+    pl = plan_k1(EPI_F32, cdiv64(V, BM), H, (int)rows, 0, num_sms);
+  else  // dH = dS W of the chunk
+    pl = plan_k1(EPI_STORE_BF16, row_tiles, H, V, 0, num_sms);
+  plan_out[0] = pl.kind;
+  plan_out[1] = pl.n_tiles;
+  plan_out[2] = pl.tiles_per_split;
+  plan_out[3] = pl.splits;
+  return IKRL_OK;
 }
 
 int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream) {

@@ -98,3 +98,44 @@ def test_importing_the_package_loads_no_oracle():
     out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip() == "False"
+
+
+def _plan(gemm, rows, H, V=151936, nsm=148):
+    import ctypes
+
+    from invokerl_b200 import _native as N
+
+    out = (ctypes.c_int32 * 4)()
+    N.call("ikrl_lmhead_plan", N.i32(gemm), N.i64(rows), N.i32(H), N.i32(V), N.i32(nsm), out)
+    return tuple(out)
+
+
+@pytest.mark.parametrize("gemm,rows,H,want", [
+    # (kernel, column tiles, tiles per unit, units per row pair); kernel 2 = wide pairs 256 x 512
+    (0, 524288, 4096, (2, 297, 75, 4)),   # 8B forward: the L2 rule's 4 vocabulary splits
+    (1, 28160, 4096, (2, 297, 75, 4)),    # 8B full dS chunk: 440 units on 74 pairs, kept
+    (1, 8700, 4096, (2, 297, 23, 13)),    # 8B last chunk: 5 splits would run 3 rounds where the mean is 2.3
+    (1, 3456, 4096, (2, 297, 20, 15)),    # 14 m-pairs: 11 splits -> 15
+    (3, 28160, 4096, (2, 8, 1, 8)),       # 8B dH stays wide
+    (0, 131072, 1024, (2, 297, 149, 2)),  # 0.6B forward: wide from K = 1024
+    (1, 10092, 1024, (2, 297, 33, 9)),    # 0.6B dS: 4 splits -> 9
+    (3, 10092, 1024, (1, 4, 1, 4)),       # 0.6B dH: 256 x 256 pairs (80 wide units would run 2 rounds)
+    (1, 256, 64, (1, 594, 3, 198)),       # K = 64: 256 x 256 pairs
+])
+def test_lmhead_launch_plan(lib, gemm, rows, H, want):
+    assert _plan(gemm, rows, H) == want
+
+
+def test_lmhead_launch_plan_balance_off(lib, monkeypatch):
+    monkeypatch.setenv("INVOKERL_B200_BALANCE_SPLITS", "0")
+    assert _plan(1, 8700, 4096) == (2, 297, 60, 5)
+    assert _plan(3, 10092, 1024) == (2, 2, 1, 2)
+
+
+def test_lmhead_launch_plan_rejects_bad_arguments(lib):
+    from invokerl_b200 import _native as N
+
+    with pytest.raises(N.IkrlError, match="gemm"):
+        _plan(4, 100, 64)
+    with pytest.raises(N.IkrlError, match="bad arguments"):
+        _plan(0, 0, 64)
