@@ -12,6 +12,12 @@
  *     ordered on that stream and nothing synchronises the host unless the comment says so.
  *   - The library allocates no device memory: outputs and workspaces belong to the caller.  A
  *     `*_workspace_bytes` function gives the workspace size where one is needed.
+ *   - Static device state: two file-scope arrays in the library's device code, present on every
+ *     GPU that loads it.  (1) The pacing counters of the 256x512 K1 kernel (512 x 4 bytes): every
+ *     paced launch on a device zeroes and uses them, so paced launches that overlap on two streams
+ *     weaken each other's pacing; the waits are bounded and the results do not depend on it.
+ *     (2) The 4 MiB scratch of ikrl_lmhead_logprob_fwd_noalloc (below); no other entry point
+ *     touches it.
  *   - Return value: IKRL_OK (0) or an IKRL_ERR_* code; `ikrl_last_error()` then holds a message
  *     (thread-local).  No C++ exception crosses this boundary.
  *   - Row-major tensors.  Masks are bool tensors read as bytes (0 / non-zero).
@@ -68,6 +74,42 @@ IKRL_API const char* ikrl_last_error(void);
 IKRL_API int ikrl_abi_version(void);
 /* Number of kernels this library has launched in this process (host-side counter). */
 IKRL_API unsigned long long ikrl_launch_count(void);
+
+/* ---- launch tuning ------------------------------------------------------------------------- */
+/* Process-wide launch choices of the tensor-core (K1) and loss (K3) kernels.  Each knob has a
+ * fixed default, the configuration the library is measured and shipped with; the library reads
+ * no environment variable.  The other values exist for A/B timing, and every value is covered by
+ * a GPU parity test.  A knob affects the calls made after it is set; set knobs before launches
+ * that should see them, not concurrently with calls on other host threads.  No counterpart in the
+ * reference (its arithmetic is PyTorch's). */
+enum {
+  IKRL_TUNE_CTA_PAIRS = 0,      /* K1: 1 CTA pairs, tcgen05 cta_group::2 (default); 0 single CTAs */
+  IKRL_TUNE_SKIP_ZERO_ROWS = 1, /* K1 backward: 1 skip rows whose upstream gradient is 0 (default);
+                                   0 process every row (no host synchronisation) */
+  IKRL_TUNE_WIDE = 2,           /* K1 pair tile: -1 auto (default: 256x512 when K >= 1024, and the
+                                   256x256 tile for dH when it balances better); 0 never 256x512;
+                                   1 always; 2 the K >= 1024 rule without the dH balance choice */
+  IKRL_TUNE_PERSISTENT = 3,     /* K1 pair kernels: 1 one resident pair per two SMs (default);
+                                   0 one pair per work unit */
+  IKRL_TUNE_PACE = 4,           /* 256x512 kernel: 1 pace the persistent pairs (default); 0 off */
+  IKRL_TUNE_PACE_KB = 5,        /* K blocks between pacing checkpoints (default 64) */
+  IKRL_TUNE_PACE_LAG = 6,       /* checkpoints a pair may lead the slowest by (default 1) */
+  IKRL_TUNE_BALANCE_SPLITS = 7, /* K1 dS launches: 1 pick the vocab split count for balance of
+                                   the persistent pairs (default); 0 the L2 rule alone */
+  IKRL_TUNE_L2_POLICY = 8,      /* 256x512 kernel L2 hints, 10*a + b for the A and B loads, each
+                                   0 normal / 1 evict-last / 2 evict-first; -1 default (a=1, b=0) */
+  IKRL_TUNE_L2_BUDGET_MB = 9,   /* L2 megabytes the vocab split rule gives the resident hidden
+                                   rows; 0 auto (default: 40 when H >= 2048, else 24) */
+  IKRL_TUNE_LOSS_KERNEL = 10,   /* GRPO/DAPO loss: 1 register loads (default); 2 bulk-copy staged;
+                                   0 the general clipped-ratio kernel */
+  IKRL_TUNE_COUNT = 11
+};
+/* Passed as `value`, restores the knob's default. */
+#define IKRL_TUNE_DEFAULT (-0x7fffffffffffffffLL - 1)
+/* Sets `knob` to `value` (IKRL_ERR_INVALID_ARGUMENT outside its range); the old value goes to
+ * *previous when that is not NULL. */
+IKRL_API int ikrl_set_tuning(int32_t knob, int64_t value, int64_t* previous);
+IKRL_API int ikrl_get_tuning(int32_t knob, int64_t* value);
 
 /* ---- K3: advantages ------------------------------------------------------------------------ */
 
@@ -231,8 +273,8 @@ IKRL_API int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, con
  * in order into a dense block (a copy of their hidden rows, [N, H] bf16 at most), and dhidden
  * is scattered back with zero rows elsewhere.  Choosing the chunks then needs the active-row
  * count on the host: the call synchronises `stream` once.  Inside a stream capture, or with
- * INVOKERL_B200_SKIP_ZERO_ROWS=0 in the environment, all rows are processed and the call does
- * not synchronise.  With N = 0 a non-accumulated dweight is zeroed and nothing else runs. */
+ * IKRL_TUNE_SKIP_ZERO_ROWS set to 0, all rows are processed and the call does not
+ * synchronise.  With N = 0 a non-accumulated dweight is zeroed and nothing else runs. */
 IKRL_API size_t ikrl_lmhead_bwd_workspace_bytes(int64_t N, int32_t H, int32_t V, int64_t chunk_rows,
                                                 int32_t dweight_dtype, int32_t accumulate_dweight);
 IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_t* ids,
@@ -242,19 +284,27 @@ IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, con
                                      size_t ws_bytes, void* stream);
 
 /* Allocation-free variant of ikrl_lmhead_logprob_fwd.  It has no counterpart in the reference.
- * For callers that cannot allocate device memory when they need log-probs (during stream capture
- * into a CUDA graph, inside hosts whose own allocator owns all device memory): the scratch comes
- * from a 4 MiB array built into the library, held on every GPU that loads it until exit.  Calls
- * needing more scratch (large N) fail with IKRL_ERR_WORKSPACE.  All calls on a device share the
- * array, so calls that overlap on the GPU race; the first call on a device looks up the array's
- * address and should come before any stream capture. */
+ * For callers that cannot allocate device memory when they need log-probs: hosts whose own
+ * allocator owns all device memory and forbids side allocations, or frameworks whose caching pool
+ * has already reserved the free memory.  The scratch comes from a 4 MiB array built into the
+ * library, held on every GPU that loads it until exit.  Calls needing more scratch (above 61,672
+ * rows at H = 4096, 116,496 at H = 1024, V = 151936) fail with IKRL_ERR_WORKSPACE before any GPU
+ * work.  All calls on a device share the array and it keeps the last call's contents (each call
+ * clears what must start at zero), so calls that overlap on the GPU race.  The first call on a
+ * device looks up the device addresses of the library's static arrays and should come before any
+ * stream capture. */
 IKRL_API int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* weight,
                                              const int64_t* ids, int64_t N, int32_t H, int32_t V,
                                              float* logp, float* lse, void* stream);
+/* Device status word of the last ikrl_lmhead_logprob_fwd_noalloc call on the current device
+ * (synchronises `stream`): IKRL_OK, or IKRL_ERR_DEVICE with *status_out = the code a tensor-core
+ * kernel recorded when a bounded wait expired (its outputs are then NaN).  No counterpart in the
+ * reference. */
+IKRL_API int ikrl_lmhead_noalloc_status(int32_t* status_out, void* stream);
 
 /* Selects the K1 GEMM kernel for later calls in this process: CTA pairs (tcgen05 cta_group::2,
  * clusters of two; the default) or single CTAs (enable = 0).  Returns the previous setting.  The
- * environment variable INVOKERL_B200_CTA_PAIRS=0 sets the initial choice. */
+ * same switch as ikrl_set_tuning(IKRL_TUNE_CTA_PAIRS, ...). */
 IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
 
 /* The launch plan the K1 calls would use, for inspection and tests; makes no CUDA call.  gemm:
@@ -262,7 +312,7 @@ IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
  * dW (fp32 accumulator), 3 its dH.  num_sms: SMs of the GPU (148 on B200; one persistent CTA
  * pair per two).  plan_out[4] = kernel (0 single CTAs 128 x 256, 1 CTA pairs 256 x 256, 2 wide
  * CTA pairs 256 x 512), column tiles, tiles per work unit, work units per row pair.  It follows
- * the same environment settings as the launches.  No counterpart in the reference. */
+ * the same tuning knobs as the launches.  No counterpart in the reference. */
 IKRL_API int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t num_sms,
                               int32_t* plan_out);
 

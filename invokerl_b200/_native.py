@@ -25,6 +25,21 @@ IKRL_KL_SIMPLE = 1
 IKRL_KL_NONE = 2
 IKRL_LOSS_GRPO = 0
 IKRL_LOSS_PPO = 1
+# Launch knobs of ikrl_set_tuning (include/invokerl_b200.h, IKRL_TUNE_*).
+TUNE = {
+    "cta_pairs": 0,
+    "skip_zero_rows": 1,
+    "wide": 2,
+    "persistent": 3,
+    "pace": 4,
+    "pace_kb": 5,
+    "pace_lag": 6,
+    "balance_splits": 7,
+    "l2_policy": 8,
+    "l2_budget_mb": 9,
+    "loss_kernel": 10,
+}
+TUNE_DEFAULT = -(1 << 63)
 LOSS_NSUMS = 16
 LOSS_NMETRICS = 12
 SIMPO_NMETRICS = 8
@@ -125,6 +140,9 @@ _SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_P, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P],
     ),
+    "ikrl_lmhead_noalloc_status": (ctypes.c_int, [POINTER(c_int32), _P]),
+    "ikrl_set_tuning": (ctypes.c_int, [c_int32, c_int64, POINTER(c_int64)]),
+    "ikrl_get_tuning": (ctypes.c_int, [c_int32, POINTER(c_int64)]),
     "ikrl_lmhead_shard_fwd": (
         ctypes.c_int,
         [_P, _P, _P, c_int64, c_int32, c_int32, c_int64, _P, _P, _P, c_size_t, _P],
@@ -189,6 +207,39 @@ def call(name: str, *args) -> None:
     if rc != 0:
         msg = lib().ikrl_last_error()
         raise IkrlError(name, rc, msg.decode() if msg else "")
+
+
+def set_tuning(knob: str, value: int | None) -> int:
+    """Set a launch knob (None restores its default); returns the previous value."""
+    prev = c_int64(0)
+    call("ikrl_set_tuning", c_int32(TUNE[knob]), c_int64(TUNE_DEFAULT if value is None else int(value)),
+         ctypes.byref(prev))
+    return int(prev.value)
+
+
+def get_tuning(knob: str) -> int:
+    v = c_int64(0)
+    call("ikrl_get_tuning", c_int32(TUNE[knob]), ctypes.byref(v))
+    return int(v.value)
+
+
+class tuning:
+    """Context manager that sets launch knobs and restores their previous values on exit:
+    ``with tuning(pace=0, wide=1): ...``."""
+
+    def __init__(self, **knobs: int | None):
+        self.knobs = knobs
+        self.prev: dict[str, int] = {}
+
+    def __enter__(self):
+        for k, v in self.knobs.items():
+            self.prev[k] = set_tuning(k, v)
+        return self
+
+    def __exit__(self, *exc):
+        for k, v in self.prev.items():
+            set_tuning(k, v)
+        return False
 
 
 # ---- tensor helpers -------------------------------------------------------------------------
@@ -282,6 +333,9 @@ __all__ = [
     "dtype_code",
     "as_mask",
     "workspace",
+    "set_tuning",
+    "get_tuning",
+    "tuning",
     "c_double",
     "c_uint8",
     "c_int32",

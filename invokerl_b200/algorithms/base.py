@@ -87,7 +87,11 @@ class BaseAlgorithm(ABC):
         dist.all_reduce(p, group=self.process_group)
         mt = metrics.double() * p_local
         dist.all_reduce(mt, group=self.process_group)
-        return loss * (p_local / float(p.item())), (mt / p).float()
+        # The pair count stays on the device (no host synchronisation); a batch with no pair on any
+        # rank gives a zero loss share and zero metrics instead of a division by zero.
+        pc = p.clamp(min=1.0)
+        share = (p_local / pc).to(loss.dtype).reshape(())
+        return loss * share, (mt / pc).float()
 
     def _global_moments(self, w: Tensor) -> Tensor:
         """[mean, unbiased std, count, enabled] over the whole batch from each rank's own

@@ -22,6 +22,9 @@ int check_launch(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Current value of a process-wide launch knob (IKRL_TUNE_*; ikrl_set_tuning).
+int64_t tuning(int knob);
+
 constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
 
 }  // namespace ikrl

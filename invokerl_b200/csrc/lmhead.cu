@@ -428,13 +428,12 @@ constexpr uint32_t kPairSmemBytes = kPairStages * kPairStageBytes + 1024;
 
 // Pacing of the persistent pairs: pairs that read the same W tiles through L2 drift apart over a
 // sweep, and a tile read by a leading pair is evicted before the trailing pairs reach it.  Each
-// pair publishes how many checkpoints it has passed (one per kPaceKb K blocks, so a long
-// reduction such as dH over the vocabulary has many per tile); a pair about to pass checkpoint j
-// waits until every unfinished pair has passed checkpoint j - kPaceLag.  The wait is a heuristic with a short bound:
-// after kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair
-// that is not resident, e.g. on a shared GPU, must not stall the others).
-constexpr int kPaceLag = 1;
-constexpr int kPaceKb = 64;  // K blocks between checkpoints (one per tile at K = 4096, 4 tiles at K = 1024)
+// pair publishes how many checkpoints it has passed (one per pace_kb K blocks, default 64: one per
+// tile at K = 4096, 4 tiles at K = 1024; a long reduction such as dH over the vocabulary has many
+// per tile); a pair about to pass checkpoint j waits until every unfinished pair has passed
+// checkpoint j - pace_lag (default 1).  The wait is a heuristic with a short bound: after
+// kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair that is
+// not resident, e.g. on a shared GPU, must not stall the others).
 constexpr uint64_t kPaceBoundNs = 20000;
 constexpr unsigned kPaceDone = 0xffffffffu;
 
@@ -731,7 +730,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
         for (int t = t_begin; t < t_end && ok; ++t, ++jt) {
           for (int kb = 0; kb < nk; ++kb) {
-            // pacing checkpoint every kPaceKb K blocks of this pair's work
+            // pacing checkpoint every pace_kb K blocks of this pair's work
             const int gkb = jt * nk + kb;
             if (p.lockstep != nullptr && rank == 0 && gkb % p.pace_kb == 0)
               pace_checkpoint(p.lockstep, pair_id, npairs, gkb / p.pace_kb, p.pace_lag, pacing);
@@ -1031,11 +1030,9 @@ int pace_array(unsigned** out) {
   return IKRL_OK;
 }
 
-// Pacing of the wide kernel's pairs: on unless INVOKERL_B200_PACE=0.
-bool pacing_enabled() {
-  const char* e = getenv("INVOKERL_B200_PACE");
-  return !(e != nullptr && e[0] == '0');
-}
+// Pacing of the wide kernel's pairs (IKRL_TUNE_PACE, on by default).
+bool pacing_enabled() { return tuning(IKRL_TUNE_PACE) != 0; }
+bool persistent_pairs() { return tuning(IKRL_TUNE_PERSISTENT) != 0; }
 
 template <int EPI, bool A_MN, bool B_MN, bool WIDE>
 int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p_in, int m_tiles, cudaStream_t s) {
@@ -1049,9 +1046,8 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   int dev = 0, nsm = kNumSMs;
   IKRL_CUDA(cudaGetDevice(&dev));
   IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
-  // One resident pair per two SMs; INVOKERL_B200_PERSISTENT=0 launches one pair per unit instead.
-  const char* pe = getenv("INVOKERL_B200_PERSISTENT");
-  const bool persistent = !(pe != nullptr && pe[0] == '0');
+  // One resident pair per two SMs; IKRL_TUNE_PERSISTENT = 0 launches one pair per unit instead.
+  const bool persistent = persistent_pairs();
   const int64_t npairs = std::max<int64_t>(1, persistent ? std::min<int64_t>(nunits, nsm / 2) : nunits);
   p.lockstep = nullptr;
   // Pacing helps the wide kernel (long tiles, W re-read across pairs); on the 256 x 256 pair
@@ -1060,10 +1056,8 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
     IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));
-    p.pace_kb = kPaceKb;
-    p.pace_lag = kPaceLag;
-    if (const char* e = getenv("INVOKERL_B200_PACE_KB")) p.pace_kb = std::max(1, atoi(e));
-    if (const char* e = getenv("INVOKERL_B200_PACE_LAG")) p.pace_lag = std::max(0, atoi(e));
+    p.pace_kb = (int)tuning(IKRL_TUNE_PACE_KB);
+    p.pace_lag = (int)tuning(IKRL_TUNE_PACE_LAG);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * npairs), 1, 1);
@@ -1093,26 +1087,17 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   return check_launch("lmhead_gemm_pair_kernel");
 }
 
-// Kernel choice: CTA pairs by default; INVOKERL_B200_CTA_PAIRS=0 in the environment, or
-// ikrl_lmhead_set_cta_pairs(0), selects the single-CTA kernel.
-std::atomic<int> g_pairs{-1};
-bool use_pairs() {
-  int v = g_pairs.load(std::memory_order_relaxed);
-  if (v < 0) {
-    const char* e = getenv("INVOKERL_B200_CTA_PAIRS");
-    v = (e != nullptr && e[0] == '0') ? 0 : 1;
-    g_pairs.store(v, std::memory_order_relaxed);
-  }
-  return v == 1;
-}
+// Kernel choice: CTA pairs by default; IKRL_TUNE_CTA_PAIRS = 0 (or ikrl_lmhead_set_cta_pairs(0))
+// selects the single-CTA kernel.
+bool use_pairs() { return tuning(IKRL_TUNE_CTA_PAIRS) != 0; }
 
-// Wide tiles (256 x 512 per pair) for long reductions: INVOKERL_B200_WIDE=0 never, =2 always,
-// otherwise when K >= 1024 (16 K blocks per tile or more; at K = 1024 the Qwen3-0.6B head ran
-// 1.4% faster wide than on 256 x 256 pairs).
+// Wide tiles (256 x 512 per pair) for long reductions: IKRL_TUNE_WIDE 0 never, 1 always, otherwise
+// when K >= 1024 (16 K blocks per tile or more; at K = 1024 the Qwen3-0.6B head ran 1.4% faster
+// wide than on 256 x 256 pairs).
 bool use_wide(int K) {
-  const char* e = getenv("INVOKERL_B200_WIDE");
-  if (e != nullptr && e[0] == '0') return false;
-  if (e != nullptr && e[0] == '2') return true;
+  const int64_t w = tuning(IKRL_TUNE_WIDE);
+  if (w == 0) return false;
+  if (w == 1) return true;
   return K >= 1024;
 }
 
@@ -1141,12 +1126,9 @@ int64_t pair_makespan(int64_t m_pairs, int n_tiles, int tps, int64_t npairs) {
 // a few pairs only (14 m-pairs x 11 splits = 154 units over 74 pairs runs 3 rounds where the mean
 // is 2.1).  Up to 3x the hinted count, take a larger count when it shortens the busiest pair's
 // work by at least 5%; more splits mean more W re-reads, so near-balanced hints stay.  Used for
-// the backward's dS launches, which have no per-split workspace.  INVOKERL_B200_BALANCE_SPLITS=0
+// the backward's dS launches, which have no per-split workspace.  IKRL_TUNE_BALANCE_SPLITS = 0
 // keeps the hint.
-bool balance_splits_enabled() {
-  const char* e = getenv("INVOKERL_B200_BALANCE_SPLITS");
-  return !(e != nullptr && e[0] == '0');
-}
+bool balance_splits_enabled() { return tuning(IKRL_TUNE_BALANCE_SPLITS) != 0; }
 
 int balanced_tiles_per_split(int64_t m_tiles, int n_tiles, int splits_hint, int64_t npairs) {
   const int64_t m_pairs = (m_tiles + 1) / 2;
@@ -1175,11 +1157,10 @@ struct K1Plan {
 K1Plan plan_k1(int epi, int64_t m_tiles, int N, int K, int splits_hint, int nsm) {
   K1Plan pl{};
   pl.kind = !use_pairs() ? 0 : (use_wide(K) ? 2 : 1);
-  const char* pers = getenv("INVOKERL_B200_PERSISTENT");
-  const bool persistent = !(pers != nullptr && pers[0] == '0');
+  const bool persistent = persistent_pairs();
   const int64_t npairs = std::max(1, nsm / 2);
   if (epi == EPI_STORE_BF16 && pl.kind == 2 && splits_hint <= 0 && persistent && balance_splits_enabled() &&
-      getenv("INVOKERL_B200_WIDE") == nullptr) {
+      tuning(IKRL_TUNE_WIDE) == -1) {
     // bf16-store launches (dH; a one-chunk bf16 dW): every column tile is a unit reducing over the
     // whole K, so a narrow N leaves few units (dH at H = 1024: 2 wide tiles per row pair; 40 row
     // pairs give 80 units, two rounds on 74 pairs where the mean is 1.08).  256-column tiles halve
@@ -1218,15 +1199,15 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
   p.split_major = 1;
   p.part_sets = p.splits * (kind == 2 ? 2 : 1);
   {
-    // Two digits "ab": L2 policy of the A and B loads of the wide kernel (0 normal, 1 evict-last,
-    // 2 evict-first).  Default "10": A (re-read by every tile of a unit) evict-last, B normal;
-    // evict-first on B measured 40% more DRAM traffic.
-    const char* e = getenv("INVOKERL_B200_L2_HINT");
+    // L2 policy of the A and B loads of the wide kernel (0 normal, 1 evict-last, 2 evict-first),
+    // IKRL_TUNE_L2_POLICY = 10 * a + b.  Default: A (re-read by every tile of a unit) evict-last,
+    // B normal; evict-first on B measured 40% more DRAM traffic.
+    const int64_t pol = tuning(IKRL_TUNE_L2_POLICY);
     p.a_policy = kind == 2 ? 1 : 0;
     p.b_policy = 0;
-    if (e != nullptr && e[0] >= '0' && e[0] <= '2') {
-      p.a_policy = e[0] - '0';
-      if (e[1] >= '0' && e[1] <= '2') p.b_policy = e[1] - '0';
+    if (pol >= 0) {
+      p.a_policy = (int)(pol / 10);
+      p.b_policy = (int)(pol % 10);
     }
   }
   if (kind == 2) return launch_gemm_pair<EPI, A_MN, B_MN, true>(a_pair, b_pair, p, m_tiles, s);
@@ -1243,7 +1224,7 @@ int choose_splits(int64_t m_tiles, int n_tiles, int H) {
   // loads are marked evict-last and whose pairs are paced) keep more rows resident and split the
   // vocabulary less: at H = 4096, 40 MB gives 4 splits.
   int64_t budget_mb = H >= 2048 ? 40 : 24;
-  if (const char* e = getenv("INVOKERL_B200_L2_BUDGET_MB")) budget_mb = std::max<int64_t>(1, atoll(e));
+  if (tuning(IKRL_TUNE_L2_BUDGET_MB) > 0) budget_mb = tuning(IKRL_TUNE_L2_BUDGET_MB);
   const int64_t resident_rows_budget = (budget_mb << 20) / (2ll * H);   // rows whose A tiles fit the budget
   const int64_t blocks_resident = std::max<int64_t>(1, resident_rows_budget / BM);
   int64_t s = cdiv64(kNumSMs, std::min<int64_t>(blocks_resident, m_tiles));
@@ -1420,11 +1401,8 @@ __global__ void scatter_rows_kernel(const uint4* __restrict__ src, const int* __
   }
 }
 
-// Row skipping is on unless INVOKERL_B200_SKIP_ZERO_ROWS=0.
-bool skip_zero_rows_enabled() {
-  const char* e = getenv("INVOKERL_B200_SKIP_ZERO_ROWS");
-  return !(e != nullptr && e[0] == '0');
-}
+// Row skipping is on unless IKRL_TUNE_SKIP_ZERO_ROWS = 0.
+bool skip_zero_rows_enabled() { return tuning(IKRL_TUNE_SKIP_ZERO_ROWS) != 0; }
 
 int check_common(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int H, int V,
                  const char* what) {
@@ -1716,9 +1694,9 @@ int ikrl_lmhead_shard_bwd(const void* hidden, const void* weight_shard, const in
 }
 
 int ikrl_lmhead_set_cta_pairs(int32_t enable) {
-  const int prev = use_pairs() ? 1 : 0;
-  g_pairs.store(enable ? 1 : 0, std::memory_order_relaxed);
-  return prev;
+  int64_t prev = 1;
+  ikrl_set_tuning(IKRL_TUNE_CTA_PAIRS, enable ? 1 : 0, &prev);
+  return (int)prev;
 }
 
 int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t num_sms, int32_t* plan_out) {
@@ -1762,13 +1740,13 @@ int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream) {
 
 // ---- allocation-free forward -------------------------------------------------------------------
 //
-// Some callers cannot allocate device memory at the moment they need log-probs: code running
-// while a stream is being captured into a CUDA graph (an allocation there is not part of the
-// graph and may be refused), hosts that embed this library behind their own device-memory
-// manager and forbid side allocations, or callers whose framework has already reserved all free
-// memory in its pool.  For them the forward below takes its scratch (the per-split row statistics
-// and the device error word) from a fixed array compiled into the library instead of a
-// caller-provided workspace.
+// Some callers cannot allocate device memory at the moment they need log-probs: hosts that embed
+// this library behind their own device-memory manager and forbid side allocations, frameworks
+// that have already reserved all free memory in their caching pool (a cudaMalloc there fails or
+// forces the pool to release memory and synchronise the device), and callers on a latency-critical
+// path where an allocation's implicit synchronisation is not acceptable.  For them the forward
+// below takes its scratch (the per-split row statistics and the device error word) from a fixed
+// array compiled into the library instead of a caller-provided workspace.
 //
 // Limits and sharing rules:
 //   * the array is kNoAllocScratchBytes (4 MiB) and lives on every GPU that loads the library
@@ -1778,7 +1756,10 @@ int ikrl_lmhead_status(const void* ws, int32_t* status_out, void* stream) {
 //     (different streams without ordering) race on it, so order them on one stream;
 //   * the array keeps whatever the last call left in it; the error word at its start is cleared
 //     by every call, the rest is fully rewritten before it is read;
-//   * the first call on each device looks up the array's device address (cudaGetSymbolAddress)
+//   * a bounded wait that expires inside a tensor-core kernel records a code in that error word
+//     and the outputs become NaN; ikrl_lmhead_noalloc_status reads the word of the current device;
+//   * the first call on each device looks up the device addresses of the library's two static
+//     arrays (this scratch and the pacing counters of the wide kernel) with cudaGetSymbolAddress,
 //     with that device current; make that first call before any stream capture begins.
 
 namespace ikrl {
@@ -1791,13 +1772,18 @@ constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kMaxDevices] = {nullptr};
 
-// Device address of g_noalloc_scratch on the current device, looked up once per device.
+// Device address of g_noalloc_scratch on the current device, looked up once per device.  The
+// same first call also resolves the pacing array, so that no later call on this device needs a
+// symbol lookup, whatever its sizes.
 int noalloc_scratch(void** out) {
   int dev = 0;
   IKRL_CUDA(cudaGetDevice(&dev));
   IKRL_REQUIRE(dev >= 0 && dev < kMaxDevices, IKRL_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_addr[dev] == nullptr) {
+    unsigned* pace = nullptr;
+    int rc = pace_array(&pace);
+    if (rc) return rc;
     void* p = nullptr;
     IKRL_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
     g_noalloc_addr[dev] = p;
@@ -1823,4 +1809,13 @@ extern "C" int ikrl_lmhead_logprob_fwd_noalloc(const void* hidden, const void* w
   void* scratch = nullptr;
   if ((rc = noalloc_scratch(&scratch))) return rc;
   return ikrl_lmhead_logprob_fwd(hidden, weight, ids, N, H, V, logp, lse, scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int ikrl_lmhead_noalloc_status(int32_t* status_out, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(status_out != nullptr, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_noalloc_status: null pointer");
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return ikrl_lmhead_status(scratch, status_out, stream);
 }

@@ -1008,12 +1008,8 @@ __global__ void dpo_pairs_kernel(const float* __restrict__ lr, const float* __re
 }
 
 // GRPO / DAPO loss kernel: 2 bulk-copy staged, 1 (default) register loads, 0 the general
-// clipped-ratio kernel (INVOKERL_B200_LEAN_LOSS; kept for A/B timing).
-int lean_loss_mode() {
-  const char* e = getenv("INVOKERL_B200_LEAN_LOSS");
-  if (e != nullptr && e[0] >= '0' && e[0] <= '2') return e[0] - '0';
-  return 1;
-}
+// clipped-ratio kernel (IKRL_TUNE_LOSS_KERNEL; kept for A/B timing).
+int lean_loss_mode() { return (int)tuning(IKRL_TUNE_LOSS_KERNEL); }
 
 // Launch with programmatic stream serialization: the kernel may be scheduled while the previous
 // kernel of the stream runs (its launch latency overlaps that kernel's tail); it calls

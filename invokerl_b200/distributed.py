@@ -125,14 +125,18 @@ def shard_batch(batch: RolloutBatch, rank: int, world: int, balance: bool = Fals
 
 
 def scatter_batch(batch: RolloutBatch | None, src: int = 0, group=None,
-                  device: torch.device | str | None = None) -> RolloutBatch:
+                  device: torch.device | str | None = None, balance: bool = True) -> RolloutBatch:
     """Give every rank its whole prompt groups of the batch held by rank `src`.
 
-    Replaces the replicate-everything `broadcast_batch` of invokerl/distributed.py:236-330: the
-    metadata (field shapes, dtypes, group size, extras layout) is broadcast as a small object,
-    then rank `src` sends each rank only its rows, so each byte of the batch crosses the network
-    once instead of world_size - 1 times.  Tensors whose leading dimension is B are sharded;
-    other tensors and non-tensor extras are broadcast whole.  Collective over `group`."""
+    Replaces the replicate-everything `broadcast_batch` of invokerl/distributed.py:236-330.  Rank
+    `src` chooses the groups of every rank -- by estimated work (`balanced_groups`, the assignment
+    `shard_batch(..., balance=True)` makes) or, with balance=False, contiguous ranges -- and
+    broadcasts that plan with the metadata (field shapes, dtypes, group size, extras layout) as a
+    small object.  Then one all-to-all moves every row field at once: `src` packs each rank's rows
+    of all fields into one byte block, and every rank receives only its own block, so each byte of
+    the batch crosses the network once instead of world_size - 1 times.  A rank's rows come in the
+    order of its groups.  Tensors whose leading dimension is B are sharded; other tensors and
+    non-tensor extras are broadcast whole.  Collective over `group`."""
     import torch.distributed as dist
 
     rank = dist.get_rank(group)
@@ -145,13 +149,25 @@ def scatter_batch(batch: RolloutBatch | None, src: int = 0, group=None,
               "old_log_probs", "ref_log_probs", "group_ids"]
     if rank == src:
         B = batch.token_ids.shape[0]
-        meta = {"B": B, "G": batch.group_size, "weight_version": batch.weight_version, "fields": {}, "extras": {}}
+        G = batch.group_size
+        if balance:
+            plan = balanced_groups(batch.response_mask, G, world)
+        else:
+            plan = []
+            for r in range(world):
+                s0, e0 = group_shard_bounds(B, G, r, world)
+                plan.append(list(range(s0 // G, e0 // G)))
+        meta = {"B": B, "G": G, "weight_version": batch.weight_version, "plan": plan, "rows": [], "extras": {},
+                "extras_order": list(batch.extras)}
         for f in fields:
             t = getattr(batch, f)
-            meta["fields"][f] = None if t is None else (tuple(t.shape), t.dtype)
+            meta["rows"].append((f, None if t is None else (tuple(t.shape), t.dtype)))
         for k, v in batch.extras.items():
             if isinstance(v, torch.Tensor):
-                meta["extras"][k] = ("rows" if (v.dim() >= 1 and v.shape[0] == B) else "whole", tuple(v.shape), v.dtype)
+                if v.dim() >= 1 and v.shape[0] == B:
+                    meta["rows"].append(("extras." + k, (tuple(v.shape), v.dtype)))
+                else:
+                    meta["extras"][k] = ("whole", tuple(v.shape), v.dtype)
             else:
                 meta["extras"][k] = ("object", v, None)
         obj = [meta]
@@ -159,41 +175,65 @@ def scatter_batch(batch: RolloutBatch | None, src: int = 0, group=None,
         obj = [None]
     dist.broadcast_object_list(obj, src=src_global, group=group)
     meta = obj[0]
-    B, G = meta["B"], meta["G"]
-    bounds = [group_shard_bounds(B, G, r, world) for r in range(world)]
-    s, e = bounds[rank]
+    G, plan = meta["G"], meta["plan"]
+    row_fields = [(name, m) for name, m in meta["rows"] if m is not None]
 
-    def move(name, full, shape, dtype, rows: bool):
-        """Rank src sends slices (rows) or the whole tensor; returns this rank's part."""
-        if rows:
-            my_shape = (e - s,) + tuple(shape[1:])
-            if rank == src:
-                for r in range(world):
-                    if r == src:
-                        continue
-                    rs, re_ = bounds[r]
-                    dist.send(full[rs:re_].contiguous().to(device), dst=dist.get_global_rank(group, r)
-                              if group is not None else r, group=group)
-                return full[s:e].contiguous().to(device)
-            out = torch.empty(my_shape, dtype=dtype, device=device)
-            dist.recv(out, src=src_global, group=group)
-            return out
-        out = full.contiguous().to(device) if rank == src else torch.empty(shape, dtype=dtype, device=device)
-        dist.broadcast(out, src=src_global, group=group)
-        return out
+    def row_bytes(shape, dtype) -> int:
+        n = 1
+        for d in shape[1:]:
+            n *= d
+        return n * torch.empty((), dtype=dtype).element_size()
 
-    vals = {}
-    for f in fields:
-        m = meta["fields"][f]
-        if m is None:
-            vals[f] = None
-            continue
-        shape, dtype = m
-        vals[f] = move(f, getattr(batch, f) if rank == src else None, shape, dtype, rows=True)
+    def padded(n: int) -> int:  # keep every field's bytes 8-byte aligned inside a block
+        return (n + 7) // 8 * 8
+
+    def block_bytes(nrows: int) -> int:
+        return sum(padded(nrows * row_bytes(*m)) for _, m in row_fields)
+
+    rows_of = [len(p) * G for p in plan]
+    if rank == src:
+        def get(name):
+            return batch.extras[name[7:]] if name.startswith("extras.") else getattr(batch, name)
+
+        parts = []
+        for r in range(world):
+            idx = torch.tensor([g * G + j for g in plan[r] for j in range(G)], dtype=torch.long)
+            for name, (shape, dtype) in row_fields:
+                t = get(name)
+                x = t.index_select(0, idx.to(t.device)).contiguous()
+                b = x.view(torch.uint8).reshape(-1)
+                pad = padded(b.numel()) - b.numel()
+                parts.append(b.to(device))
+                if pad:
+                    parts.append(torch.zeros(pad, dtype=torch.uint8, device=device))
+        send = torch.cat(parts) if parts else torch.empty(0, dtype=torch.uint8, device=device)
+        in_splits = [block_bytes(rows_of[r]) for r in range(world)]
+    else:
+        send = torch.empty(0, dtype=torch.uint8, device=device)
+        in_splits = [0] * world
+    mine = block_bytes(rows_of[rank])
+    recv = torch.empty(mine, dtype=torch.uint8, device=device)
+    out_splits = [mine if q == src else 0 for q in range(world)]
+    dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
+
+    vals: dict = {f: None for f in fields}
     extras = {}
+    off = 0
+    nr = rows_of[rank]
+    for name, (shape, dtype) in row_fields:
+        nb = nr * row_bytes(shape, dtype)
+        t = recv[off:off + nb].view(dtype).reshape((nr,) + tuple(shape[1:]))
+        off += padded(nb)
+        if name.startswith("extras."):
+            extras[name[7:]] = t
+        else:
+            vals[name] = t
     for k, (kind, a, b) in meta["extras"].items():
         if kind == "object":
             extras[k] = a
         else:
-            extras[k] = move(k, batch.extras[k] if rank == src else None, a, b, rows=(kind == "rows"))
+            out = batch.extras[k].contiguous().to(device) if rank == src else torch.empty(a, dtype=b, device=device)
+            dist.broadcast(out, src=src_global, group=group)
+            extras[k] = out
+    extras = {k: extras[k] for k in meta["extras_order"]}
     return RolloutBatch(**vals, group_size=G, weight_version=meta["weight_version"], extras=extras)

@@ -7,8 +7,6 @@ current stream; nothing here computes on the CPU or falls back to ATen for the h
 
 from __future__ import annotations
 
-import os
-
 import torch
 
 from . import _native as N
@@ -350,8 +348,18 @@ def logits_logprob_raw(logits: torch.Tensor, ids: torch.Tensor, with_target: boo
 # K1: fused LM-head log-prob (policy.py:124-191)
 # ---------------------------------------------------------------------------------------------
 
-# bf16 dlogits workspace of one backward chunk; INVOKERL_B200_DS_CHUNK_BYTES overrides it.
-DEFAULT_DS_CHUNK_BYTES = int(os.environ.get("INVOKERL_B200_DS_CHUNK_BYTES", str(8 << 30)))
+# bf16 dlogits workspace of one backward chunk (8 GiB: 28,160 rows at V = 151936).  Callers that
+# want another size pass chunk_rows; set_ds_chunk_bytes changes the default for the process.
+DEFAULT_DS_CHUNK_BYTES = 8 << 30
+
+
+def set_ds_chunk_bytes(nbytes: int) -> int:
+    """Default bytes of the backward's dlogits chunk for later calls; returns the previous value."""
+    global DEFAULT_DS_CHUNK_BYTES
+    if nbytes < (1 << 20):
+        raise ValueError(f"dlogits chunk of {nbytes} bytes is too small")
+    prev, DEFAULT_DS_CHUNK_BYTES = DEFAULT_DS_CHUNK_BYTES, int(nbytes)
+    return prev
 
 
 def default_chunk_rows(N: int, V: int, budget_bytes: int | None = None) -> int:
@@ -414,8 +422,15 @@ def lmhead_status(ws: torch.Tensor) -> None:
     call("ikrl_lmhead_status", ptr(ws), N.byref(st), N.stream_of(ws.device))
 
 
-# Tests set this to read the device status word after every tensor-core call (a host sync).
-_CHECK_DEVICE_STATUS = os.environ.get("INVOKERL_B200_CHECK_STATUS", "0") == "1"
+# When set (set_check_device_status), every tensor-core call reads its device status word
+# afterwards and raises on a recorded fault; this synchronises the host once per call.
+_CHECK_DEVICE_STATUS = False
+
+
+def set_check_device_status(enable: bool) -> bool:
+    global _CHECK_DEVICE_STATUS
+    prev, _CHECK_DEVICE_STATUS = _CHECK_DEVICE_STATUS, bool(enable)
+    return prev
 
 
 class LMHeadLogProb(torch.autograd.Function):

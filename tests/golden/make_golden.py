@@ -1,8 +1,10 @@
 """Generate the golden fixtures of tests/golden/ by running the reference implementation.
 
-Run in a container that has the reference checkout (invokerl, pure Python over PyTorch):
+Run in a container that has the reference checkout (invokerl, pure Python over PyTorch), naming
+its root either way:
 
-    PYTHONPATH=<reference checkout> python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference <reference checkout>
+    INVOKERL_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Each case stores its seeded inputs (or, for the one large case, the seed that regenerates them)
 and the reference's outputs: advantages, loss, metrics dict and d loss / d new_log_probs for the
@@ -23,7 +25,23 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 
-REF = os.environ.get("INVOKERL_REFERENCE", "/root/reference")
+def _reference_root() -> str:
+    """Root of the reference checkout: --reference PATH, else $INVOKERL_REFERENCE; no default."""
+    if "--reference" in sys.argv:
+        i = sys.argv.index("--reference")
+        if i + 1 >= len(sys.argv):
+            raise SystemExit("--reference needs a path")
+        root = sys.argv[i + 1]
+        del sys.argv[i:i + 2]
+    else:
+        root = os.environ.get("INVOKERL_REFERENCE", "")
+    if not root or not (Path(root) / "invokerl" / "policy.py").exists():
+        raise SystemExit("name the reference checkout with --reference PATH or INVOKERL_REFERENCE=PATH "
+                         "(the directory that contains invokerl/policy.py)")
+    return root
+
+
+REF = _reference_root()
 if REF not in sys.path:
     sys.path.insert(0, REF)
 

@@ -119,7 +119,16 @@ def test_row_sharded_loss_matches_global_gloo():
     torch.testing.assert_close(grad, g, rtol=1e-5, atol=1e-8)
 
 
-def _scatter_worker(rank, world, port, q):
+def _scatter_source_batch():
+    b = rollout_batch(6, 4, 48, prompt_len=(4, 16), completion_len=(4, 30), seed=31)
+    b.extras["truncated"] = torch.arange(24) % 5 == 0
+    b.extras["note"] = "kept"
+    b.extras["scale"] = torch.tensor([2.0, 3.0])
+    b.extras["values"] = torch.randn(24, 48, generator=torch.Generator().manual_seed(3))
+    return b
+
+
+def _scatter_worker(rank, world, port, q, balance):
     import datetime
 
     from invokerl_b200.distributed import scatter_batch
@@ -127,40 +136,88 @@ def _scatter_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        b = None
-        if rank == 0:
-            b = rollout_batch(6, 4, 48, prompt_len=(4, 16), completion_len=(4, 30), seed=31)
-            b.extras["truncated"] = torch.arange(24) % 5 == 0
-            b.extras["note"] = "kept"
-            b.extras["scale"] = torch.tensor([2.0, 3.0])
-        local = scatter_batch(b, src=0, device="cpu")
-        q.put((rank, local.token_ids, local.rewards, local.response_mask, local.extras["truncated"],
-               local.extras["note"], local.extras["scale"], local.group_size))
+        b = _scatter_source_batch() if rank == 0 else None
+        local = scatter_batch(b, src=0, device="cpu", balance=balance)
+        q.put((rank, {k: v for k, v in vars(local).items()}))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_scatter_batch_sends_each_rank_its_groups(world):
+@pytest.mark.parametrize("world,balance", [(2, True), (3, True), (2, False), (3, False), (8, True)])
+def test_scatter_batch_sends_each_rank_its_groups(world, balance):
+    """Every rank receives exactly the rows shard_batch gives it (balanced by work, or contiguous),
+    with every field, row-shaped extras sharded and the other extras whole; with 8 ranks and 6
+    groups two ranks receive no rows."""
     from invokerl_b200.distributed import shard_batch
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_scatter_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_scatter_worker, args=(r, world, port, q, balance)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=120) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    full = rollout_batch(6, 4, 48, prompt_len=(4, 16), completion_len=(4, 30), seed=31)
-    full.extras["truncated"] = torch.arange(24) % 5 == 0
-    for rank, ids, rew, rm, tr, note, scale, G in got:
-        ref = shard_batch(full, rank, world)
-        assert torch.equal(ids, ref.token_ids) and torch.equal(rew, ref.rewards)
-        assert torch.equal(rm, ref.response_mask) and torch.equal(tr, ref.extras["truncated"])
-        assert note == "kept" and torch.equal(scale, torch.tensor([2.0, 3.0])) and G == 4
+    full = _scatter_source_batch()
+    nrows = 0
+    for rank, loc in got:
+        ref = shard_batch(full, rank, world, balance=balance)
+        for f in ("token_ids", "prompt_mask", "response_mask", "attention_mask", "rewards", "old_log_probs",
+                  "ref_log_probs", "group_ids"):
+            assert loc[f].dtype == getattr(ref, f).dtype, f
+            assert torch.equal(loc[f], getattr(ref, f)), f
+        assert loc["token_rewards"] is None and loc["group_size"] == 4
+        assert list(loc["extras"]) == list(full.extras)
+        assert torch.equal(loc["extras"]["new_log_probs"], ref.extras["new_log_probs"])
+        assert torch.equal(loc["extras"]["truncated"], ref.extras["truncated"])
+        assert torch.equal(loc["extras"]["values"], ref.extras["values"])
+        assert loc["extras"]["note"] == "kept" and torch.equal(loc["extras"]["scale"], torch.tensor([2.0, 3.0]))
+        nrows += loc["token_ids"].shape[0]
+    assert nrows == 24
+
+
+def _pair_share_worker(rank, world, port, q, pairs):
+    import datetime
+
+    from invokerl_b200.algorithms import SimPO
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        loss = torch.tensor(0.5 + rank, requires_grad=True)
+        metrics = torch.arange(8, dtype=torch.float32) + 10 * rank
+        share, mt = SimPO(row_sharded=True)._pair_share(loss, metrics, 2 * pairs[rank])
+        share.backward()
+        q.put((rank, float(share), mt, float(loss.grad)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("pairs", [(3, 5), (0, 4), (0, 0)])
+def test_pair_share_over_ranks_gloo(pairs):
+    """SimPO / DPO row shards: the loss share is local mean x local pairs / global pairs and the
+    metrics are pair-weighted means; a rank without pairs, or a batch with none at all, gives a
+    zero share and no division by zero."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_pair_share_worker, args=(r, world, port, q, pairs)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    tot = max(1, sum(pairs))
+    want_mt = sum((torch.arange(8, dtype=torch.float64) + 10 * r) * pairs[r] for r in range(world)) / tot
+    for rank, share, mt, grad in got:
+        assert abs(share - (0.5 + rank) * pairs[rank] / tot) <= 1e-6
+        assert abs(grad - pairs[rank] / tot) <= 1e-6
+        assert torch.isfinite(mt).all()
+        torch.testing.assert_close(mt, want_mt.float(), rtol=1e-6, atol=1e-6)
 
 
 def test_balanced_groups_cover_every_group_once_and_balance_work():

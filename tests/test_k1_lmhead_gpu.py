@@ -6,6 +6,7 @@ import torch
 
 import oracle
 from helpers import load
+from invokerl_b200 import _native as N
 from invokerl_b200 import ops
 from invokerl_b200.synthetic import lmhead_inputs
 
@@ -22,8 +23,6 @@ def check_device_status(monkeypatch):
 @pytest.fixture(params=["cta_pairs", "single_cta"])
 def kernel_variant(request):
     """Run a test on both K1 GEMM kernels: CTA pairs (cta_group::2) and single CTAs."""
-    from invokerl_b200 import _native as N
-
     prev = N.lib().ikrl_lmhead_set_cta_pairs(1 if request.param == "cta_pairs" else 0)
     yield request.param
     N.lib().ikrl_lmhead_set_cta_pairs(prev)
@@ -148,19 +147,10 @@ def test_full_size_properties(N, H, kernel_variant):
 
 
 def _bwd(h, w, t, lse, g, skip: bool, **kw):
-    import os
-
-    prev = os.environ.get("INVOKERL_B200_SKIP_ZERO_ROWS")
-    os.environ["INVOKERL_B200_SKIP_ZERO_ROWS"] = "1" if skip else "0"
-    try:
+    with N.tuning(skip_zero_rows=1 if skip else 0):
         out = ops.lmhead_backward_raw(h, w, t, lse, g, **kw)
         torch.cuda.synchronize()
         return out
-    finally:
-        if prev is None:
-            del os.environ["INVOKERL_B200_SKIP_ZERO_ROWS"]
-        else:
-            os.environ["INVOKERL_B200_SKIP_ZERO_ROWS"] = prev
 
 
 @pytest.mark.parametrize("N,H,V,chunk,frac", [

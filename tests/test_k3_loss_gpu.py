@@ -6,6 +6,7 @@ import torch
 
 import oracle
 from helpers import ALGO_CASES, assert_metrics_close, load, make_batch
+from invokerl_b200 import _native as N
 from invokerl_b200 import ops
 from invokerl_b200.algorithms import DAPO, DPO, GRPO, PPO, SimPO
 from invokerl_b200.synthetic import rollout_batch
@@ -134,10 +135,14 @@ def test_group_size_one_gives_nan_like_torch_std():
 @pytest.mark.parametrize("lean", ["2", "1", "0"])
 @pytest.mark.parametrize("kl_type,lp_dtype", [("schulman", torch.float32), ("simple", torch.float32),
                                              ("schulman", torch.bfloat16)])
-def test_grpo_kernel_variants_agree_with_oracle(lean, kl_type, lp_dtype, monkeypatch):
+def test_grpo_kernel_variants_agree_with_oracle(lean, kl_type, lp_dtype):
     """The three GRPO loss kernels (bulk-copy staged, register loads, general clipped-ratio) on a
     batch of 23 full 1024-token tiles plus a 448-token partial tile."""
-    monkeypatch.setenv("INVOKERL_B200_LEAN_LOSS", lean)
+    with N.tuning(loss_kernel=int(lean)):
+        _grpo_variant_case(kl_type, lp_dtype)
+
+
+def _grpo_variant_case(kl_type, lp_dtype):
     b = rollout_batch(6, 4, 1000, prompt_len=(16, 200), completion_len=(100, 800), seed=77,
                       lp_dtype=lp_dtype)
     nl = b.extras["new_log_probs"]

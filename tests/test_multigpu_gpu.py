@@ -218,3 +218,50 @@ def test_two_rank_algorithms_match_reference_golden(name):
     assert_metrics_close(metrics, out["metrics"], rtol=1e-4, atol=1e-6)
     bf = out["grad"].dtype == torch.bfloat16
     torch.testing.assert_close(grad.float(), out["grad"].float(), rtol=1e-2 if bf else 1e-4, atol=1e-7)
+
+
+def _scatter_nccl_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from invokerl_b200.distributed import scatter_batch, shard_batch
+    from invokerl_b200.synthetic import rollout_batch
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        full = rollout_batch(6, 8, 256, prompt_len=(8, 64), completion_len=(16, 180), vocab=V, seed=12)
+        full.extras["truncated"] = torch.arange(48) % 7 == 0
+        local = scatter_batch(full if rank == 0 else None, src=0)
+        ref = shard_batch(full, rank, world, balance=True)
+        ok = local.token_ids.device == dev
+        for f in ("token_ids", "prompt_mask", "response_mask", "attention_mask", "rewards", "old_log_probs",
+                  "ref_log_probs", "group_ids"):
+            ok = ok and torch.equal(getattr(local, f).cpu(), getattr(ref, f))
+        for k in ("new_log_probs", "truncated"):
+            ok = ok and torch.equal(local.extras[k].cpu(), ref.extras[k])
+        q.put((rank, bool(ok), int(local.token_ids.shape[0])))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_scatter_batch_over_nccl_matches_balanced_shards():
+    """Rollout distribution over NCCL (replacing invokerl/distributed.py:236-302): each rank
+    receives, on its own GPU, exactly the work-balanced groups shard_batch(balance=True) gives it."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_scatter_nccl_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in got), got
+    assert sum(n for _, _, n in got) == 48

@@ -126,10 +126,56 @@ def test_lmhead_launch_plan(lib, gemm, rows, H, want):
     assert _plan(gemm, rows, H) == want
 
 
-def test_lmhead_launch_plan_balance_off(lib, monkeypatch):
-    monkeypatch.setenv("INVOKERL_B200_BALANCE_SPLITS", "0")
-    assert _plan(1, 8700, 4096) == (2, 297, 60, 5)
-    assert _plan(3, 10092, 1024) == (2, 2, 1, 2)
+def test_lmhead_launch_plan_balance_off(lib):
+    from invokerl_b200 import _native as N
+
+    with N.tuning(balance_splits=0):
+        assert _plan(1, 8700, 4096) == (2, 297, 60, 5)
+        assert _plan(3, 10092, 1024) == (2, 2, 1, 2)
+    assert _plan(1, 8700, 4096) == (2, 297, 23, 13)
+
+
+def test_lmhead_launch_plan_follows_the_knobs(lib):
+    from invokerl_b200 import _native as N
+
+    with N.tuning(cta_pairs=0):
+        assert _plan(0, 524288, 4096)[0] == 0
+    with N.tuning(wide=0):
+        assert _plan(0, 524288, 4096)[0] == 1
+    with N.tuning(wide=2):  # the K >= 1024 rule without the dH balance choice
+        assert _plan(3, 10092, 1024) == (2, 2, 1, 2)
+    with N.tuning(l2_budget_mb=8):  # less L2 for resident rows -> more vocabulary splits
+        assert _plan(0, 524288, 4096)[3] > 4
+
+
+def test_tuning_knobs_range_checks_and_defaults(lib):
+    """ikrl_set_tuning validates on the host; IKRL_TUNE_DEFAULT restores the shipped default; the
+    library reads no environment variable."""
+    from invokerl_b200 import _native as N
+
+    defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": 1, "pace_kb": 64,
+                "pace_lag": 1, "balance_splits": 1, "l2_policy": -1, "l2_budget_mb": 0, "loss_kernel": 1}
+    assert {k: N.get_tuning(k) for k in N.TUNE} == defaults
+    prev = N.set_tuning("pace_kb", 7)
+    assert prev == 64 and N.get_tuning("pace_kb") == 7
+    N.set_tuning("pace_kb", None)
+    assert N.get_tuning("pace_kb") == 64
+    for knob, bad in [("l2_policy", 13), ("l2_policy", 30), ("pace_kb", 0), ("wide", 3), ("loss_kernel", 3)]:
+        with pytest.raises(N.IkrlError, match="ikrl_set_tuning"):
+            N.set_tuning(knob, bad)
+    assert {k: N.get_tuning(k) for k in N.TUNE} == defaults
+    with pytest.raises(N.IkrlError, match="unknown knob"):
+        N.call("ikrl_set_tuning", N.i32(99), N.i64(0), None)
+    src = "".join(p.read_text() for p in sorted((ROOT / "invokerl_b200" / "csrc").glob("*.cu")))
+    assert "getenv" not in src
+
+
+def test_no_alloc_limits_match_the_documented_row_counts(lib):
+    """The allocation-free forward's 4 MiB scratch holds the forward workspace of up to 61,672 rows
+    at H = 4096 and 116,496 at H = 1024 (V = 151936), the limits its documentation states."""
+    w = lib.ikrl_lmhead_fwd_workspace_bytes
+    for H, rows in [(4096, 61672), (1024, 116496)]:
+        assert w(rows, H, 151936) <= 4 << 20 < w(rows + 1, H, 151936)
 
 
 def test_lmhead_launch_plan_rejects_bad_arguments(lib):

@@ -1,11 +1,14 @@
 """The allocation-free LM-head forward (`ikrl_lmhead_logprob_fwd_noalloc`).
 
-Callers that cannot allocate device memory at the point of the call -- a stream being captured
-into a CUDA graph, or a host application whose own allocator owns the GPU's memory -- use this
-entry point: its scratch is a fixed 4 MiB array inside the library.  These tests call it through
-the C ABI twice in a row (different shapes, so the second call runs on whatever the first left
-in the shared array) and check each result against the workspace-taking entry point, and check
-that a call too large for the built-in scratch is refused before any GPU work.
+Some callers cannot allocate device memory when they need log-probs: a host application whose own
+allocator owns all of the GPU's memory and forbids side allocations, or a framework whose caching
+pool has already reserved the free memory.  They use this entry point: its scratch is a fixed
+4 MiB array inside the library.  These tests call it through the C ABI twice in a row (different
+shapes, so the second call runs on whatever the first left in the shared array) and check each
+result bit for bit against the workspace-taking entry point, which runs the same kernels with the
+same launch plan, and against the CPU oracle; they read the device status word of the built-in
+scratch after every call, and check that a call too large for the scratch is refused before any
+GPU work.
 
 The file is named so that pytest collects it last.
 """
@@ -13,6 +16,7 @@ The file is named so that pytest collects it last.
 import pytest
 import torch
 
+import oracle
 from invokerl_b200 import _native as N
 from invokerl_b200.synthetic import lmhead_inputs
 
@@ -42,6 +46,12 @@ def forward_no_alloc(h, w, t):
     return logp, lse
 
 
+def no_alloc_status() -> int:
+    st = N.c_int32(-1)
+    N.call("ikrl_lmhead_noalloc_status", N.byref(st), N.stream_of(torch.device(DEV)))
+    return int(st.value)
+
+
 @pytest.mark.parametrize("shapes", [[(512, 1024, 151936), (200, 256, 5000)]])
 def test_no_alloc_forward_matches_workspace_forward_twice(shapes):
     for i, (n, H, V) in enumerate(shapes):
@@ -50,10 +60,14 @@ def test_no_alloc_forward_matches_workspace_forward_twice(shapes):
         lp_ref, lse_ref = forward_with_workspace(h, w, t)
         lp, lse = forward_no_alloc(h, w, t)
         torch.cuda.synchronize()
+        assert no_alloc_status() == 0
         assert torch.isfinite(lp).all()
-        # the same kernels on the same inputs; the tests' log-prob tolerance is 2e-3 absolute
-        assert float((lp - lp_ref).abs().max()) <= 2e-3
-        assert float((lse - lse_ref).abs().max()) <= 2e-3
+        # the same kernels, launch plan and fixed-order combine on the same inputs: bit-identical
+        assert torch.equal(lp, lp_ref)
+        assert torch.equal(lse, lse_ref)
+        # and the oracle's fp32 log-probs within the tests' log-prob tolerance, 2e-3 absolute
+        lp_o = oracle.lmhead_logprob(li.hidden, li.weight, li.targets)
+        assert float((lp.cpu() - lp_o).abs().max()) <= 2e-3
 
 
 def test_no_alloc_forward_rejects_rows_beyond_its_scratch():
