@@ -167,6 +167,35 @@ def batch_bytes(b) -> int:
     return sum(v.numel() * v.element_size() for v in vars(b).values() if isinstance(v, torch.Tensor))
 
 
+_REF_PKG: list = []
+
+
+def reference_package():
+    """The unmodified reference package (invokerl, pure Python) from baseline/_ref, imported once;
+    None when it is not there."""
+    if not _REF_PKG:
+        ref_root = ROOT / "baseline" / "_ref"
+        mod = None
+        if (ref_root / "invokerl" / "policy.py").exists():
+            if str(ref_root) not in sys.path:
+                sys.path.insert(0, str(ref_root))
+            import invokerl.algorithms
+            import invokerl.policy
+
+            mod = invokerl
+        _REF_PKG.append(mod)
+    return _REF_PKG[0]
+
+
+def time_cpu(fn, steps: int) -> float:
+    """Seconds per call of fn on the host (one untimed call first)."""
+    fn()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn()
+    return (time.perf_counter() - t0) / max(1, steps)
+
+
 # ---- workloads -------------------------------------------------------------------------------------
 
 
@@ -309,7 +338,56 @@ class LMHeadGRPO:
         return one, h2d, d2h
 
     def cpu_sample(self, rows, steps):
-        """Reference arithmetic on the host CPU: fp32 LM-head log-probs + GRPO loss + autograd."""
+        """The reference's own CPU path on a bounded sample: invokerl's PolicyModel._chunked_lm_head_ce
+        (policy.py:124-191; bf16 F.linear + -F.cross_entropy) and its GRPO compute_advantages /
+        compute_loss (grpo.py:46-143) + autograd, on G sequences of rows/G tokens.  Without the
+        reference package, the oracle's fp32 restatement of the same arithmetic."""
+        ref = reference_package()
+        if ref is None:
+            return self._cpu_sample_port(rows, steps)
+        from invokerl.algorithms import GRPO as RefGRPO
+        from invokerl.algorithms import RolloutBatch as RefBatch
+        from invokerl.policy import PolicyModel as RefPolicy
+
+        from invokerl_b200.synthetic import lmhead_inputs
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        G = self.G
+        Ts = max(1, rows // G)
+        rows = G * Ts
+        li = lmhead_inputs(rows, self.H, V, seed=3)
+        head = torch.nn.Linear(self.H, V, bias=False, dtype=torch.bfloat16)
+        with torch.no_grad():
+            head.weight.copy_(li.weight)
+        pm = RefPolicy.__new__(RefPolicy)
+        pm.model = torch.nn.Module()
+        pm.model.lm_head = head
+        hidden = li.hidden.view(G, Ts, self.H).clone().requires_grad_(True)
+        targets = li.targets.view(G, Ts)
+        g = torch.Generator().manual_seed(5)
+        rm = torch.rand(G, Ts, generator=g) < 0.6
+        rm[:, 0] = True
+        old = -torch.empty(G, Ts).exponential_(1.0, generator=g)
+        rb = RefBatch(token_ids=targets, prompt_mask=~rm, response_mask=rm, attention_mask=torch.ones_like(rm),
+                      rewards=torch.bernoulli(torch.full((G,), 0.5), generator=g), token_rewards=None,
+                      old_log_probs=old, ref_log_probs=old + 0.1 * torch.randn(G, Ts, generator=g),
+                      group_ids=torch.zeros(G, dtype=torch.long), group_size=G)
+        algo = RefGRPO(clip_eps=0.2, beta=0.04)
+
+        def one():
+            hidden.grad = None
+            head.weight.grad = None
+            lp = pm._chunked_lm_head_ce(hidden, targets, 64)
+            adv = algo.compute_advantages(rb)
+            loss, _ = algo.compute_loss(lp, rb, adv)
+            loss.backward()
+
+        dt = time_cpu(one, steps)
+        return rows / dt, dt, (f"{G} sequences x {Ts} tokens = {rows} rows x H={self.H} x V={V} per step: invokerl's "
+                               "own _chunked_lm_head_ce (bf16) + GRPO + autograd on the host CPU"), "reference"
+
+    def _cpu_sample_port(self, rows, steps):
+        """The oracle's fp32 restatement of the same step (reference package absent)."""
         import oracle
         from invokerl_b200.synthetic import lmhead_inputs
 
@@ -328,20 +406,15 @@ class LMHeadGRPO:
         def one():
             hh.grad = None
             ww.grad = None
-            logits = hh @ ww.t()
-            lp = torch.gather(logits, 1, li.targets[:, None]).squeeze(1) - torch.logsumexp(logits, dim=1)
+            lp = oracle.lmhead_logprob(hh, ww, li.targets)
             ratio = torch.exp(lp - old)
             pl = -torch.minimum(ratio * adv, torch.clamp(ratio, 0.8, 1.2) * adv)
             d = ref - lp
             loss = ((pl + 0.04 * (torch.exp(d) - d - 1)) * mask).sum() / mask.sum().clamp(min=1)
             loss.backward()
 
-        one()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            one()
-        dt = (time.perf_counter() - t0) / steps
-        return rows / dt, dt, f"{rows} rows x H={self.H} x V={V} per step (fp32 torch on the host CPU)"
+        dt = time_cpu(one, steps)
+        return rows / dt, dt, f"{rows} rows x H={self.H} x V={V} per step (the oracle, fp32 torch on the host CPU)", "port"
 
 
 class LogitsLogProb:
@@ -405,23 +478,22 @@ class LogitsLogProb:
         return one, h2d, d2h
 
     def cpu_sample(self, rows, steps):
+        """The reference's FSDP-branch log-prob (policy.py:100-104): -F.cross_entropy on bf16 logits
+        [rows, V], reduction="none", and its autograd, on the host CPU."""
+        from invokerl_b200.synthetic import logits_inputs
+
         torch.set_num_threads(os.cpu_count() or 1)
-        g = torch.Generator().manual_seed(1)
-        x = (2.0 * torch.randn(rows, V, generator=g)).float().requires_grad_(True)
-        t = torch.randint(0, V, (rows,), generator=g)
-        up = torch.randn(rows, generator=g)
+        logits, t, up = logits_inputs(rows, V, seed=1)
+        x = logits.requires_grad_(True)
 
         def one():
             x.grad = None
             lp = -torch.nn.functional.cross_entropy(x, t, reduction="none")
-            lp.backward(up)
+            lp.backward(up.to(lp.dtype))
 
-        one()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            one()
-        dt = (time.perf_counter() - t0) / steps
-        return rows / dt, dt, f"{rows} rows x V={V} per step (fp32 -F.cross_entropy + autograd on the host CPU)"
+        dt = time_cpu(one, steps)
+        return rows / dt, dt, (f"{rows} rows x V={V} bf16 per step: invokerl's FSDP-branch -F.cross_entropy "
+                               "(policy.py:100-104) + autograd on the host CPU"), "reference"
 
 
 class GRPOHooks:
@@ -546,25 +618,44 @@ class GRPOHooks:
         return one, h2d, d2h
 
     def cpu_sample(self, rows, steps):
-        import oracle
+        """invokerl's own GRPO compute_advantages + compute_loss + backward (grpo.py:46-143) on the
+        host CPU, on the first `rows` prompt groups of the same synthetic batch (all of them when
+        rows is 0)."""
         from invokerl_b200.synthetic import rollout_batch
 
+        ref = reference_package()
         torch.set_num_threads(os.cpu_count() or 1)
-        b = rollout_batch(self.P, self.G, self.T, prompt_len=self.pl, completion_len=self.cl, seed=0)
+        P = self.P if rows <= 0 else min(self.P, rows)
+        b = rollout_batch(P, self.G, self.T, prompt_len=self.pl, completion_len=self.cl, seed=0)
+        new = b.extras["new_log_probs"]
+        if ref is None:
+            import oracle
 
-        def one():
-            adv = oracle.group_advantages(b.rewards, b.response_mask, self.G)
-            oracle.clip_ratio_loss(b.extras["new_log_probs"], b.old_log_probs, b.ref_log_probs, adv,
-                                   b.response_mask, b.rewards)
+            def one():
+                adv = oracle.group_advantages(b.rewards, b.response_mask, self.G)
+                oracle.clip_ratio_loss(new, b.old_log_probs, b.ref_log_probs, adv, b.response_mask, b.rewards)
 
-        one()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            one()
-        dt = (time.perf_counter() - t0) / steps
-        n = self.P * self.G * self.T
-        return n / dt, dt, f"the whole batch ({n} tokens) per step (fp32 torch on the host CPU)"
+            kind, what = "port", "the oracle's restatement"
+        else:
+            from invokerl.algorithms import GRPO as RefGRPO
+            from invokerl.algorithms import RolloutBatch as RefBatch
 
+            rb = RefBatch(token_ids=b.token_ids, prompt_mask=b.prompt_mask, response_mask=b.response_mask,
+                          attention_mask=b.attention_mask, rewards=b.rewards, token_rewards=None,
+                          old_log_probs=b.old_log_probs, ref_log_probs=b.ref_log_probs, group_ids=b.group_ids,
+                          group_size=self.G)
+            algo = RefGRPO(clip_eps=0.2, beta=0.04)
+
+            def one():
+                lp = new.clone().requires_grad_(True)
+                adv = algo.compute_advantages(rb)
+                loss, _ = algo.compute_loss(lp, rb, adv)
+                loss.backward()
+
+            kind, what = "reference", "invokerl's own GRPO"
+        dt = time_cpu(one, steps)
+        n = P * self.G * self.T
+        return n / dt, dt, f"{P * self.G} rows x T={self.T} ({n} tokens) per step: {what} + autograd on the host CPU", kind
 
 
 def init_single_rank_group(device) -> None:
@@ -754,138 +845,194 @@ class E2EGRPO:
 
 WORKLOADS = {"lmhead-8b": LMHeadGRPO, "lmhead-0.6b": LMHeadGRPO, "logits": LogitsLogProb, "grpo": GRPOHooks,
              "grpo-hbm": GRPOHooks, "e2e-0.6b": E2EGRPO}
-CPU_ROWS = {"lmhead-8b": 32, "lmhead-0.6b": 96, "logits": 1024, "grpo": 0, "grpo-hbm": 0, "e2e-0.6b": 0}
+# Rows of the bounded CPU sample per step (the reference's CPU path; 0 = every prompt group).
+CPU_ROWS = {"lmhead-8b": 32, "lmhead-0.6b": 96, "logits": 1024, "grpo": 0, "grpo-hbm": 8, "e2e-0.6b": 0}
+# Lines the default run adds after the headline, each a workload of its own with the same keys.
+SECONDARY = ("logits", "lmhead-0.6b", "grpo-hbm")
+SECONDARY_STEPS = {"logits": 20, "lmhead-0.6b": 10, "grpo-hbm": 20}
+
+# DRAM traffic of the dominant kernel per unit of work, from ncu captures (dram__bytes_read.sum +
+# dram__bytes_write.sum); the line's roofline.traffic is this figure times the units of one step.
+TRAFFIC = {}
 
 
-def run_native(args, rank, world, device) -> dict | None:
-    from invokerl_b200 import _native, ops
+class Timed:
+    """Device time of `steps` calls of `step` after `warmup` untimed ones, bracketed by a barrier and
+    a synchronize on both sides and taken as the max over ranks, with nvidia-smi clocks sampled
+    during the timed region and this library's launch count."""
 
-    wl = WORKLOADS[args.workload](args.workload, args)
-    wl.setup(rank, world, device)
-    timer = EventTimer()
-    for name in wl.timed_functions():
-        setattr(ops, name, timer.wrap(getattr(ops, name)))
+    def __init__(self, step, steps, warmup, world, device, timer=None):
+        from invokerl_b200 import _native
 
-    for _ in range(args.warmup):
-        wl.step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    sampler = ClockSampler(device.index)
-    sampler.start()
-    time.sleep(0.3)
-    launches0 = _native.lib().ikrl_launch_count()
-    timer.active = True
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    start.record()
-    loss = 0.0
-    for _ in range(args.steps):
-        loss, _ = wl.step()
-    end.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    timer.active = False
-    launches = _native.lib().ikrl_launch_count() - launches0
-    clocks = sampler.stop()
-    ms = start.elapsed_time(end)
-    kms = timer.total_ms() if timer.pairs else ms
-    t = torch.tensor([ms, kms], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, kms = float(t[0]), float(t[1])
-
-    # Outside the timed region: the data-parallel reduction of the LM-head weight gradient that a
-    # DP / FSDP layer would add per step (one NCCL all-reduce of dW in its dtype), reported apart.
-    dw_allreduce = None
-    if world > 1 and isinstance(wl, LMHeadGRPO) and wl.weight.grad is not None:
-        gw = wl.weight.grad
-        for _ in range(2):
-            dist.all_reduce(gw)
-        torch.cuda.synchronize()
-        dist.barrier()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(5):
-            dist.all_reduce(gw)
-        s1.record()
-        torch.cuda.synchronize()
-        ta = torch.tensor([s0.elapsed_time(s1) / 5], dtype=torch.float64, device=device)
-        dist.all_reduce(ta, op=dist.ReduceOp.MAX)
-        nbytes = gw.numel() * gw.element_size()
-        dw_allreduce = {"ms": float(ta[0]), "bytes": int(nbytes), "dtype": str(gw.dtype).replace("torch.", ""),
-                        "bus_gbs": 2 * (world - 1) / world * nbytes / (float(ta[0]) / 1e3) / 1e9,
-                        "note": "NCCL all-reduce of dW per step, not in the timed region"}
-
-    e2e = None
-    if not args.no_e2e:
-        one, h2d, d2h = wl.e2e()
-        one()
+        for _ in range(warmup):
+            step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        n = max(1, min(args.steps, 3))
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(n):
-            one()
-        e.record()
+        sampler = ClockSampler(device.index)
+        sampler.start()
+        time.sleep(0.3)
+        launches0 = _native.lib().ikrl_launch_count()
+        if timer is not None:
+            timer.active = True
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
-        te = torch.tensor([s.elapsed_time(e)], dtype=torch.float64, device=device)
         if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": wl.tokens_per_step() * n / (float(te[0]) / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n}
+            dist.barrier()
+        start.record()
+        out = None
+        for _ in range(steps):
+            out = step()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if timer is not None:
+            timer.active = False
+        self.launches = int(_native.lib().ikrl_launch_count() - launches0)
+        self.clocks = sampler.stop()
+        ms = start.elapsed_time(end)
+        kms = timer.total_ms() if (timer is not None and timer.pairs) else ms
+        t = torch.tensor([ms, kms], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        self.ms, self.kms = float(t[0]), float(t[1])
+        self.has_kernel_time = timer is not None and bool(timer.pairs)
+        self.out = out
+        self.steps = steps
+
+
+def time_e2e(one, n, world, device) -> float:
+    """ms for n end-to-end steps (max over ranks), after one untimed step."""
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        one()
+    e.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([s.elapsed_time(e)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    return float(te[0])
+
+
+def run_native(args, key, rank, world, device, steps, warmup, cpu_baseline=True) -> dict | None:
+    """One JSON line for workload `key` on this package's kernels."""
+    from invokerl_b200 import ops
+
+    wl = WORKLOADS[key](key, args)
+    wl.setup(rank, world, device)
+    timer = EventTimer()
+    saved = {}
+    for name in wl.timed_functions():
+        saved[name] = getattr(ops, name)
+        setattr(ops, name, timer.wrap(saved[name]))
+    try:
+        tm = Timed(wl.step, steps, warmup, world, device, timer)
+        loss = tm.out[0] if tm.out else 0.0
+
+        # Outside the timed region: the data-parallel reduction of the LM-head weight gradient that a
+        # DP / FSDP layer adds per step (one NCCL all-reduce of dW in its dtype), timed apart and also
+        # added to the step in value_with_dw_allreduce.
+        dw_allreduce = None
+        if world > 1 and isinstance(wl, LMHeadGRPO) and wl.weight.grad is not None:
+            gw = wl.weight.grad
+            for _ in range(2):
+                dist.all_reduce(gw)
+            torch.cuda.synchronize()
+            dist.barrier()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for _ in range(5):
+                dist.all_reduce(gw)
+            s1.record()
+            torch.cuda.synchronize()
+            ta = torch.tensor([s0.elapsed_time(s1) / 5], dtype=torch.float64, device=device)
+            dist.all_reduce(ta, op=dist.ReduceOp.MAX)
+            nbytes = gw.numel() * gw.element_size()
+            dw_allreduce = {"ms": float(ta[0]), "bytes": int(nbytes), "dtype": str(gw.dtype).replace("torch.", ""),
+                            "bus_gbs": 2 * (world - 1) / world * nbytes / (float(ta[0]) / 1e3) / 1e9,
+                            "note": "NCCL all-reduce of dW per step, timed after the timed region"}
+        rank_rows = None
+        if world > 1 and isinstance(wl, LMHeadGRPO):
+            mine = torch.tensor([wl.Bl * wl.T, int(wl.dev_batch.response_mask.sum())], dtype=torch.float64,
+                                device=device)
+            allr = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allr, mine)
+            rows = [int(x[0]) for x in allr]
+            act = [int(x[1]) for x in allr]
+            rank_rows = {"rows_max": max(rows), "rows_mean": sum(rows) / world, "active_rows_max": max(act),
+                         "active_rows_mean": sum(act) / world, "active_rows_per_rank": act}
+
+        e2e = None
+        if not args.no_e2e:
+            one, h2d, d2h = wl.e2e()
+            n = max(1, min(steps, 3))
+            te = time_e2e(one, n, world, device)
+            e2e = {"value": wl.tokens_per_step() * n / (te / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                   "d2h_bytes_per_step": int(d2h), "steps": n}
+    finally:
+        for name, fn in saved.items():
+            setattr(ops, name, fn)
 
     if rank != 0:
+        del wl
         return None
     peaks, peak_src = load_peaks()
+    ms, kms = tm.ms, tm.kms
     res = {
         "metric": METRIC,
-        "value": wl.tokens_per_step() * args.steps / (ms / 1e3),
+        "value": wl.tokens_per_step() * steps / (ms / 1e3),
         "unit": UNIT,
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms / args.steps,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": ms / steps,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "f32" if args.workload.startswith("grpo") else "bf16",
+        "dtype": "f32" if key.startswith("grpo") else "bf16",
         "data": "synthetic (seeded; random-init weights)",
         "config": wl.config(world),
-        "roofline": (wl.step_roofline(ms / args.steps, (kms / args.steps) if timer.pairs else 0.0, peaks, peak_src)
-                     if isinstance(wl, E2EGRPO) else wl.roofline(kms / args.steps, peaks, peak_src)),
+        "roofline": (wl.step_roofline(ms / steps, (kms / steps) if tm.has_kernel_time else 0.0, peaks, peak_src)
+                     if isinstance(wl, E2EGRPO) else wl.roofline(kms / steps, peaks, peak_src)),
         "e2e": e2e,
-        "gpu_launches": int(launches),
-        "clocks": clocks,
-        "dw_allreduce": dw_allreduce,
+        "gpu_launches": tm.launches,
+        "clocks": tm.clocks,
         "loss": loss,
     }
-    if world == 1 and not args.no_cpu_baseline and not isinstance(wl, E2EGRPO):
-        rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", CPU_ROWS[args.workload]))
-        tok_s, dt, sample = wl.cpu_sample(rows, 3)
-        res["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                               "sample": sample + f"; 3 steps of {dt:.2f} s"}
+    if dw_allreduce is not None:
+        res["dw_allreduce"] = dw_allreduce
+        step_ms = ms / steps + dw_allreduce["ms"]
+        res["value_with_dw_allreduce"] = wl.tokens_per_step() / (step_ms / 1e3)
+    if rank_rows is not None:
+        res["rank_rows"] = rank_rows
+    if world == 1 and cpu_baseline and not args.no_cpu_baseline and not isinstance(wl, E2EGRPO):
+        tok_s, dt, sample, kind = wl.cpu_sample(CPU_ROWS[key], 3)
+        res["cpu_baseline"] = {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
+                               "sample": sample + f"; 3 steps of {dt:.3f} s"}
+    del wl
     return res
 
 
 def run_reference(args, rank, world) -> dict | None:
-    """The reference's CPU arithmetic on the host cores (rank 0 only), same metric and config."""
+    """The reference's own CPU implementation of the path on the host cores (rank 0 only), same
+    metric, unit and config; each step a bounded sample of the workload."""
     if rank != 0:
         return None
     if args.workload == "e2e-0.6b":
         return {"impl": "reference", "unavailable": "a 0.6B-parameter training step on the host CPU is not a "
                 "meaningful baseline; bench.py --workload e2e-0.6b --reference-gpu times the reference's GPU path"}
     wl = WORKLOADS[args.workload](args.workload, args)
-    rows = int(os.environ.get("IKRL_BENCH_CPU_ROWS", max(1, CPU_ROWS[args.workload] // 2)))
+    rows = CPU_ROWS[args.workload]
     for _ in range(max(0, args.warmup - 1)):
         wl.cpu_sample(rows, 1)
-    tok_s, dt, sample = wl.cpu_sample(rows, max(1, args.steps))
-    cfg = dict(wl.config(world)) if not isinstance(wl, GRPOHooks) else dict(wl.config(world))
+    tok_s, dt, sample, kind = wl.cpu_sample(rows, max(1, args.steps))
+    cfg = dict(wl.config(world))
     cfg["sample"] = sample
     return {
         "metric": METRIC,
@@ -898,37 +1045,35 @@ def run_reference(args, rank, world) -> dict | None:
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": "f32" if args.workload.startswith("grpo") else "bf16",
         "data": "synthetic (seeded)",
         "impl": "reference",
         "config": cfg,
-        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+        "cpu_baseline": {"value": tok_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
                          "sample": sample},
         "e2e": {"value": tok_s, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
-def run_reference_gpu(args, device) -> dict:
-    """The reference's own GPU path for the LM-head workloads, for comparison: invokerl's
-    PolicyModel._chunked_lm_head_ce (F.linear + -F.cross_entropy per 64-token chunk under
-    torch.utils.checkpoint, cuBLAS GEMMs) and its GRPO, imported unchanged from baseline/_ref."""
-    ref_root = ROOT / "baseline" / "_ref"
-    if not (ref_root / "invokerl" / "policy.py").exists():
-        return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
-    if args.workload not in LMHeadGRPO.PRESETS and args.workload not in ("e2e-0.6b", "grpo", "grpo-hbm", "logits"):
-        return {"impl": "reference-gpu", "unavailable": f"no GPU reference leg for workload {args.workload}"}
-    sys.path.insert(0, str(ref_root))
-    if args.workload == "e2e-0.6b":
-        return run_reference_gpu_e2e(args, device)
-    if args.workload in ("grpo", "grpo-hbm"):
-        return run_reference_gpu_hooks(args, device)
-    if args.workload == "logits":
-        return run_reference_gpu_logits(args, device)
-    from invokerl.algorithms import GRPO as RefGRPO
+# ---- the reference's own GPU path on the same box -------------------------------------------------
+
+
+def ref_batch_of(db):
     from invokerl.algorithms import RolloutBatch as RefBatch
+
+    return RefBatch(token_ids=db.token_ids, prompt_mask=db.prompt_mask, response_mask=db.response_mask,
+                    attention_mask=db.attention_mask, rewards=db.rewards, token_rewards=None,
+                    old_log_probs=db.old_log_probs, ref_log_probs=db.ref_log_probs, group_ids=db.group_ids,
+                    group_size=db.group_size)
+
+
+def ref_gpu_lmhead(key, args, device):
+    """invokerl's PolicyModel._chunked_lm_head_ce (F.linear + -F.cross_entropy per 64-token chunk
+    under torch.utils.checkpoint, cuBLAS GEMMs; policy.py:124-191) and its GRPO (grpo.py:46-143)."""
+    from invokerl.algorithms import GRPO as RefGRPO
     from invokerl.policy import PolicyModel as RefPolicy
 
-    wl = LMHeadGRPO(args.workload, args)
+    wl = LMHeadGRPO(key, args)
     wl.setup(0, 1, device)
     H, B, T = wl.H, wl.B, wl.T
     head = torch.nn.Linear(H, V, bias=False, device=device, dtype=torch.bfloat16)
@@ -938,106 +1083,144 @@ def run_reference_gpu(args, device) -> dict:
     pm.model = torch.nn.Module()
     pm.model.lm_head = head
     hidden = wl.hidden.detach().view(B, T, H).clone().requires_grad_(True)
-    db = wl.dev_batch
-    rb = RefBatch(token_ids=db.token_ids, prompt_mask=db.prompt_mask, response_mask=db.response_mask,
-                  attention_mask=db.attention_mask, rewards=db.rewards, token_rewards=None,
-                  old_log_probs=db.old_log_probs, ref_log_probs=db.ref_log_probs, group_ids=db.group_ids,
-                  group_size=db.group_size)
+    host_hidden = hidden.detach().cpu().pin_memory()
+    hb = host_batch(wl.local)
+    rb = ref_batch_of(wl.dev_batch)
     algo = RefGRPO(clip_eps=0.2, beta=0.04)
     del wl
 
+    def run(h, b):
+        head.weight.grad = None
+        lp = pm._chunked_lm_head_ce(h, b.token_ids, 64)
+        adv = algo.compute_advantages(b)
+        loss, _ = algo.compute_loss(lp, b, adv)
+        loss.backward()
+        return loss
+
     def step():
         hidden.grad = None
-        head.weight.grad = None
-        lp = pm._chunked_lm_head_ce(hidden, rb.token_ids, 64)
-        adv = algo.compute_advantages(rb)
-        loss, _ = algo.compute_loss(lp, rb, adv)
-        loss.backward()
+        return run(hidden, rb)
 
-    for _ in range(max(1, args.warmup - 1)):
-        step()
-    torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = max(1, min(args.steps, 3))
-    s.record()
-    for _ in range(n):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / n
-    return {"metric": METRIC, "impl": "reference-gpu", "value": B * T / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
-            "steps": n, "config": {"workload": LMHeadGRPO.PRESETS[args.workload]["name"] + ", invokerl's own "
-                                   "chunked F.linear + cross_entropy path and GRPO on the same GPU"},
-            "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
+    def e2e():
+        h = host_hidden.to(device, non_blocking=True).requires_grad_(True)
+        b = ref_batch_of(to_device_batch(hb, device))
+        return float(run(h, b).detach())  # the reference reads its metrics with .item() as well
+
+    return dict(step=step, e2e=e2e, tokens=B * T, h2d=host_hidden.numel() * 2 + batch_bytes(hb), d2h=4,
+                workload=LMHeadGRPO.PRESETS[key]["name"] + ", invokerl's own chunked F.linear + cross_entropy "
+                "path and GRPO on the same GPU")
 
 
-def run_reference_gpu_hooks(args, device) -> dict:
+def ref_gpu_hooks(key, args, device):
     """invokerl's own GRPO compute_advantages + compute_loss + backward (its eager ATen ops and
-    metric .item() calls) on the same device batch as the grpo workloads."""
+    metric .item() calls) on the same batch as the grpo workloads."""
     from invokerl.algorithms import GRPO as RefGRPO
-    from invokerl.algorithms import RolloutBatch as RefBatch
 
-    wl = GRPOHooks(args.workload, args)
+    wl = GRPOHooks(key, args)
     wl.setup(0, 1, device)
-    db = wl.dev_batch
-    rb = RefBatch(token_ids=db.token_ids, prompt_mask=db.prompt_mask, response_mask=db.response_mask,
-                  attention_mask=db.attention_mask, rewards=db.rewards, token_rewards=None,
-                  old_log_probs=db.old_log_probs, ref_log_probs=db.ref_log_probs, group_ids=db.group_ids,
-                  group_size=db.group_size)
+    rb = ref_batch_of(wl.dev_batch)
+    hb = host_batch(wl.local)
+    host_lp = wl.new.pin_memory()
     algo = RefGRPO(clip_eps=0.2, beta=0.04)
     lp0 = wl.lp.detach()
+    tokens = wl.tokens_per_step()
+    cfg = wl.config(1)["workload"]
+    del wl
+
+    def run(lp, b):
+        adv = algo.compute_advantages(b)
+        loss, _ = algo.compute_loss(lp, b, adv)
+        loss.backward()
+        return loss
 
     def step():
-        lp = lp0.clone().requires_grad_(True)
-        adv = algo.compute_advantages(rb)
-        loss, _ = algo.compute_loss(lp, rb, adv)
-        loss.backward()
+        return run(lp0.clone().requires_grad_(True), rb)
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    n = max(5, args.steps)
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(n):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / n
-    tokens = wl.tokens_per_step()
-    return {"metric": METRIC, "impl": "reference-gpu", "value": tokens / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
-            "steps": n, "config": {"workload": wl.config(1)["workload"] + ", invokerl's own GRPO on the same GPU"}}
+    def e2e():
+        b = ref_batch_of(to_device_batch(hb, device))
+        return float(run(host_lp.to(device, non_blocking=True).requires_grad_(True), b).detach())
+
+    return dict(step=step, e2e=e2e, tokens=tokens, h2d=batch_bytes(hb) + host_lp.numel() * 4, d2h=4,
+                workload=cfg + ", invokerl's own GRPO on the same GPU")
 
 
-def run_reference_gpu_logits(args, device) -> dict:
+def ref_gpu_logits(key, args, device):
     """The reference's materialised-logits log-prob (policy.py:100-104: -F.cross_entropy over
-    [N, V] bf16 logits, reduction="none") forward + backward on the logits workload's inputs."""
+    [N, V] bf16 logits, reduction="none") forward + autograd backward."""
     import torch.nn.functional as F
 
-    wl = LogitsLogProb(args.workload, args)
+    wl = LogitsLogProb(key, args)
     wl.setup(0, 1, device)
     x = wl.logits.detach().requires_grad_(True)
+    t, up = wl.t, wl.up
+    host_logits = x.detach().cpu().pin_memory()
+    host_t, host_up = t.cpu().pin_memory(), up.cpu().pin_memory()
+    n = wl.N
+    del wl
+
+    def run(xx, tt, uu):
+        lp = -F.cross_entropy(xx, tt, reduction="none")
+        lp.backward(uu.to(lp.dtype))
+        return lp
 
     def step():
         x.grad = None
-        lp = -F.cross_entropy(x, wl.t, reduction="none")
-        (lp * wl.up).sum().backward()
+        return run(x, t, up)
 
-    for _ in range(max(3, args.warmup)):
-        step()
+    def e2e():
+        xx = host_logits.to(device, non_blocking=True).requires_grad_(True)
+        lp = run(xx, host_t.to(device, non_blocking=True), host_up.to(device, non_blocking=True))
+        return float(lp.detach().float().sum())
+
+    return dict(step=step, e2e=e2e, tokens=n,
+                h2d=host_logits.numel() * 2 + host_t.numel() * 8 + host_up.numel() * 4, d2h=4,
+                workload=f"logits bf16 [{n}, {V}]: invokerl's -F.cross_entropy fwd + autograd bwd on the same GPU")
+
+
+def reference_gpu_line(key, args, device, steps, warmup) -> dict:
+    """The reference's own GPU path for workload `key` on this GPU: value, ms_per_step, e2e and the
+    clocks of its timed region, for the same config as this package's line."""
+    if reference_package() is None:
+        return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
+    if key == "e2e-0.6b":
+        return run_reference_gpu_e2e(args, device)
+    make = ref_gpu_lmhead if key in LMHeadGRPO.PRESETS else ref_gpu_hooks if key.startswith("grpo") else ref_gpu_logits
+    torch.cuda.reset_peak_memory_stats(device)
+    leg = make(key, args, device)
     torch.cuda.synchronize()
-    n = max(5, args.steps)
+    sampler = ClockSampler(device.index)
+    for _ in range(warmup):
+        leg["step"]()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(n):
-        step()
+    for _ in range(steps):
+        leg["step"]()
     e.record()
     torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / n
-    return {"metric": METRIC, "impl": "reference-gpu", "value": wl.N / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
-            "steps": n, "config": {"workload": "logits bf16 [%d, %d]: -F.cross_entropy fwd + autograd bwd on the same "
-                                               "GPU" % (wl.N, V)},
-            "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
+    clocks = sampler.stop()
+    ms = s.elapsed_time(e) / steps
+    ne = max(1, min(steps, 3))
+    te = time_e2e(leg["e2e"], ne, 1, device)
+    out = {"impl": "reference-gpu", "metric": METRIC, "value": leg["tokens"] / (ms / 1e3), "unit": UNIT,
+           "ms_per_step": ms, "steps": steps, "warmup": warmup, "same_config": True,
+           "e2e": {"value": leg["tokens"] * ne / (te / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(leg["h2d"]),
+                   "d2h_bytes_per_step": int(leg["d2h"]), "steps": ne},
+           "clocks": clocks, "config": {"workload": leg["workload"]},
+           "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9}
+    del leg
+    release(device)
+    return out
+
+
+def release(device):
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize(device)
+    torch.cuda.empty_cache()
 
 
 def run_reference_gpu_e2e(args, device) -> dict:
@@ -1049,7 +1232,7 @@ def run_reference_gpu_e2e(args, device) -> dict:
     from invokerl.policy import PolicyModel as RefPolicy
     from invokerl_b200.synthetic import rollout_batch
 
-    wl = E2EGRPO(args.workload, args)
+    wl = E2EGRPO("e2e-0.6b", args)
     model = E2EGRPO.build_model(device)
     cfg = model.config
     if wl.fsdp:
@@ -1109,6 +1292,21 @@ def run_reference_gpu_e2e(args, device) -> dict:
             "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
 
 
+def apply_tuning(args) -> dict:
+    """--tune knob=value and --ds-chunk-bytes: launch knobs of the library for A/B runs."""
+    from invokerl_b200 import _native, ops
+
+    applied = {}
+    for kv in args.tune:
+        k, v = kv.split("=", 1)
+        _native.set_tuning(k, int(v))
+        applied[k] = int(v)
+    if args.ds_chunk_bytes:
+        ops.set_ds_chunk_bytes(args.ds_chunk_bytes)
+        applied["ds_chunk_bytes"] = args.ds_chunk_bytes
+    return applied
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1120,11 +1318,16 @@ def main() -> int:
     ap.add_argument("--rows", type=int, default=0, help="override the rows of the logits workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="only the headline line: no reference_gpu leg and no secondary workloads")
     ap.add_argument("--fsdp", action="store_true",
                     help="e2e-0.6b: wrap the model in FSDP as invokerl's PolicyModel.fsdp() does (per-layer "
                          "FULL_SHARD); the log-prob path then takes the materialised-logits branch")
     ap.add_argument("--reference-gpu", action="store_true",
                     help="time the reference's own GPU path (baseline/_ref) instead; one extra JSON line")
+    ap.add_argument("--tune", action="append", default=[], metavar="KNOB=VALUE",
+                    help="set a library launch knob (ikrl_set_tuning) for an A/B run")
+    ap.add_argument("--ds-chunk-bytes", type=int, default=0, help="bytes of the K1 backward's dlogits chunk")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1136,17 +1339,34 @@ def main() -> int:
         return 0
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    tuned = apply_tuning(args)
     if args.reference_gpu:
         if rank == 0:
-            print(json.dumps(run_reference_gpu(args, device)), flush=True)
+            print(json.dumps(reference_gpu_line(args.workload, args, device, max(1, min(args.steps, 5)),
+                                                max(1, args.warmup))), flush=True)
         if dist.is_initialized():
             dist.destroy_process_group()
         return 0
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
-        res = run_native(args, rank, world, device)
+        res = run_native(args, args.workload, rank, world, device, args.steps, args.warmup)
+        release(device)
         if rank == 0 and res is not None:
+            if tuned:
+                res["tuning"] = tuned
+            extra = world == 1 and not args.no_secondary and args.workload == "lmhead-8b" and not tuned
+            if extra:
+                # The reference's own B200 path on the same config, then the other configs, each a
+                # line of its own with its reference leg.
+                res["reference_gpu"] = reference_gpu_line(args.workload, args, device, 3, 2)
+                res["secondary"] = []
+                for key in SECONDARY:
+                    line = run_native(args, key, 0, 1, device, SECONDARY_STEPS[key], 3)
+                    release(device)
+                    line["workload_key"] = key
+                    line["reference_gpu"] = reference_gpu_line(key, args, device, min(10, SECONDARY_STEPS[key]), 3)
+                    res["secondary"].append(line)
             print(json.dumps(res), flush=True)
     finally:
         if dist.is_initialized():  # torchrun ranks, or the one-rank group of --fsdp
