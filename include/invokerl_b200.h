@@ -287,8 +287,8 @@ IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, con
  * For callers that cannot allocate device memory when they need log-probs: hosts whose own
  * allocator owns all device memory and forbids side allocations, or frameworks whose caching pool
  * has already reserved the free memory.  The scratch comes from a 4 MiB array built into the
- * library, held on every GPU that loads it until exit.  Calls needing more scratch (above 61,672
- * rows at H = 4096, 116,496 at H = 1024, V = 151936) fail with IKRL_ERR_WORKSPACE before any GPU
+ * library, held on every GPU that loads it until exit.  Calls needing more scratch (above 31,772
+ * rows at H = 4096, 61,672 at H = 1024, V = 151936) fail with IKRL_ERR_WORKSPACE before any GPU
  * work.  All calls on a device share the array and it keeps the last call's contents (each call
  * clears what must start at zero), so calls that overlap on the GPU race.  The first call on a
  * device looks up the device addresses of the library's static arrays and should come before any

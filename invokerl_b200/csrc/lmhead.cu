@@ -36,8 +36,10 @@ constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
-// The wide kernel runs two epilogue warps per TMEM lane quadrant, each on half of the 512 columns.
-constexpr int kWideEpiWarps = 8;
+// The wide kernel runs four epilogue warps per TMEM lane quadrant, each on a quarter of the columns
+// of each 256-column half of the 512-column tile (64 columns per half).
+constexpr int kWideEpiWarps = 16;
+constexpr int kWideGroups = kWideEpiWarps / 4;
 constexpr int kWideThreads = 64 + 32 * kWideEpiWarps;
 constexpr uint32_t kTileA = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileB = BN * BK * 2;  // 32 KB
@@ -72,6 +74,7 @@ struct GemmParams {
   unsigned* lockstep;     // [npairs] tiles started per pair (zeroed per launch), or null: no pacing
   int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
   int pace_kb, pace_lag;  // pacing: K blocks between checkpoints, checkpoints a pair may lead by
+  int ds_tma;             // DLOGITS in the wide kernel: 1 = stage dS in shared memory, TMA-store it
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
@@ -89,28 +92,34 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-// Epilogue role (warps 2-5): drain accumulator tiles from TMEM, one row per thread, and apply the
+// Epilogue role (warps 2..): drain accumulator tiles from TMEM, one row per thread, and apply the
 // epilogue EPI.  acc_full[a] are this CTA's barriers; acc_empty[a] are the addresses the warps
 // arrive on when a tile is consumed (this CTA's, or the pair leader's when cluster_arrive).
 // tile_base: number of tiles this CTA consumed before this unit (accumulator ring position).
 // Returns false when a wait gave up (abort).
-// SPLIT (wide tile, one accumulator): every warp drains its 128 columns of the first 256-column
-// half, releases that half (acc_empty[0]) so the next tile's first-half MMAs can start, then
-// drains its 128 columns of the second half and releases it (acc_empty[1]).
-template <int EPI, int TILE_N = BN, int NBUF = 2, int HALVES = 1, bool SPLIT = false>
+// GROUPS: column groups; warp w drains TMEM lane quadrant w % 4 and column group (w - 2) / 4.
+// SPLIT (wide tile, one accumulator): every warp loads its columns of the first 256-column half
+// into registers and releases that half (acc_empty[0]) at once, so the next tile's first-half
+// MMAs start while it computes; then it does the same for the second half (acc_empty[1]).
+// stage_smem (DLOGITS only, 0 = unused): this warp's 2 KB staging tile; the dS values of each
+// 32 x 32 block are written there in the 64-byte swizzled layout of tm_store and sent to global
+// memory with one TMA store per block, instead of 32 scattered row stores.
+template <int EPI, int TILE_N = BN, int NBUF = 2, int GROUPS = 1, bool SPLIT = false>
 __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem_base, int m0, int split, int t_begin,
                                               int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
                                               const uint32_t (&acc_empty)[2], bool cluster_arrive,
-                                              volatile int* abort_v, int tile_base = 0) {
+                                              volatile int* abort_v, int tile_base = 0,
+                                              const CUtensorMap* tm_store = nullptr, uint32_t stage_smem = 0) {
   const int ntiles = t_end - t_begin;
   bool ok = true;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
-  constexpr int kCols = TILE_N / HALVES;  // columns of the tile this warp drains
-  static_assert(!SPLIT || (HALVES == 2 && NBUF == 1), "split drain needs two column groups, one accumulator");
+  constexpr int kCols = TILE_N / GROUPS;  // columns of the tile this warp drains
+  static_assert(!SPLIT || NBUF == 1, "split drain needs one accumulator");
   constexpr int kSegs = SPLIT ? 2 : 1;                      // column segments, drained in order
-  constexpr int kSegCols = SPLIT ? TILE_N / 4 : kCols;
-  const int half = HALVES == 1 ? 0 : (warp - 2) / 4;
-  const int c_lo = half * kCols;
+  constexpr int kSegCols = SPLIT ? TILE_N / (2 * GROUPS) : kCols;
+  static_assert(!SPLIT || kSegCols % 32 == 0, "split segments are whole 32-column chunks");
+  const int group = GROUPS == 1 ? 0 : (warp - 2) / 4;
+  const int c_lo = group * kCols;
   const int r = q * 32 + lane;
   const int grow = m0 + r;
   const bool row_ok = grow < p.M;
@@ -131,6 +140,101 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   if (tgt != -100) tgt -= p.id_offset;
   float run_m = -INFINITY, run_s = 0.f, tval = 0.f;
   bool found = false;
+
+  // The epilogue of one 32-column chunk of this thread's row, columns [col0, col0 + 32) of the
+  // output (col0 < N; the chunk may end past N).  Warp-uniform control flow.
+  auto chunk = [&](const float* v, int col0) {
+    const int nvalid = min(32, p.N - col0);
+    if constexpr (EPI == EPI_LSE) {
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nvalid) cm = fmaxf(cm, v[i]);
+      cm *= kLog2e;
+      if (cm > run_m) {
+        run_s *= fast_exp2(run_m - cm);
+        run_m = cm;
+      }
+      float cs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
+      run_s += cs;
+      // Target gather without a dynamically indexed register array (which would go to local
+      // memory): exactly one term is v[rel] * 1, every other term adds zero.
+      const int64_t rel = tgt - col0;
+      if (rel >= 0 && rel < nvalid) {
+        const int rr = (int)rel;
+        float acc_t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
+        tval = acc_t;
+        found = true;
+      }
+    } else if constexpr (EPI == EPI_DLOGITS) {
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float p0 = fast_exp2(fmaf(v[i], kLog2e, -lse2));
+        const float p1 = fast_exp2(fmaf(v[i + 1], kLog2e, -lse2));
+        const float d0 = gval * (((int64_t)(col0 + i) == tgt ? 1.f : 0.f) - p0);
+        const float d1 = gval * (((int64_t)(col0 + i + 1) == tgt ? 1.f : 0.f) - p1);
+        w[i >> 1] = pack_bf16x2(d0, d1);
+      }
+      if (stage_smem != 0) {
+        // One TMA store per 32 x 32 block: row `lane` goes to the staging tile with its 16-byte
+        // chunks in the 64-byte swizzled order; the tensor map clips rows >= M and columns >= N.
+        if (lane == 0) bulk_wait_read_all();  // the previous block's store has read the tile
+        __syncwarp();
+        const uint32_t row_addr = stage_smem + (uint32_t)lane * 64u;
+        const uint32_t sw = ((uint32_t)lane >> 1) & 3u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          st_shared_v4(row_addr + ((((uint32_t)k) ^ sw) << 4), w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tm_store, stage_smem, col0, m0 + q * 32);
+          bulk_commit();
+        }
+      } else if (row_ok) {
+        uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
+    } else if constexpr (EPI == EPI_STORE_BF16) {
+      if (row_ok) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) w[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
+        uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
+    } else {  // EPI_F32
+      if (row_ok) {
+        float* dst = p.out_f32 + (int64_t)grow * p.ld_f32 + col0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (4 * k >= nvalid) break;
+          float4 x = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          if (p.f32_mode != F32_STORE) {
+            const float4 o = *reinterpret_cast<const float4*>(dst + 4 * k);
+            x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+          }
+          if (p.f32_mode == F32_ADD_TO_BF16) {
+            uint16_t* d16 = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0 + 4 * k;
+            *reinterpret_cast<uint2*>(d16) = make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
+          } else {
+            *reinterpret_cast<float4*>(dst + 4 * k) = x;
+          }
+        }
+      }
+    }
+  };
+
   for (int j = 0; j < ntiles; ++j) {
     const int acc = NBUF == 2 ? ((tile_base + j) & 1) : 0;
     const uint32_t acc_phase = NBUF == 2 ? ((uint32_t)((tile_base + j) >> 1) & 1u) : ((uint32_t)(tile_base + j) & 1u);
@@ -140,7 +244,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       if (row_ok && p.f32_mode != F32_STORE) {
 #pragma unroll
         for (int sg = 0; sg < kSegs; ++sg) {
-          const int n0p = (t_begin + j) * TILE_N + (SPLIT ? sg * (TILE_N / 2) + half * kSegCols : c_lo);
+          const int n0p = (t_begin + j) * TILE_N + (SPLIT ? sg * (TILE_N / 2) + group * kSegCols : c_lo);
           const int ncols = min(kSegCols, p.N - n0p);
           if (ncols > 0)
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
@@ -156,106 +260,48 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
     tc_fence_after();
     const int n0 = (t_begin + j) * TILE_N;
     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
-    for (int sg = 0; sg < kSegs; ++sg) {
-    const int cs = SPLIT ? sg * (TILE_N / 2) + half * kSegCols : c_lo;
-#pragma unroll 1
-    for (int c = cs; c < cs + kSegCols; c += 32) {
-      const int col0 = n0 + c;
-      if (col0 >= p.N) break;  // warp-uniform
-      float v[32];
-      tmem_ld32(tbase + (uint32_t)c, v);
-      tmem_wait_ld();
-      const int nvalid = min(32, p.N - col0);
-      if constexpr (EPI == EPI_LSE) {
-        float cm = -INFINITY;
+    if constexpr (SPLIT) {
+      // Load a half's columns, release the half, then compute from registers.
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nvalid) cm = fmaxf(cm, v[i]);
-        cm *= kLog2e;
-        if (cm > run_m) {
-          run_s *= fast_exp2(run_m - cm);
-          run_m = cm;
-        }
-        float cs = 0.f;
+      for (int sg = 0; sg < 2; ++sg) {
+        const int cs = sg * (TILE_N / 2) + group * kSegCols;
+        float v[kSegCols];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
-        run_s += cs;
-        // Target gather without a dynamically indexed register array (which would go to local
-        // memory): exactly one term is v[rel] * 1, every other term adds zero.
-        const int64_t rel = tgt - col0;
-        if (rel >= 0 && rel < nvalid) {
-          const int rr = (int)rel;
-          float acc_t = 0.f;
+        for (int cc = 0; cc < kSegCols; cc += 32) tmem_ld32p(tbase + (uint32_t)(cs + cc), v + cc);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty[sg]);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
-          tval = acc_t;
-          found = true;
-        }
-      } else if constexpr (EPI == EPI_DLOGITS) {
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = fast_exp2(fmaf(v[i], kLog2e, -lse2));
-          const float p1 = fast_exp2(fmaf(v[i + 1], kLog2e, -lse2));
-          const float d0 = gval * (((int64_t)(col0 + i) == tgt ? 1.f : 0.f) - p0);
-          const float d1 = gval * (((int64_t)(col0 + i + 1) == tgt ? 1.f : 0.f) - p1);
-          w[i >> 1] = pack_bf16x2(d0, d1);
-        }
-        if (row_ok) {
-          uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-        }
-      } else if constexpr (EPI == EPI_STORE_BF16) {
-        if (row_ok) {
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) w[i >> 1] = pack_bf16x2(v[i], v[i + 1]);
-          uint16_t* dst = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0;
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (8 * k < nvalid) st_global_v4(dst + 8 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-        }
-      } else {  // EPI_F32
-        if (row_ok) {
-          float* dst = p.out_f32 + (int64_t)grow * p.ld_f32 + col0;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            if (4 * k >= nvalid) break;
-            float4 x = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-            if (p.f32_mode != F32_STORE) {
-              const float4 o = *reinterpret_cast<const float4*>(dst + 4 * k);
-              x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-            }
-            if (p.f32_mode == F32_ADD_TO_BF16) {
-              uint16_t* d16 = p.out_bf16 + (int64_t)grow * p.ld_bf16 + col0 + 4 * k;
-              *reinterpret_cast<uint2*>(d16) = make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
-            } else {
-              *reinterpret_cast<float4*>(dst + 4 * k) = x;
-            }
-          }
-        }
+        for (int cc = 0; cc < kSegCols; cc += 32)
+          if (n0 + cs + cc < p.N) chunk(v + cc, n0 + cs + cc);
       }
-    }
-    if (SPLIT && sg == 0) {
+    } else {
+#pragma unroll 1
+      for (int c = c_lo; c < c_lo + kCols; c += 32) {
+        const int col0 = n0 + c;
+        if (col0 >= p.N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32p(tbase + (uint32_t)c, v);
+        tmem_wait_ld();
+        chunk(v, col0);
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc_empty[0]);  // first half drained
+      if (lane == 0) {
+        if (cluster_arrive) mbar_arrive_cluster(acc_empty[acc]);
+        else mbar_arrive(acc_empty[acc]);
+      }
     }
-    }  // column segments
-    tc_fence_before();
+  }
+  if constexpr (EPI == EPI_DLOGITS) {
+    // Every TMA store of this warp has completed before the CTA can exit.
+    if (stage_smem != 0 && lane == 0) bulk_wait_all();
     __syncwarp();
-    if (lane == 0) {
-      const int rel = SPLIT ? 1 : acc;
-      if (cluster_arrive) mbar_arrive_cluster(acc_empty[rel]);
-      else mbar_arrive(acc_empty[rel]);
-    }
   }
   if constexpr (EPI == EPI_LSE) {
     if (row_ok && !*abort_v) {
-      const int set = split * HALVES + half;
+      const int set = split * GROUPS + group;
       p.part_m[(int64_t)set * p.M + grow] = run_m;
       p.part_s[(int64_t)set * p.M + grow] = run_s;
       if (found) p.part_t[grow] = tval;
@@ -474,7 +520,7 @@ __device__ __forceinline__ void pace_checkpoint(unsigned* prog, int pair_id, int
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     lmhead_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            const GemmParams p) {
+                            const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kPairStages], empty_bar[kPairStages], acc_full[2], acc_empty[2], drain_bar;
   __shared__ uint32_t tmem_holder;
@@ -666,11 +712,15 @@ constexpr int kWideStages = 4;
 constexpr uint32_t kWideTileB = (WN / 2) * BK * 2;  // 32 KB: this CTA's half of the B tile
 constexpr uint32_t kWideStageBytes = kTileA + kWideTileB;
 constexpr uint32_t kWideSmemBytes = kWideStages * kWideStageBytes + 1024;
+// DLOGITS adds one 32 x 32 bf16 staging tile per epilogue warp for the TMA stores of dS.
+constexpr uint32_t kDsStageBytes = 32 * 32 * 2;
+constexpr uint32_t kWideDsSmemBytes = kWideSmemBytes + kWideEpiWarps * kDsStageBytes;
+static_assert(kWideDsSmemBytes <= 232448 - 256, "wide DLOGITS kernel exceeds the shared memory of a CTA");
 
 template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kWideThreads, 1)
     lmhead_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            const GemmParams p) {
+                            const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kWideStages], empty_bar[kWideStages], acc_full[2], acc_empty[2], drain_bar;
   __shared__ uint32_t tmem_holder;
@@ -862,14 +912,17 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     // ---------------- epilogue (both CTAs, own 128 rows x 512 columns) ----------------
     const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
     const uint32_t ae[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0), mapa_shared(smem_u32(&acc_empty[1]), 0)};
+    const uint32_t stage = (EPI == EPI_DLOGITS && p.ds_tma)
+                               ? smem_base + kWideStages * kWideStageBytes + (uint32_t)(warp - 2) * kDsStageBytes
+                               : 0u;
     int jb = 0;
     for (int u = pair_id; u < nunits; u += npairs) {
       const int split = u % p.splits;
       const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
       const int t_begin = split * p.tiles_per_split;
       const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-      if (!epilogue_role<EPI, WN, 1, 2, true>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae, true, abort_v,
-                                              jb))
+      if (!epilogue_role<EPI, WN, 1, kWideGroups, true>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae,
+                                                        true, abort_v, jb, &tmC, stage))
         break;
       jb += t_end - t_begin;
     }
@@ -997,6 +1050,26 @@ int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
   return IKRL_OK;
 }
 
+// Tensor map for the wide kernel's TMA stores of dS: bf16 [outer, inner] with row stride `ld`
+// elements, 32 x 32 boxes (64-byte rows) in the 64-byte swizzled shared-memory layout.  Stores clip
+// at the inner and outer extents.
+int make_store_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t outer, uint64_t ld, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  IKRL_REQUIRE(fn != nullptr, IKRL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  IKRL_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, IKRL_ERR_ALIGNMENT,
+               "%s: base address must be 16-byte aligned", what);
+  IKRL_REQUIRE((ld * 2) % 16 == 0, IKRL_ERR_ALIGNMENT, "%s: row stride %llu elements is not a multiple of 8", what,
+               (unsigned long long)ld);
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  IKRL_REQUIRE(r == CUDA_SUCCESS, IKRL_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return IKRL_OK;
+}
+
 template <int EPI, bool A_MN, bool B_MN>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int m_tiles, cudaStream_t s) {
   auto kern = lmhead_gemm_kernel<EPI, A_MN, B_MN>;
@@ -1035,10 +1108,12 @@ bool pacing_enabled() { return tuning(IKRL_TUNE_PACE) != 0; }
 bool persistent_pairs() { return tuning(IKRL_TUNE_PERSISTENT) != 0; }
 
 template <int EPI, bool A_MN, bool B_MN, bool WIDE>
-int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p_in, int m_tiles, cudaStream_t s) {
+int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap* c, const GemmParams& p_in,
+                     int m_tiles, cudaStream_t s) {
   GemmParams p = p_in;
   auto kern = WIDE ? lmhead_gemm_wide_kernel<EPI, A_MN, B_MN> : lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
-  const uint32_t smem_bytes = WIDE ? kWideSmemBytes : kPairSmemBytes;
+  p.ds_tma = (WIDE && EPI == EPI_DLOGITS && c != nullptr) ? 1 : 0;
+  const uint32_t smem_bytes = WIDE ? (p.ds_tma ? kWideDsSmemBytes : kWideSmemBytes) : kPairSmemBytes;
   IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
   IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
   const int64_t nunits = (int64_t)((m_tiles + 1) / 2) * p.splits;
@@ -1071,7 +1146,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const GemmParam
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, p.ds_tma ? *c : a, p);
   if (e != cudaSuccess) {
     int nclusters = -1;
     cudaError_t e2 = cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg);
@@ -1185,9 +1260,11 @@ K1Plan plan_k1(int epi, int64_t m_tiles, int N, int K, int splits_hint, int nsm)
 
 // Launch one K1 GEMM with the kernel plan_k1 selects, filling in the tile ranges; p.splits holds
 // the count actually used.
+// c_store: tensor map of the dS chunk for the wide kernel's TMA stores (DLOGITS), or null.
 template <int EPI, bool A_MN, bool B_MN>
 int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CUtensorMap& a_pair,
-              const CUtensorMap& b_pair, GemmParams& p, int m_tiles, int splits_hint, cudaStream_t s) {
+              const CUtensorMap& b_pair, GemmParams& p, int m_tiles, int splits_hint, cudaStream_t s,
+              const CUtensorMap* c_store = nullptr) {
   int dev = 0, nsm = kNumSMs;
   IKRL_CUDA(cudaGetDevice(&dev));
   IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
@@ -1197,7 +1274,7 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
   p.tiles_per_split = pl.tiles_per_split;
   p.splits = pl.splits;
   p.split_major = 1;
-  p.part_sets = p.splits * (kind == 2 ? 2 : 1);
+  p.part_sets = p.splits * (kind == 2 ? kWideGroups : 1);
   {
     // L2 policy of the A and B loads of the wide kernel (0 normal, 1 evict-last, 2 evict-first),
     // IKRL_TUNE_L2_POLICY = 10 * a + b.  Default: A (re-read by every tile of a unit) evict-last,
@@ -1210,8 +1287,8 @@ int launch_k1(const CUtensorMap& a_single, const CUtensorMap& b_single, const CU
       p.b_policy = (int)(pol % 10);
     }
   }
-  if (kind == 2) return launch_gemm_pair<EPI, A_MN, B_MN, true>(a_pair, b_pair, p, m_tiles, s);
-  if (kind == 1) return launch_gemm_pair<EPI, A_MN, B_MN, false>(a_pair, b_pair, p, m_tiles, s);
+  if (kind == 2) return launch_gemm_pair<EPI, A_MN, B_MN, true>(a_pair, b_pair, c_store, p, m_tiles, s);
+  if (kind == 1) return launch_gemm_pair<EPI, A_MN, B_MN, false>(a_pair, b_pair, nullptr, p, m_tiles, s);
   return launch_gemm<EPI, A_MN, B_MN>(a_single, b_single, p, m_tiles, s);
 }
 
@@ -1248,9 +1325,9 @@ FwdLayout fwd_layout(int64_t N, int H, int V) {
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   L.err_off = 0;
   L.pm_off = 256;
-  // up to two partial sets per split (the wide kernel's two column halves)
-  L.ps_off = al(L.pm_off + (size_t)2 * L.splits * N * 4);
-  L.pt_off = al(L.ps_off + (size_t)2 * L.splits * N * 4);
+  // up to kWideGroups partial sets per split (the wide kernel's column groups)
+  L.ps_off = al(L.pm_off + (size_t)kWideGroups * L.splits * N * 4);
+  L.pt_off = al(L.ps_off + (size_t)kWideGroups * L.splits * N * 4);
   L.total = al(L.pt_off + (size_t)N * 4);
   return L;
 }
@@ -1570,8 +1647,9 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
     const uint16_t* hc = hsrc + c0 * H;
     // 1) dS = g * (onehot - softmax(h W^T)) for this chunk
     {
-      CUtensorMap ta;
+      CUtensorMap ta, tds;
       if ((rc = make_tmap(&ta, hc, H, rows, H, BM, "hidden chunk"))) return rc;
+      if ((rc = make_store_tmap(&tds, dS, V, rows, L.lds, "dS store"))) return rc;
       GemmParams p{};
       p.M = (int)rows; p.N = V; p.K = H;
       const int sp = choose_splits(m_tiles, n_vt, H);
@@ -1579,7 +1657,7 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
       p.id_offset = vocab_start;
       p.out_bf16 = dS; p.ld_bf16 = L.lds;
       p.err = err;
-      if ((rc = launch_k1<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, sp, s))) return rc;
+      if ((rc = launch_k1<EPI_DLOGITS, false, false>(ta, t_w_k, ta, t_w_k2, p, m_tiles, sp, s, &tds))) return rc;
     }
     // 2) dW (+)= dS^T h[chunk]
     if (dweight) {

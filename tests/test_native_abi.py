@@ -171,10 +171,10 @@ def test_tuning_knobs_range_checks_and_defaults(lib):
 
 
 def test_no_alloc_limits_match_the_documented_row_counts(lib):
-    """The allocation-free forward's 4 MiB scratch holds the forward workspace of up to 61,672 rows
-    at H = 4096 and 116,496 at H = 1024 (V = 151936), the limits its documentation states."""
+    """The allocation-free forward's 4 MiB scratch holds the forward workspace of up to 31,772 rows
+    at H = 4096 and 61,672 at H = 1024 (V = 151936), the limits its documentation states."""
     w = lib.ikrl_lmhead_fwd_workspace_bytes
-    for H, rows in [(4096, 61672), (1024, 116496)]:
+    for H, rows in [(4096, 31772), (1024, 61672)]:
         assert w(rows, H, 151936) <= 4 << 20 < w(rows + 1, H, 151936)
 
 
