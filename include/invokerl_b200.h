@@ -91,8 +91,10 @@ enum {
                                    1 always; 2 the K >= 1024 rule without the dH balance choice */
   IKRL_TUNE_PERSISTENT = 3,     /* K1 pair kernels: 1 one resident pair per two SMs (default);
                                    0 one pair per work unit */
-  IKRL_TUNE_PACE = 4,           /* 256x512 kernel: 1 pace the persistent pairs (default); 0 off */
-  IKRL_TUNE_PACE_KB = 5,        /* K blocks between pacing checkpoints (default 64) */
+  IKRL_TUNE_PACE = 4,           /* 256x512 kernel: which launches pace their persistent pairs, a
+                                   mask: 1 forward, 2 dS recompute, 4 dH (and a one-chunk bf16
+                                   dW), 8 fp32 dW; default 15 (all); 0 none */
+  IKRL_TUNE_PACE_KB = 5,        /* K blocks between pacing checkpoints (default 128) */
   IKRL_TUNE_PACE_LAG = 6,       /* checkpoints a pair may lead the slowest by (default 1) */
   IKRL_TUNE_BALANCE_SPLITS = 7, /* K1 dS launches: 1 pick the vocab split count for balance of
                                    the persistent pairs (default); 0 the L2 rule alone */

@@ -29,8 +29,8 @@ constexpr KnobSpec kKnobs[IKRL_TUNE_COUNT] = {
     {1, 0, 1},          // IKRL_TUNE_SKIP_ZERO_ROWS
     {-1, -1, 2},        // IKRL_TUNE_WIDE
     {1, 0, 1},          // IKRL_TUNE_PERSISTENT
-    {1, 0, 1},          // IKRL_TUNE_PACE
-    {64, 1, 1 << 20},   // IKRL_TUNE_PACE_KB
+    {15, 0, 15},        // IKRL_TUNE_PACE
+    {128, 1, 1 << 20},  // IKRL_TUNE_PACE_KB
     {1, 0, 64},         // IKRL_TUNE_PACE_LAG
     {1, 0, 1},          // IKRL_TUNE_BALANCE_SPLITS
     {-1, -1, 22},       // IKRL_TUNE_L2_POLICY

@@ -474,9 +474,9 @@ constexpr uint32_t kPairSmemBytes = kPairStages * kPairStageBytes + 1024;
 
 // Pacing of the persistent pairs: pairs that read the same W tiles through L2 drift apart over a
 // sweep, and a tile read by a leading pair is evicted before the trailing pairs reach it.  Each
-// pair publishes how many checkpoints it has passed (one per pace_kb K blocks, default 64: one per
-// tile at K = 4096, 4 tiles at K = 1024; a long reduction such as dH over the vocabulary has many
-// per tile); a pair about to pass checkpoint j waits until every unfinished pair has passed
+// pair publishes how many checkpoints it has passed (one per pace_kb K blocks, default 128: one per
+// two tiles at K = 4096, 8 tiles at K = 1024; a long reduction such as dH over the vocabulary has
+// many per tile); a pair about to pass checkpoint j waits until every unfinished pair has passed
 // checkpoint j - pace_lag (default 1).  The wait is a heuristic with a short bound: after
 // kPaceBoundNs without progress the pair stops pacing for the rest of the launch (a pair that is
 // not resident, e.g. on a shared GPU, must not stall the others).
@@ -1103,8 +1103,9 @@ int pace_array(unsigned** out) {
   return IKRL_OK;
 }
 
-// Pacing of the wide kernel's pairs (IKRL_TUNE_PACE, on by default).
-bool pacing_enabled() { return tuning(IKRL_TUNE_PACE) != 0; }
+// Pacing of the wide kernel's pairs: IKRL_TUNE_PACE is a mask over the epilogues, bit EPI set =
+// launches with that epilogue are paced (all by default).
+bool pacing_enabled(int epi) { return (tuning(IKRL_TUNE_PACE) >> epi) & 1; }
 bool persistent_pairs() { return tuning(IKRL_TUNE_PERSISTENT) != 0; }
 
 template <int EPI, bool A_MN, bool B_MN, bool WIDE>
@@ -1127,7 +1128,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
   p.lockstep = nullptr;
   // Pacing helps the wide kernel (long tiles, W re-read across pairs); on the 256 x 256 pair
   // kernel at K = 1024 it measured 7% slower (checkpoints every 4 short tiles stall the producer).
-  if (WIDE && persistent && npairs <= kMaxPacedPairs && pacing_enabled()) {
+  if (WIDE && persistent && npairs <= kMaxPacedPairs && pacing_enabled(EPI)) {
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
     IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));

@@ -153,13 +153,13 @@ def test_tuning_knobs_range_checks_and_defaults(lib):
     library reads no environment variable."""
     from invokerl_b200 import _native as N
 
-    defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": 1, "pace_kb": 64,
+    defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": 15, "pace_kb": 128,
                 "pace_lag": 1, "balance_splits": 1, "l2_policy": -1, "l2_budget_mb": 0, "loss_kernel": 1}
     assert {k: N.get_tuning(k) for k in N.TUNE} == defaults
     prev = N.set_tuning("pace_kb", 7)
-    assert prev == 64 and N.get_tuning("pace_kb") == 7
+    assert prev == 128 and N.get_tuning("pace_kb") == 7
     N.set_tuning("pace_kb", None)
-    assert N.get_tuning("pace_kb") == 64
+    assert N.get_tuning("pace_kb") == 128
     for knob, bad in [("l2_policy", 13), ("l2_policy", 30), ("pace_kb", 0), ("wide", 3), ("loss_kernel", 3)]:
         with pytest.raises(N.IkrlError, match="ikrl_set_tuning"):
             N.set_tuning(knob, bad)
