@@ -304,8 +304,16 @@ class LMHeadGRPO:
                            "the 2*N_act*H*V logits recompute of the backward is executed but not counted",
             "rows": n, "active_rows": n_act,
             "executed_tflop_per_step": (2.0 * n + 6.0 * n_act) * self.H * V / 1e12,
-            "traffic": None,
+            "traffic": self._traffic(n, n_act),
+            "traffic_unit": "bytes per step (all K1 launches of one step)",
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the K1 launches of a 65,536-row "
+                              "step, scaled by rows (forward) and active rows (backward chunks)",
         }
+
+    def _traffic(self, n, n_act):
+        f = TRAFFIC["lmhead_fwd_per_row"].get(self.H)
+        b = TRAFFIC["lmhead_bwd_per_active_row"].get(self.H)
+        return None if f is None or b is None else f * n + b * n_act
 
     def config(self, world):
         return {
@@ -455,7 +463,9 @@ class LogitsLogProb:
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                 "peak_source": f"{peak_src} HBM copy",
                 "algorithmic": "fwd reads 2NV bytes; bwd writes 2NV and reads 2*N_active*V (rows with a zero "
-                               "upstream are written as zeros without reading)", "traffic": None}
+                               "upstream are written as zeros without reading)",
+                "traffic": TRAFFIC["logits_per_row"] * self.N, "traffic_unit": "bytes per step",
+                "traffic_source": "ncu dram bytes of the fwd + bwd kernels on [4096, 151936], scaled by rows"}
 
     def config(self, world):
         return {"workload": "unfused logits->log-prob fwd+bwd: logits bf16 [16384, 151936] N(0,2), 50% masked upstream",
@@ -594,7 +604,8 @@ class GRPOHooks:
                 "advantages_kernel": {"ms": km["advantages"], "achieved_gbs": adv_gbs,
                                       "frac": adv_gbs / peaks["hbm_gbs"],
                                       "algorithmic": "5 B/token: reads mask (1 B), writes adv (fp32)"},
-                "traffic": None}
+                "traffic": TRAFFIC["grpo_loss_per_token"] * n, "traffic_unit": "bytes per loss-kernel launch",
+                "traffic_source": "ncu dram bytes of the loss kernel on 8,388,608 tokens, scaled by tokens"}
 
     def config(self, world):
         B = self.P * self.G
@@ -853,7 +864,19 @@ SECONDARY_STEPS = {"logits": 20, "lmhead-0.6b": 10, "grpo-hbm": 20}
 
 # DRAM traffic of the dominant kernel per unit of work, from ncu captures (dram__bytes_read.sum +
 # dram__bytes_write.sum); the line's roofline.traffic is this figure times the units of one step.
-TRAFFIC = {}
+TRAFFIC = {
+    # K1 at H = 4096, V = 151936 (profiles/lmhead_8b_dram_traffic.md; bench.py --batch 16): the forward
+    # over 65,536 rows moved 51.37 GB, one full 28,160-row backward chunk (dS recompute, dW, dH)
+    # 106.1 GB.  The forward's W re-reads grow with the rows, the backward's with the chunks.
+    "lmhead_fwd_per_row": {4096: 51.37e9 / 65536},
+    "lmhead_bwd_per_active_row": {4096: 106.1e9 / 28160},
+    # K2 forward + backward over [4096, 151936] bf16 logits, 51% active rows
+    # (profiles/logits_logprob_fwd_bwd_4096x151936.md): 3.069 GB.
+    "logits_per_row": 3.069e9 / 4096,
+    # K3 GRPO loss kernel over 8,388,608 tokens (profiles/grpo_loss_and_advantages_1024x8192.md):
+    # 160.9 MB.
+    "grpo_loss_per_token": 160.9e6 / 8388608,
+}
 
 
 class Timed:
