@@ -822,7 +822,11 @@ class E2EGRPO:
         peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         H = self.cfg.hidden_size
         n_rows = self.dev_batch.token_ids.numel()
-        head_tf = 6.0 * n_rows * H * V / (kernel_ms_per_step / 1e3) / 1e12 if kernel_ms_per_step > 0 else None
+        # The head's algorithmic FLOPs: the forward over every row, dH and dW over the rows with a
+        # nonzero upstream gradient (the response tokens; the last position of a row has no target).
+        n_act = int(self.dev_batch.response_mask[:, 1:].sum())
+        head_flops = (2.0 * n_rows + 4.0 * n_act) * H * V
+        head_tf = head_flops / (kernel_ms_per_step / 1e3) / 1e12 if kernel_ms_per_step > 0 else None
         return {"kernel": "whole GRPO step (HF transformer + fused LM-head log-prob + K3 loss + AdamW); MFU",
                 "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{peak_src} bf16 sustained",
@@ -830,6 +834,7 @@ class E2EGRPO:
                                "+ causal attention fwd+bwd; checkpoint recompute not counted",
                 "lmhead_kernels_ms_per_step": kernel_ms_per_step,
                 "lmhead_tflops": head_tf,
+                "lmhead_active_rows": n_act,
                 "traffic": None}
 
     def config(self, world):
@@ -859,8 +864,8 @@ WORKLOADS = {"lmhead-8b": LMHeadGRPO, "lmhead-0.6b": LMHeadGRPO, "logits": Logit
 # Rows of the bounded CPU sample per step (the reference's CPU path; 0 = every prompt group).
 CPU_ROWS = {"lmhead-8b": 32, "lmhead-0.6b": 96, "logits": 1024, "grpo": 0, "grpo-hbm": 8, "e2e-0.6b": 0}
 # Lines the default run adds after the headline, each a workload of its own with the same keys.
-SECONDARY = ("logits", "lmhead-0.6b", "grpo-hbm")
-SECONDARY_STEPS = {"logits": 20, "lmhead-0.6b": 10, "grpo-hbm": 20}
+SECONDARY = ("logits", "lmhead-0.6b", "grpo-hbm", "e2e-0.6b")
+SECONDARY_STEPS = {"logits": 20, "lmhead-0.6b": 10, "grpo-hbm": 20, "e2e-0.6b": 3}
 
 # DRAM traffic of the dominant kernel per unit of work, from ncu captures (dram__bytes_read.sum +
 # dram__bytes_write.sum); the line's roofline.traffic is this figure times the units of one step.
@@ -1206,7 +1211,7 @@ def reference_gpu_line(key, args, device, steps, warmup) -> dict:
     if reference_package() is None:
         return {"impl": "reference-gpu", "unavailable": "the reference package is not in baseline/_ref"}
     if key == "e2e-0.6b":
-        return run_reference_gpu_e2e(args, device)
+        return run_reference_gpu_e2e(args, device, steps, warmup)
     make = ref_gpu_lmhead if key in LMHeadGRPO.PRESETS else ref_gpu_hooks if key.startswith("grpo") else ref_gpu_logits
     torch.cuda.reset_peak_memory_stats(device)
     leg = make(key, args, device)
@@ -1246,7 +1251,7 @@ def release(device):
     torch.cuda.empty_cache()
 
 
-def run_reference_gpu_e2e(args, device) -> dict:
+def run_reference_gpu_e2e(args, device, steps: int | None = None, warmup: int | None = None) -> dict:
     """The same GRPO train step with invokerl's own PolicyModel.forward (its chunked
     F.linear + cross_entropy log-prob path under torch.utils.checkpoint) and its GRPO, on the same
     random-init model, batch and optimizer."""
@@ -1286,8 +1291,10 @@ def run_reference_gpu_e2e(args, device) -> dict:
         opt.step()
         opt.zero_grad(set_to_none=True)
 
+    steps = max(1, min(args.steps, 3)) if steps is None else steps
+    warmup = max(1, args.warmup - 1) if warmup is None else warmup
     try:
-        for _ in range(max(1, args.warmup - 1)):
+        for _ in range(warmup):
             step()
         torch.cuda.synchronize()
     except torch.cuda.OutOfMemoryError as e:
@@ -1296,18 +1303,23 @@ def run_reference_gpu_e2e(args, device) -> dict:
                                f" path): {str(e).splitlines()[0][:160]}",
                 "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9}
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = max(1, min(args.steps, 3))
+    n = steps
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    time.sleep(0.3)
     s.record()
     for _ in range(n):
         step()
     e.record()
     torch.cuda.synchronize()
+    clocks = sampler.stop()
     ms = s.elapsed_time(e) / n
     fpt = E2EGRPO.model_flops_per_token(cfg, wl.T)
     peaks, _ = load_peaks()
     achieved = fpt * wl.B * wl.T / (ms / 1e3) / 1e12
     return {"metric": METRIC, "impl": "reference-gpu", "value": wl.B * wl.T / (ms / 1e3), "unit": UNIT,
-            "ms_per_step": ms, "steps": n, "mfu_tflops": achieved,
+            "ms_per_step": ms, "steps": n, "warmup": warmup, "same_config": True, "clocks": clocks,
+            "mfu_tflops": achieved,
             "mfu_frac": achieved / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
             "config": {"workload": "GRPO train step, random-init Qwen3-0.6B + AdamW, invokerl's own "
                                    "PolicyModel.forward (chunked F.linear + cross_entropy) and GRPO on the same GPU",
