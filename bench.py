@@ -873,8 +873,10 @@ TRAFFIC = {
     # K1 at H = 4096, V = 151936 (profiles/lmhead_8b_dram_traffic.md; bench.py --batch 16): the forward
     # over 65,536 rows moved 51.37 GB, one full 28,160-row backward chunk (dS recompute, dW, dH)
     # 106.1 GB.  The forward's W re-reads grow with the rows, the backward's with the chunks.
-    "lmhead_fwd_per_row": {4096: 51.37e9 / 65536},
-    "lmhead_bwd_per_active_row": {4096: 106.1e9 / 28160},
+    # At H = 1024 (profiles/lmhead_0.6b_dram_traffic.md; the whole Qwen3-0.6B config): the forward
+    # over 131,072 rows moved 4.66 GB, the one backward chunk of 10,066 active rows 13.0 GB.
+    "lmhead_fwd_per_row": {4096: 51.37e9 / 65536, 1024: 4.66e9 / 131072},
+    "lmhead_bwd_per_active_row": {4096: 106.1e9 / 28160, 1024: 13.0e9 / 10066},
     # K2 forward + backward over [4096, 151936] bf16 logits, 51% active rows
     # (profiles/logits_logprob_fwd_bwd_4096x151936.md): 3.069 GB.
     "logits_per_row": 3.069e9 / 4096,
