@@ -170,6 +170,13 @@ def batch_bytes(b) -> int:
 _REF_PKG: list = []
 
 
+def ops_stats() -> dict:
+    """Rows the logit cache held in the last forward that needed a gradient, and its candidates."""
+    from invokerl_b200 import ops
+
+    return ops.LOGIT_CACHE_STATS
+
+
 def reference_package():
     """The unmodified reference package (invokerl, pure Python) from baseline/_ref, imported once;
     None when it is not there."""
@@ -270,7 +277,10 @@ class LMHeadGRPO:
     def _step(self, batch, hidden, ids):
         from invokerl_b200 import ops
 
-        lp = ops.lmhead_logprob(hidden, self.weight, ids).view(self.Bl, self.T)
+        # The attended rows may carry a gradient (the loss weights the response tokens among them),
+        # as PolicyModel.forward passes them.
+        lp = ops.lmhead_logprob(hidden, self.weight, ids, cache_rows=batch.attention_mask.reshape(-1))
+        lp = lp.view(self.Bl, self.T)
         adv = self.algo.compute_advantages(batch)
         loss, metrics = self.algo.compute_loss(lp, batch, adv)
         loss.backward()
@@ -301,9 +311,12 @@ class LMHeadGRPO:
             "peak_source": f"{peak_src} bf16 sustained (kernel timed inside a multi-second step)",
             "algorithmic": "2*N*H*V (fwd over all N rows) + 4*N_act*H*V (dH and dW over the N_act rows whose "
                            "upstream gradient is nonzero; masked rows contribute exact zeros and are skipped); "
-                           "the 2*N_act*H*V logits recompute of the backward is executed but not counted",
+                           "the backward's logits recompute of active rows without a logit-cache slot is executed "
+                           "but not counted",
             "rows": n, "active_rows": n_act,
-            "executed_tflop_per_step": (2.0 * n + 6.0 * n_act) * self.H * V / 1e12,
+            "logit_cache": dict(ops_stats()),
+            "executed_tflop_per_step": (2.0 * n + 4.0 * n_act + 2.0 * max(0, n_act - ops_stats()["rows"]))
+                                       * self.H * V / 1e12,
             "traffic": self._traffic(n, n_act),
             "traffic_unit": "bytes per step (all K1 launches of one step)",
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the K1 launches of a 65,536-row "

@@ -285,6 +285,37 @@ IKRL_API int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, con
                                      int32_t dweight_dtype, int32_t accumulate_dweight, void* ws,
                                      size_t ws_bytes, void* stream);
 
+/* Logit cache: the same forward and backward (invokerl/policy.py:124-191 and its autograd), with
+ * the backward's logits recompute replaced by stored softmax numerators where memory allows.  The
+ * reference recomputes every chunk's logits under torch.utils.checkpoint; here the forward can
+ * store, for up to `cache_rows` rows, each 32-column chunk's numerators 2^(S log2e - m) in bf16
+ * relative to the chunk maximum m, and m (fp32, log2 units); the backward then forms those rows'
+ * dS = g (onehot - numerator 2^(m - lse log2e)) with a memory-bound pass instead of a GEMM, and
+ * recomputes only the active rows without a slot.  Results equal the uncached calls up to the
+ * bf16 rounding of the numerators (the same relative precision as the bf16 dS itself).
+ *
+ * Cache storage, owned by the caller, per slot: ikrl_lmhead_cache_row_elems gives q_elems bf16
+ * (cache_q rows, 16-byte aligned) and m_elems fp32 (cache_m rows).  Forward: rows with
+ * cache_mask[r] != 0 (every row when cache_mask is NULL) and a target other than -100 get slots
+ * 0, 1, ... in row order until cache_rows are used; cache_slot[N] receives each row's slot or -1.
+ * Workspace: ikrl_lmhead_cache_fwd_workspace_bytes.  Backward: pass the forward's cache_slot,
+ * cache_q and cache_m, unchanged since; workspace and synchronisation as ikrl_lmhead_logprob_bwd
+ * (inside a stream capture, or with IKRL_TUNE_SKIP_ZERO_ROWS = 0, the cache is not used and every
+ * row is recomputed).  V must be a multiple of 8.  No counterpart in the reference. */
+IKRL_API int ikrl_lmhead_cache_row_elems(int32_t V, int64_t* q_elems, int64_t* m_elems);
+IKRL_API size_t ikrl_lmhead_cache_fwd_workspace_bytes(int64_t N, int32_t H, int32_t V);
+IKRL_API int ikrl_lmhead_logprob_fwd_cached(const void* hidden, const void* weight, const int64_t* ids,
+                                            int64_t N, int32_t H, int32_t V, float* logp, float* lse,
+                                            const uint8_t* cache_mask, int64_t cache_rows,
+                                            int32_t* cache_slot, void* cache_q, float* cache_m, void* ws,
+                                            size_t ws_bytes, void* stream);
+IKRL_API int ikrl_lmhead_logprob_bwd_cached(const void* hidden, const void* weight, const int64_t* ids,
+                                            const float* lse, const float* dlogp, int64_t N, int32_t H,
+                                            int32_t V, int64_t chunk_rows, void* dhidden, void* dweight,
+                                            int32_t dweight_dtype, int32_t accumulate_dweight,
+                                            const int32_t* cache_slot, const void* cache_q,
+                                            const float* cache_m, void* ws, size_t ws_bytes, void* stream);
+
 /* Allocation-free variant of ikrl_lmhead_logprob_fwd.  It has no counterpart in the reference.
  * For callers that cannot allocate device memory when they need log-probs: hosts whose own
  * allocator owns all device memory and forbids side allocations, or frameworks whose caching pool

@@ -134,6 +134,17 @@ _SIGNATURES: dict[str, tuple] = {
         [_P, _P, _P, _P, _P, c_int64, c_int32, c_int32, c_int64, _P, _P, c_int32, c_int32, _P, c_size_t, _P],
     ),
     "ikrl_lmhead_status": (ctypes.c_int, [_P, POINTER(c_int32), _P]),
+    "ikrl_lmhead_cache_row_elems": (ctypes.c_int, [c_int32, POINTER(c_int64), POINTER(c_int64)]),
+    "ikrl_lmhead_cache_fwd_workspace_bytes": (c_size_t, [c_int64, c_int32, c_int32]),
+    "ikrl_lmhead_logprob_fwd_cached": (
+        ctypes.c_int,
+        [_P, _P, _P, c_int64, c_int32, c_int32, _P, _P, _P, c_int64, _P, _P, _P, _P, c_size_t, _P],
+    ),
+    "ikrl_lmhead_logprob_bwd_cached": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _P, c_int64, c_int32, c_int32, c_int64, _P, _P, c_int32, c_int32, _P, _P, _P, _P,
+         c_size_t, _P],
+    ),
     "ikrl_lmhead_set_cta_pairs": (ctypes.c_int, [c_int32]),
     "ikrl_lmhead_plan": (ctypes.c_int, [c_int32, c_int64, c_int32, c_int32, c_int32, POINTER(c_int32)]),
     "ikrl_lmhead_logprob_fwd_noalloc": (

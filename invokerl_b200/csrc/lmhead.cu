@@ -26,6 +26,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <vector>
 
 namespace ikrl {
 namespace {
@@ -75,6 +76,14 @@ struct GemmParams {
   int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
   int pace_kb, pace_lag;  // pacing: K blocks between checkpoints, checkpoints a pair may lead by
   int ds_tma;             // DLOGITS in the wide kernel: 1 = stage dS in shared memory, TMA-store it
+  // Logit cache (LSE, optional): rows with slot[r] >= 0 store, per 32-column chunk, the bf16
+  // numerators 2^(S log2e - m) relative to the chunk maximum m and m itself (log2 units), so the
+  // backward can form dS without recomputing the logits.
+  const int* slot;        // [M] cache slot of each row, -1 = not cached; null = no cache
+  uint16_t* cache_q;      // [slots][ld_cache] bf16 numerators
+  float* cache_m;         // [slots][n_mchunks] chunk maxima, log2 units
+  int64_t ld_cache;
+  int n_mchunks;
 };
 
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err) {
@@ -128,6 +137,10 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   if constexpr (EPI == EPI_LSE || EPI == EPI_DLOGITS) {
     if (row_ok) tgt = p.ids[grow];
   }
+  int cslot = -1;  // logit-cache slot of this row (LSE)
+  if constexpr (EPI == EPI_LSE) {
+    if (row_ok && p.slot != nullptr) cslot = p.slot[grow];
+  }
   if constexpr (EPI == EPI_DLOGITS) {
     if (row_ok) {
       lse2 = p.lse[grow] * kLog2e;
@@ -143,7 +156,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
 
   // The epilogue of one 32-column chunk of this thread's row, columns [col0, col0 + 32) of the
   // output (col0 < N; the chunk may end past N).  Warp-uniform control flow.
-  auto chunk = [&](const float* v, int col0) {
+  auto chunk = [&](float* v, int col0) {
     const int nvalid = min(32, p.N - col0);
     if constexpr (EPI == EPI_LSE) {
       float cm = -INFINITY;
@@ -151,15 +164,6 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       for (int i = 0; i < 32; ++i)
         if (i < nvalid) cm = fmaxf(cm, v[i]);
       cm *= kLog2e;
-      if (cm > run_m) {
-        run_s *= fast_exp2(run_m - cm);
-        run_m = cm;
-      }
-      float cs = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < nvalid) cs += fast_exp2(fmaf(v[i], kLog2e, -run_m));
-      run_s += cs;
       // Target gather without a dynamically indexed register array (which would go to local
       // memory): exactly one term is v[rel] * 1, every other term adds zero.
       const int64_t rel = tgt - col0;
@@ -170,6 +174,28 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
         for (int i = 0; i < 32; ++i) acc_t += (i == rr) ? v[i] : 0.f;
         tval = acc_t;
         found = true;
+      }
+      // Numerators relative to the chunk maximum cm (in place of the logits), then the running
+      // (max, sum) update; the numerators are what the logit cache stores.
+      float cs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v[i] = i < nvalid ? fast_exp2(fmaf(v[i], kLog2e, -cm)) : 0.f;
+        cs += v[i];
+      }
+      if (cm > run_m) {
+        run_s = fmaf(run_s, fast_exp2(run_m - cm), cs);
+        run_m = cm;
+      } else {
+        run_s = fmaf(cs, fast_exp2(cm - run_m), run_s);
+      }
+      if (cslot >= 0) {
+        uint16_t* dst = p.cache_q + (int64_t)cslot * p.ld_cache + col0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          st_global_v4(dst + 8 * k, pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
+                       pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+        p.cache_m[(int64_t)cslot * p.n_mchunks + (col0 >> 5)] = cm;
       }
     } else if constexpr (EPI == EPI_DLOGITS) {
       uint32_t w[16];
@@ -1360,8 +1386,8 @@ BwdLayout bwd_layout(int64_t N, int H, int V, int64_t chunk_rows, int dweight_dt
   L.dw_off = al(L.ds_off + (size_t)L.chunk * L.lds * 2);
   size_t o = L.dw_off + (L.need_dw32 ? al((size_t)V * H * 4) : 0);
   L.cblocks = (int)std::max<int64_t>(1, cdiv64(N, kCompactRows));
-  L.cnt_off = o;   o = al(o + (size_t)L.cblocks * 4);
-  L.nact_off = o;  o = al(o + 8);
+  L.cnt_off = o;   o = al(o + (size_t)2 * L.cblocks * 4);
+  L.nact_off = o;  o = al(o + 16);
   L.idx_off = o;   o = al(o + (size_t)N * 4);
   L.pos_off = o;   o = al(o + (size_t)N * 4);
   L.idc_off = o;   o = al(o + (size_t)N * 8);
@@ -1384,15 +1410,150 @@ __device__ __forceinline__ bool row_active(const float* __restrict__ g, const in
   return ids[r] != -100 && g[r] != 0.f;
 }
 
+// Rows are in two classes when the forward cached logits: active rows with a cache slot (their dS
+// comes from the cache) and the other active rows (their dS is recomputed by the GEMM).  The
+// compaction puts the cached class first, each class in row order.  Without a cache (slot null)
+// every active row is in the second class.
+__device__ __forceinline__ bool row_cached(const int* __restrict__ slot, int64_t r) {
+  return slot != nullptr && slot[r] >= 0;
+}
+
+// counts[b] = cached active rows of block b, counts[nb + b] = the other active rows.
 __global__ void __launch_bounds__(kCompactThreads) active_count_kernel(const float* __restrict__ g,
-                                                                       const int64_t* __restrict__ ids, int64_t N,
+                                                                       const int64_t* __restrict__ ids,
+                                                                       const int* __restrict__ slot, int64_t N,
                                                                        int* __restrict__ counts) {
+  __shared__ int wsum[2][kCompactThreads / 32];
+  const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
+  int cc = 0, cu = 0;
+  for (int i = threadIdx.x; i < kCompactRows; i += blockDim.x) {
+    const int64_t r = r0 + i;
+    if (r < N && row_active(g, ids, r)) {
+      if (row_cached(slot, r)) ++cc;
+      else ++cu;
+    }
+  }
+  cc = warp_sum(cc);
+  cu = warp_sum(cu);
+  if ((threadIdx.x & 31) == 0) {
+    wsum[0][threadIdx.x >> 5] = cc;
+    wsum[1][threadIdx.x >> 5] = cu;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tc = 0, tu = 0;
+    for (int w = 0; w < kCompactThreads / 32; ++w) {
+      tc += wsum[0][w];
+      tu += wsum[1][w];
+    }
+    counts[blockIdx.x] = tc;
+    counts[gridDim.x + blockIdx.x] = tu;
+  }
+}
+
+// Block b writes its cached active rows after those of blocks 0..b-1, and its other active rows
+// after all cached rows and the other rows of blocks 0..b-1, each in row order: idx[k] = row,
+// pos[row] = k (-1 for skipped rows), and the compacted ids / lse / g.  The last block writes
+// n_out[0] = active rows and n_out[1] = cached active rows.
+__global__ void __launch_bounds__(kCompactThreads) compact_rows_kernel(
+    const float* __restrict__ g, const int64_t* __restrict__ ids, const int* __restrict__ slot,
+    const float* __restrict__ lse, int64_t N, const int* __restrict__ counts, int* __restrict__ idx,
+    int* __restrict__ pos, int64_t* __restrict__ ids_c, float* __restrict__ lse_c, float* __restrict__ g_c,
+    int64_t* __restrict__ n_out) {
+  constexpr int kWarps = kCompactThreads / 32;
+  __shared__ int wt[2][kWarps];
+  __shared__ int s_base[3];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nb = (int)gridDim.x;
+  int pc = 0, pu = 0, tc = 0;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    const int c = counts[b];
+    tc += c;
+    if (b < (int)blockIdx.x) {
+      pc += c;
+      pu += counts[nb + b];
+    }
+  }
+  pc = warp_sum(pc);
+  pu = warp_sum(pu);
+  tc = warp_sum(tc);
+  __shared__ int red[3][kWarps];
+  if (lane == 0) {
+    red[0][warp] = pc;
+    red[1][warp] = pu;
+    red[2][warp] = tc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int a = 0, b2 = 0, c2 = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      a += red[0][w];
+      b2 += red[1][w];
+      c2 += red[2][w];
+    }
+    s_base[0] = a;       // cached rows before this block
+    s_base[1] = c2 + b2; // other rows: after every cached row and the earlier blocks' other rows
+    s_base[2] = c2;      // cached rows in total
+  }
+  __syncthreads();
+  int base_c = s_base[0], base_u = s_base[1];
+  const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
+  for (int off = 0; off < kCompactRows; off += kCompactThreads) {
+    const int64_t r = r0 + off + threadIdx.x;
+    const bool act = r < N && row_active(g, ids, r);
+    const bool cached = act && row_cached(slot, r);
+    const unsigned bc = __ballot_sync(0xffffffffu, cached);
+    const unsigned bu = __ballot_sync(0xffffffffu, act && !cached);
+    __syncthreads();  // wt is reused
+    if (lane == 0) {
+      wt[0][warp] = __popc(bc);
+      wt[1][warp] = __popc(bu);
+    }
+    __syncthreads();
+    int before_c = 0, before_u = 0, total_c = 0, total_u = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      before_c += (w < warp) ? wt[0][w] : 0;
+      before_u += (w < warp) ? wt[1][w] : 0;
+      total_c += wt[0][w];
+      total_u += wt[1][w];
+    }
+    if (act) {
+      const unsigned below = (1u << lane) - 1u;
+      const int k = cached ? base_c + before_c + __popc(bc & below) : base_u + before_u + __popc(bu & below);
+      idx[k] = (int)r;
+      pos[r] = k;
+      ids_c[k] = ids[r];
+      lse_c[k] = lse[r];
+      g_c[k] = g[r];
+    } else if (r < N) {
+      pos[r] = -1;
+    }
+    base_c += total_c;
+    base_u += total_u;
+  }
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+    n_out[0] = base_u;  // the last block's other rows end at the total active count
+    n_out[1] = s_base[2];
+  }
+}
+
+// Cache slots of the forward: rows with cache_mask[r] != 0 (all rows when null) and a target,
+// numbered in row order; rows past `cap` of them get -1.  counts[b] = such rows of block b.
+__device__ __forceinline__ bool row_wants_cache(const uint8_t* __restrict__ mask, const int64_t* __restrict__ ids,
+                                                int64_t r) {
+  return ids[r] != -100 && (mask == nullptr || mask[r] != 0);
+}
+
+__global__ void __launch_bounds__(kCompactThreads) cache_count_kernel(const uint8_t* __restrict__ mask,
+                                                                      const int64_t* __restrict__ ids, int64_t N,
+                                                                      int* __restrict__ counts) {
   __shared__ int wsum[kCompactThreads / 32];
   const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
   int c = 0;
   for (int i = threadIdx.x; i < kCompactRows; i += blockDim.x) {
     const int64_t r = r0 + i;
-    if (r < N && row_active(g, ids, r)) ++c;
+    if (r < N && row_wants_cache(mask, ids, r)) ++c;
   }
   c = warp_sum(c);
   if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = c;
@@ -1404,13 +1565,10 @@ __global__ void __launch_bounds__(kCompactThreads) active_count_kernel(const flo
   }
 }
 
-// Block b writes its active rows after those of blocks 0..b-1, in row order: idx[k] = row,
-// pos[row] = k (-1 for skipped rows), and the compacted ids / lse / g.  The last block writes
-// the total to n_act.
-__global__ void __launch_bounds__(kCompactThreads) compact_rows_kernel(
-    const float* __restrict__ g, const int64_t* __restrict__ ids, const float* __restrict__ lse, int64_t N,
-    const int* __restrict__ counts, int* __restrict__ idx, int* __restrict__ pos, int64_t* __restrict__ ids_c,
-    float* __restrict__ lse_c, float* __restrict__ g_c, int64_t* __restrict__ n_act) {
+__global__ void __launch_bounds__(kCompactThreads) cache_slot_kernel(const uint8_t* __restrict__ mask,
+                                                                     const int64_t* __restrict__ ids, int64_t N,
+                                                                     const int* __restrict__ counts, int64_t cap,
+                                                                     int* __restrict__ slot) {
   constexpr int kWarps = kCompactThreads / 32;
   __shared__ int wtot[kWarps];
   __shared__ int s_base;
@@ -1430,9 +1588,9 @@ __global__ void __launch_bounds__(kCompactThreads) compact_rows_kernel(
   const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
   for (int off = 0; off < kCompactRows; off += kCompactThreads) {
     const int64_t r = r0 + off + threadIdx.x;
-    const bool act = r < N && row_active(g, ids, r);
-    const unsigned bal = __ballot_sync(0xffffffffu, act);
-    __syncthreads();  // wtot is reused
+    const bool want = r < N && row_wants_cache(mask, ids, r);
+    const unsigned bal = __ballot_sync(0xffffffffu, want);
+    __syncthreads();
     if (lane == 0) wtot[warp] = __popc(bal);
     __syncthreads();
     int before = 0, total = 0;
@@ -1441,19 +1599,45 @@ __global__ void __launch_bounds__(kCompactThreads) compact_rows_kernel(
       before += (w < warp) ? wtot[w] : 0;
       total += wtot[w];
     }
-    if (act) {
+    if (r < N) {
       const int k = base + before + __popc(bal & ((1u << lane) - 1u));
-      idx[k] = (int)r;
-      pos[r] = k;
-      ids_c[k] = ids[r];
-      lse_c[k] = lse[r];
-      g_c[k] = g[r];
-    } else if (r < N) {
-      pos[r] = -1;
+      slot[r] = (want && k < cap) ? k : -1;
     }
     base += total;
   }
-  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) *n_act = base;
+}
+
+// dS of cached rows: for chunk row k (compacted row c0 + k, original row idx[c0 + k]) and column
+// j < V, dS = g * ([j == t] - q * 2^(m - lse log2e)), with q the cached bf16 numerator and m its
+// chunk maximum.  Eight columns per thread (16-byte loads and stores); V must be a multiple of 8.
+__global__ void __launch_bounds__(256) ds_from_cache_kernel(
+    const uint16_t* __restrict__ cache_q, const float* __restrict__ cache_m, int64_t ld_cache, int n_mchunks,
+    const int* __restrict__ slot, const int* __restrict__ idx, const int64_t* __restrict__ ids_c,
+    const float* __restrict__ lse_c, const float* __restrict__ g_c, int64_t c0, int64_t rows, int V,
+    int64_t id_offset, uint16_t* __restrict__ ds, int64_t ld_ds) {
+  const int vec = V >> 3;
+  const int64_t total = rows * vec;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = i / vec;
+    const int j0 = (int)(i - k * vec) << 3;
+    const int64_t kc = c0 + k;
+    const int sl = slot[idx[kc]];
+    const float lse2 = lse_c[kc] * kLog2e;
+    const float gv = g_c[kc];
+    const int64_t t = ids_c[kc] - id_offset;
+    const uint4 qv = *reinterpret_cast<const uint4*>(cache_q + (int64_t)sl * ld_cache + j0);
+    const float sc = fast_exp2(cache_m[(int64_t)sl * n_mchunks + (j0 >> 5)] - lse2);
+    const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float p0 = bf16lo(w[e]) * sc, p1 = bf16hi(w[e]) * sc;
+      const float d0 = gv * (((int64_t)(j0 + 2 * e) == t ? 1.f : 0.f) - p0);
+      const float d1 = gv * (((int64_t)(j0 + 2 * e + 1) == t ? 1.f : 0.f) - p1);
+      o[e] = pack_bf16x2(d0, d1);
+    }
+    *reinterpret_cast<uint4*>(ds + k * ld_ds + j0) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // h_c[k] = h[idx[k]] for k < n, 16 bytes per thread.
@@ -1505,9 +1689,25 @@ static int clear_status_word(void* ws, size_t ws_bytes, void* stream) {
   return IKRL_OK;
 }
 
+// Logit cache of a forward (all null / 0: none).  mask: rows that may be cached (null = every row
+// with a target); cap: cache slots; slot: [N] output, each row's slot or -1; q / m: the cache.
+struct CacheArgs {
+  const uint8_t* mask = nullptr;
+  int64_t cap = 0;
+  int* slot = nullptr;
+  uint16_t* q = nullptr;
+  float* m = nullptr;
+};
+
+// Workspace of the caching forward: the forward's, then the per-block counts of the slot numbering.
+size_t cache_fwd_workspace_bytes(int64_t N, int H, int V) {
+  const size_t base = fwd_layout(N, H, V).total;
+  return base + ((((size_t)std::max<int64_t>(1, cdiv64(N, kCompactRows)) * 4) + 255) & ~size_t(255));
+}
+
 static int lmhead_fwd_impl(const char* what, const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
                     int32_t V, int64_t vocab_start, bool shard, float* logp, float* lse, void* ws, size_t ws_bytes,
-                    void* stream) {
+                    void* stream, const CacheArgs& cache = CacheArgs()) {
   int rc = check_common(hidden, weight, ids, N, H, V, what);
   if (rc) return rc;
   if (N == 0) return clear_status_word(ws, ws_bytes, stream);
@@ -1534,6 +1734,20 @@ static int lmhead_fwd_impl(const char* what, const void* hidden, const void* wei
   p.part_s = reinterpret_cast<float*>(w + L.ps_off);
   p.part_t = reinterpret_cast<float*>(w + L.pt_off);
   p.err = err;
+  if (cache.slot != nullptr) {
+    // Number the rows that get a cache slot (row order, at most cap of them).
+    int* counts = reinterpret_cast<int*>(w + L.total);
+    const int nb = (int)cdiv64(N, kCompactRows);
+    cache_count_kernel<<<nb, kCompactThreads, 0, s>>>(cache.mask, ids, N, counts);
+    if ((rc = check_launch("cache_count_kernel"))) return rc;
+    cache_slot_kernel<<<nb, kCompactThreads, 0, s>>>(cache.mask, ids, N, counts, cache.cap, cache.slot);
+    if ((rc = check_launch("cache_slot_kernel"))) return rc;
+    p.slot = cache.slot;
+    p.cache_q = cache.q;
+    p.cache_m = cache.m;
+    p.ld_cache = cdiv64(V, 64) * 64;
+    p.n_mchunks = (int)cdiv64(V, 32);
+  }
   const int m_tiles = (int)cdiv64(N, BM);
   if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s))) return rc;
   if (shard) {
@@ -1547,10 +1761,14 @@ static int lmhead_fwd_impl(const char* what, const void* hidden, const void* wei
 }
 
 
+// cache_slot / cache_q / cache_m: the logit cache a forward filled (all null: no cache).  Active
+// rows with a slot take their dS from the cache; the others are recomputed by the dS GEMM.
 static int lmhead_bwd_impl(const char* what, const void* hidden, const void* weight, const int64_t* ids,
                            const float* lse, const float* dlogp, int64_t N, int32_t H, int32_t V, int64_t vocab_start,
                            int64_t chunk_rows, void* dhidden, void* dweight, int32_t dweight_dtype,
-                           int32_t accumulate_dweight, void* ws, size_t ws_bytes, void* stream) {
+                           int32_t accumulate_dweight, void* ws, size_t ws_bytes, void* stream,
+                           const int* cache_slot = nullptr, const uint16_t* cache_q = nullptr,
+                           const float* cache_m = nullptr) {
   int rc = check_common(hidden, weight, ids, N, H, V, what);
   if (rc) return rc;
   IKRL_REQUIRE(dweight_dtype == IKRL_DTYPE_F32 || dweight_dtype == IKRL_DTYPE_BF16, IKRL_ERR_UNSUPPORTED,
@@ -1590,6 +1808,8 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
   int64_t Nw = N;
   uint16_t* dh_out = reinterpret_cast<uint16_t*>(dhidden);  // where the dH GEMMs write
   const int* pos = nullptr;                                  // set when dH must be scattered back
+  const int* idx_c = nullptr;                                // compacted row -> row
+  int64_t n_cached = 0;                                      // leading compacted rows whose dS is cached
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   IKRL_CUDA(cudaStreamIsCapturing(s, &cap));
   if (skip_zero_rows_enabled() && cap == cudaStreamCaptureStatusNone && N <= INT32_MAX) {
@@ -1602,30 +1822,32 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
     float* g_c = reinterpret_cast<float*>(w + L.gc_off);
     uint16_t* h_c = reinterpret_cast<uint16_t*>(w + L.hc_off);
     const int nb = (int)cdiv64(N, kCompactRows);
-    active_count_kernel<<<nb, kCompactThreads, 0, s>>>(dlogp, ids, N, counts);
+    active_count_kernel<<<nb, kCompactThreads, 0, s>>>(dlogp, ids, cache_slot, N, counts);
     if ((rc = check_launch("active_count_kernel"))) return rc;
-    compact_rows_kernel<<<nb, kCompactThreads, 0, s>>>(dlogp, ids, lse, N, counts, idx, posw, ids_c, lse_c, g_c,
-                                                        n_act_d);
+    compact_rows_kernel<<<nb, kCompactThreads, 0, s>>>(dlogp, ids, cache_slot, lse, N, counts, idx, posw, ids_c,
+                                                        lse_c, g_c, n_act_d);
     if ((rc = check_launch("compact_rows_kernel"))) return rc;
-    // The chunk plan depends on the active count: read it back (one stream synchronisation).
-    int64_t n_act = 0;
-    IKRL_CUDA(cudaMemcpyAsync(&n_act, n_act_d, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    // The chunk plan depends on the active counts: read them back (one stream synchronisation).
+    int64_t counts_h[2] = {0, 0};
+    IKRL_CUDA(cudaMemcpyAsync(counts_h, n_act_d, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     IKRL_CUDA(cudaStreamSynchronize(s));
-    IKRL_REQUIRE(n_act >= 0 && n_act <= N, IKRL_ERR_DEVICE, "%s: bad active-row count %lld", what,
-                 (long long)n_act);
+    const int64_t n_act = counts_h[0];
+    n_cached = counts_h[1];
+    IKRL_REQUIRE(n_act >= 0 && n_act <= N && n_cached >= 0 && n_cached <= n_act, IKRL_ERR_DEVICE,
+                 "%s: bad active-row counts %lld, %lld", what, (long long)n_act, (long long)n_cached);
     if (n_act == 0) {
       if (dhidden) IKRL_CUDA(cudaMemsetAsync(dhidden, 0, (size_t)N * H * 2, s));
       if (dweight && !accumulate_dweight)
         IKRL_CUDA(cudaMemsetAsync(dweight, 0, (size_t)V * H * (dweight_dtype == IKRL_DTYPE_F32 ? 4 : 2), s));
       return IKRL_OK;
     }
-    if (n_act < N) {
+    if (n_act < N || n_cached > 0) {  // cached rows come first, so the order differs from the rows'
       const int vpr = H / 8;
       const int gb = (int)std::min<int64_t>(cdiv64(n_act * vpr, 256), 148ll * 16);
       gather_rows_kernel<<<gb, 256, 0, s>>>(reinterpret_cast<const uint4*>(hidden), idx, n_act, vpr,
                                             reinterpret_cast<uint4*>(h_c));
       if ((rc = check_launch("gather_rows_kernel"))) return rc;
-      hsrc = h_c; idsrc = ids_c; lsesrc = lse_c; gsrc = g_c; Nw = n_act;
+      hsrc = h_c; idsrc = ids_c; lsesrc = lse_c; gsrc = g_c; Nw = n_act; idx_c = idx;
       // dH of a chunk overwrites that chunk's gathered rows once dW has read them.
       if (dhidden) { dh_out = h_c; pos = posw; }
     }
@@ -1633,7 +1855,18 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
 
   const BwdLayout Lw = bwd_layout(Nw, H, V, chunk_rows, dweight_dtype, accumulate_dweight);
   const int64_t chunk = std::min(L.chunk, Lw.chunk);
-  const int64_t nchunks = cdiv64(Nw, chunk);
+  // Chunks: first the cached rows [0, n_cached), then the others, so every chunk takes its dS one
+  // way (from the cache, or by the recompute GEMM).
+  struct Chunk {
+    int64_t c0, rows;
+    bool cached;
+  };
+  std::vector<Chunk> chunks;
+  for (int seg = 0; seg < 2; ++seg) {
+    const int64_t a0 = seg == 0 ? 0 : n_cached, a1 = seg == 0 ? n_cached : Nw;
+    for (int64_t c0 = a0; c0 < a1; c0 += chunk) chunks.push_back({c0, std::min<int64_t>(chunk, a1 - c0), seg == 0});
+  }
+  const int64_t nchunks = (int64_t)chunks.size();
   const bool use_dw32 = (dweight_dtype == IKRL_DTYPE_BF16) && nchunks > 1;
 
   CUtensorMap t_w_k, t_w_k2, t_w_mn;
@@ -1642,12 +1875,18 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
   if ((rc = make_tmap(&t_w_mn, weight, H, V, H, 64, "weight^T"))) return rc;
 
   for (int64_t ci = 0; ci < nchunks; ++ci) {
-    const int64_t c0 = ci * chunk;
-    const int64_t rows = std::min<int64_t>(chunk, Nw - c0);
+    const int64_t c0 = chunks[ci].c0;
+    const int64_t rows = chunks[ci].rows;
     const int m_tiles = (int)cdiv64(rows, BM);
     const uint16_t* hc = hsrc + c0 * H;
-    // 1) dS = g * (onehot - softmax(h W^T)) for this chunk
-    {
+    // 1) dS = g * (onehot - softmax(h W^T)) for this chunk: from the logit cache, or recomputed
+    if (chunks[ci].cached) {
+      const int64_t work = rows * (V / 8);
+      const int gb = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv64(work, 256), 148ll * 16));
+      ds_from_cache_kernel<<<gb, 256, 0, s>>>(cache_q, cache_m, L.lds, (int)cdiv64(V, 32), cache_slot, idx_c,
+                                              idsrc, lsesrc, gsrc, c0, rows, V, vocab_start, dS, L.lds);
+      if ((rc = check_launch("ds_from_cache_kernel"))) return rc;
+    } else {
       CUtensorMap ta, tds;
       if ((rc = make_tmap(&ta, hc, H, rows, H, BM, "hidden chunk"))) return rc;
       if ((rc = make_store_tmap(&tds, dS, V, rows, L.lds, "dS store"))) return rc;
@@ -1758,6 +1997,58 @@ int ikrl_lmhead_logprob_bwd(const void* hidden, const void* weight, const int64_
   clear_error();
   return lmhead_bwd_impl("ikrl_lmhead_logprob_bwd", hidden, weight, ids, lse, dlogp, N, H, V, 0, chunk_rows, dhidden,
                          dweight, dweight_dtype, accumulate_dweight, ws, ws_bytes, stream);
+}
+
+int ikrl_lmhead_cache_row_elems(int32_t V, int64_t* q_elems, int64_t* m_elems) {
+  clear_error();
+  IKRL_REQUIRE(V > 0 && q_elems && m_elems, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_cache_row_elems: bad arguments");
+  *q_elems = cdiv64(V, 64) * 64;
+  *m_elems = cdiv64(V, 32);
+  return IKRL_OK;
+}
+
+size_t ikrl_lmhead_cache_fwd_workspace_bytes(int64_t N, int32_t H, int32_t V) {
+  if (N <= 0 || H <= 0 || V <= 0) return 256;
+  return cache_fwd_workspace_bytes(N, H, V);
+}
+
+int ikrl_lmhead_logprob_fwd_cached(const void* hidden, const void* weight, const int64_t* ids, int64_t N, int32_t H,
+                                   int32_t V, float* logp, float* lse, const uint8_t* cache_mask, int64_t cache_rows,
+                                   int32_t* cache_slot, void* cache_q, float* cache_m, void* ws, size_t ws_bytes,
+                                   void* stream) {
+  clear_error();
+  const char* what = "ikrl_lmhead_logprob_fwd_cached";
+  IKRL_REQUIRE(V % 8 == 0, IKRL_ERR_UNSUPPORTED, "%s: the logit cache needs V (%d) to be a multiple of 8", what, V);
+  IKRL_REQUIRE(cache_rows >= 0, IKRL_ERR_INVALID_ARGUMENT, "%s: cache_rows %lld < 0", what, (long long)cache_rows);
+  IKRL_REQUIRE(N == 0 || (cache_slot && lse && (cache_rows == 0 || (cache_q && cache_m))), IKRL_ERR_INVALID_ARGUMENT,
+               "%s: null pointer", what);
+  IKRL_REQUIRE((reinterpret_cast<uintptr_t>(cache_q) & 15) == 0 && (reinterpret_cast<uintptr_t>(cache_m) & 3) == 0,
+               IKRL_ERR_ALIGNMENT, "%s: cache_q must be 16-byte and cache_m 4-byte aligned", what);
+  const size_t need = N > 0 ? cache_fwd_workspace_bytes(N, H, V) : 0;
+  IKRL_REQUIRE(N == 0 || (ws != nullptr && ws_bytes >= need), IKRL_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes",
+               what, ws_bytes, need);
+  CacheArgs c;
+  c.mask = cache_mask;
+  c.cap = cache_rows;
+  c.slot = cache_slot;
+  c.q = reinterpret_cast<uint16_t*>(cache_q);
+  c.m = cache_m;
+  return lmhead_fwd_impl(what, hidden, weight, ids, N, H, V, 0, false, logp, lse, ws, ws_bytes, stream, c);
+}
+
+int ikrl_lmhead_logprob_bwd_cached(const void* hidden, const void* weight, const int64_t* ids, const float* lse,
+                                   const float* dlogp, int64_t N, int32_t H, int32_t V, int64_t chunk_rows,
+                                   void* dhidden, void* dweight, int32_t dweight_dtype, int32_t accumulate_dweight,
+                                   const int32_t* cache_slot, const void* cache_q, const float* cache_m, void* ws,
+                                   size_t ws_bytes, void* stream) {
+  clear_error();
+  IKRL_REQUIRE(V % 8 == 0, IKRL_ERR_UNSUPPORTED, "ikrl_lmhead_logprob_bwd_cached: the logit cache needs V (%d) to "
+               "be a multiple of 8", V);
+  IKRL_REQUIRE(N == 0 || (cache_slot && cache_q && cache_m), IKRL_ERR_INVALID_ARGUMENT,
+               "ikrl_lmhead_logprob_bwd_cached: null cache pointer");
+  return lmhead_bwd_impl("ikrl_lmhead_logprob_bwd_cached", hidden, weight, ids, lse, dlogp, N, H, V, 0, chunk_rows,
+                         dhidden, dweight, dweight_dtype, accumulate_dweight, ws, ws_bytes, stream, cache_slot,
+                         reinterpret_cast<const uint16_t*>(cache_q), cache_m);
 }
 
 int ikrl_lmhead_shard_bwd(const void* hidden, const void* weight_shard, const int64_t* ids, const float* lse,

@@ -371,25 +371,94 @@ def default_chunk_rows(N: int, V: int, budget_bytes: int | None = None) -> int:
     return min(N, rows) if N > rows else N
 
 
-def lmhead_forward_raw(hidden: torch.Tensor, weight: torch.Tensor, ids: torch.Tensor):
-    """(logp [N] fp32, lse [N] fp32) of the fused kernel; hidden [N, H] and weight [V, H] bf16."""
+class LogitCache:
+    """Softmax numerators the forward stored for up to `rows` rows (bf16, relative to each
+    32-column chunk's maximum) and those maxima (fp32), with each row's slot (-1: not cached).
+    The backward forms the cached rows' dlogits from it instead of recomputing their logits."""
+
+    def __init__(self, n_rows: int, V: int, rows: int, device):
+        q_el, m_el = N.c_int64(0), N.c_int64(0)
+        call("ikrl_lmhead_cache_row_elems", i32(V), N.byref(q_el), N.byref(m_el))
+        self.rows = int(rows)
+        self.q = torch.empty(self.rows, q_el.value, dtype=torch.bfloat16, device=device)
+        self.m = torch.empty(self.rows, m_el.value, dtype=torch.float32, device=device)
+        self.slot = torch.empty(n_rows, dtype=torch.int32, device=device)
+
+    @staticmethod
+    def bytes_per_row(V: int) -> int:
+        q_el, m_el = N.c_int64(0), N.c_int64(0)
+        call("ikrl_lmhead_cache_row_elems", i32(V), N.byref(q_el), N.byref(m_el))
+        return 2 * q_el.value + 4 * m_el.value
+
+
+# How much device memory the autograd op may give the logit cache: "auto" uses up to `fraction`
+# of the memory free at the forward, after the backward's workspace and outputs and `reserve_bytes`
+# are set aside; "off" never caches (the backward recomputes the logits of every active row).
+_LOGIT_CACHE = {"mode": "auto", "reserve_bytes": 4 << 30, "fraction": 0.9, "min_rows": 1024}
+# Cache rows and candidate rows of the last forward that needed a gradient (for reports).
+LOGIT_CACHE_STATS = {"rows": 0, "candidates": 0}
+
+
+def set_logit_cache(mode: str = "auto", reserve_bytes: int | None = None, fraction: float | None = None) -> dict:
+    """Set the logit-cache policy of `lmhead_logprob`; returns the previous one."""
+    if mode not in ("auto", "off"):
+        raise ValueError(f"logit cache mode {mode!r} is not 'auto' or 'off'")
+    prev = dict(_LOGIT_CACHE)
+    _LOGIT_CACHE["mode"] = mode
+    if reserve_bytes is not None:
+        _LOGIT_CACHE["reserve_bytes"] = int(reserve_bytes)
+    if fraction is not None:
+        _LOGIT_CACHE["fraction"] = float(fraction)
+    return prev
+
+
+def logit_cache_rows(n_rows: int, H: int, V: int, device, candidates: int, chunk_rows: int | None = None) -> int:
+    """Cache rows the policy allows for a forward of n_rows rows with `candidates` cacheable rows."""
+    if _LOGIT_CACHE["mode"] == "off" or V % 8 or candidates <= 0:
+        return 0
+    free, _ = torch.cuda.mem_get_info(device)
+    free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+    if chunk_rows is None:
+        chunk_rows = default_chunk_rows(n_rows, V)
+    bwd = int(N.lib().ikrl_lmhead_bwd_workspace_bytes(n_rows, H, V, chunk_rows, N.IKRL_DTYPE_BF16, 0))
+    outputs = n_rows * H * 2 + V * H * 2  # dhidden and dweight of the backward
+    avail = (free - bwd - outputs - _LOGIT_CACHE["reserve_bytes"]) * _LOGIT_CACHE["fraction"]
+    rows = min(candidates, max(0, int(avail) // LogitCache.bytes_per_row(V)))
+    return rows if rows >= _LOGIT_CACHE["min_rows"] else 0
+
+
+def lmhead_forward_raw(hidden: torch.Tensor, weight: torch.Tensor, ids: torch.Tensor,
+                       cache: LogitCache | None = None, cache_mask: torch.Tensor | None = None):
+    """(logp [N] fp32, lse [N] fp32) of the fused kernel; hidden [N, H] and weight [V, H] bf16.
+    With `cache`, the forward also fills it for rows where `cache_mask` (bool [N]; all rows when
+    None) is set, in row order until its rows are used."""
     dev = N.require_cuda(hidden, weight, ids)
     Nr, H = hidden.shape
     V = weight.shape[0]
     logp = torch.empty(Nr, dtype=torch.float32, device=dev)
     lse = torch.empty(Nr, dtype=torch.float32, device=dev)
-    nbytes = int(N.lib().ikrl_lmhead_fwd_workspace_bytes(Nr, H, V))
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    call("ikrl_lmhead_logprob_fwd", ptr(hidden), ptr(weight), ptr(ids), i64(Nr), i32(H), i32(V), ptr(logp),
-         ptr(lse), ptr(ws), sz(nbytes), N.stream_of(dev))
+    if cache is None:
+        nbytes = int(N.lib().ikrl_lmhead_fwd_workspace_bytes(Nr, H, V))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        call("ikrl_lmhead_logprob_fwd", ptr(hidden), ptr(weight), ptr(ids), i64(Nr), i32(H), i32(V), ptr(logp),
+             ptr(lse), ptr(ws), sz(nbytes), N.stream_of(dev))
+    else:
+        m8 = None if cache_mask is None else N.as_mask(cache_mask.reshape(-1))
+        nbytes = int(N.lib().ikrl_lmhead_cache_fwd_workspace_bytes(Nr, H, V))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        call("ikrl_lmhead_logprob_fwd_cached", ptr(hidden), ptr(weight), ptr(ids), i64(Nr), i32(H), i32(V),
+             ptr(logp), ptr(lse), ptr(m8), i64(cache.rows), ptr(cache.slot), ptr(cache.q), ptr(cache.m), ptr(ws),
+             sz(nbytes), N.stream_of(dev))
     if _CHECK_DEVICE_STATUS:
         lmhead_status(ws)
     return logp, lse
 
 
 def lmhead_backward_raw(hidden, weight, ids, lse, dlogp, want_dh=True, want_dw=True, dw_dtype=torch.bfloat16,
-                        chunk_rows: int | None = None, dweight_out: torch.Tensor | None = None):
-    """(dhidden bf16 [N, H] | None, dweight [V, H] | None) for upstream dlogp [N] fp32."""
+                        chunk_rows: int | None = None, dweight_out: torch.Tensor | None = None,
+                        cache: LogitCache | None = None):
+    """(dhidden bf16 [N, H] | None, dweight [V, H] | None) for upstream dlogp [N] fp32; `cache` is
+    the LogitCache the forward filled, if any."""
     dev = N.require_cuda(hidden, weight, ids, lse, dlogp)
     Nr, H = hidden.shape
     V = weight.shape[0]
@@ -408,9 +477,14 @@ def lmhead_backward_raw(hidden, weight, ids, lse, dlogp, want_dh=True, want_dw=T
     dcode = N.IKRL_DTYPE_F32 if (dw is not None and dw.dtype == torch.float32) else N.IKRL_DTYPE_BF16
     nbytes = int(N.lib().ikrl_lmhead_bwd_workspace_bytes(Nr, H, V, chunk_rows, dcode, accumulate))
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-    call("ikrl_lmhead_logprob_bwd", ptr(hidden), ptr(weight), ptr(ids), ptr(lse), ptr(dlogp), i64(Nr), i32(H),
-         i32(V), i64(chunk_rows), ptr(dh), ptr(dw), i32(dcode), i32(accumulate), ptr(ws), sz(nbytes),
-         N.stream_of(dev))
+    if cache is None:
+        call("ikrl_lmhead_logprob_bwd", ptr(hidden), ptr(weight), ptr(ids), ptr(lse), ptr(dlogp), i64(Nr), i32(H),
+             i32(V), i64(chunk_rows), ptr(dh), ptr(dw), i32(dcode), i32(accumulate), ptr(ws), sz(nbytes),
+             N.stream_of(dev))
+    else:
+        call("ikrl_lmhead_logprob_bwd_cached", ptr(hidden), ptr(weight), ptr(ids), ptr(lse), ptr(dlogp), i64(Nr),
+             i32(H), i32(V), i64(chunk_rows), ptr(dh), ptr(dw), i32(dcode), i32(accumulate), ptr(cache.slot),
+             ptr(cache.q), ptr(cache.m), ptr(ws), sz(nbytes), N.stream_of(dev))
     if _CHECK_DEVICE_STATUS:
         lmhead_status(ws)
     return dh, dw
@@ -434,31 +508,49 @@ def set_check_device_status(enable: bool) -> bool:
 
 
 class LMHeadLogProb(torch.autograd.Function):
-    """log p(targets) of hidden @ weight.T without materialising the logits; fp32 output."""
+    """log p(targets) of hidden @ weight.T without materialising the logits; fp32 output.
+
+    When a gradient is needed and memory allows (`set_logit_cache`), the forward also keeps a
+    logit cache for the rows in `cache_rows` (bool [N]; every row when None), so the backward
+    forms their dlogits from it instead of recomputing the logits; it is freed by the backward."""
 
     @staticmethod
-    def forward(ctx, hidden, weight, ids, chunk_rows):
-        logp, lse = lmhead_forward_raw(hidden, weight, ids)
+    def forward(ctx, hidden, weight, ids, chunk_rows, cache_rows, grad_mode):
+        cache = None
+        # grad_mode: whether gradients were being recorded at the call (forward itself runs without)
+        if grad_mode and (ctx.needs_input_grad[0] or ctx.needs_input_grad[1]):
+            Nr, H = hidden.shape
+            V = weight.shape[0]
+            cand = Nr if cache_rows is None else int(cache_rows.sum())  # one host read per forward
+            rows = logit_cache_rows(Nr, H, V, hidden.device, cand, chunk_rows)
+            if rows > 0:
+                cache = LogitCache(Nr, V, rows, hidden.device)
+            LOGIT_CACHE_STATS.update(rows=rows, candidates=cand)
+        logp, lse = lmhead_forward_raw(hidden, weight, ids, cache, cache_rows)
         ctx.save_for_backward(hidden, weight, ids, lse)
         ctx.chunk_rows = chunk_rows
+        ctx.cache = cache
         return logp
 
     @staticmethod
     def backward(ctx, g):
         hidden, weight, ids, lse = ctx.saved_tensors
         want_dh, want_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        cache, ctx.cache = ctx.cache, None
         if not (want_dh or want_dw):
-            return None, None, None, None
+            return None, None, None, None, None, None
         dh, dw = lmhead_backward_raw(hidden, weight, ids, lse, g.contiguous().float(), want_dh, want_dw,
                                      weight.dtype if weight.dtype == torch.float32 else torch.bfloat16,
-                                     ctx.chunk_rows)
-        return dh, dw, None, None
+                                     ctx.chunk_rows, cache=cache)
+        return dh, dw, None, None, None, None
 
 
 def lmhead_logprob(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
-                   chunk_rows: int | None = None) -> torch.Tensor:
+                   chunk_rows: int | None = None, cache_rows: torch.Tensor | None = None) -> torch.Tensor:
     """Fused F.linear(hidden, weight) + log-softmax gather: hidden [..., H], targets [...] -> fp32 [...].
-    Targets of -100 give 0 (ignored rows)."""
+    Targets of -100 give 0 (ignored rows).  `cache_rows` (bool, shaped like targets) names the rows
+    that may carry a gradient, for the logit cache; rows outside it are recomputed in the backward if
+    they do (results are the same either way)."""
     N.require_cuda(hidden, weight, targets)
     H = hidden.shape[-1]
     shape = targets.shape
@@ -473,7 +565,13 @@ def lmhead_logprob(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Te
     ids = targets.reshape(-1).to(torch.int64).contiguous()
     if h.shape[0] != ids.shape[0]:
         raise ValueError(f"{h.shape[0]} hidden rows but {ids.shape[0]} targets")
-    return LMHeadLogProb.apply(h, w, ids, chunk_rows).reshape(shape)
+    cr = None
+    if cache_rows is not None:
+        cr = cache_rows.reshape(-1)
+        if cr.shape[0] != ids.shape[0]:
+            raise ValueError(f"cache_rows has {cr.shape[0]} entries for {ids.shape[0]} rows")
+        cr = cr.to(device=h.device, dtype=torch.bool).contiguous()
+    return LMHeadLogProb.apply(h, w, ids, chunk_rows, cr, torch.is_grad_enabled()).reshape(shape)
 
 
 # ---------------------------------------------------------------------------------------------

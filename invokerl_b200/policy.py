@@ -79,7 +79,11 @@ class PolicyModel:
         # Every position t < T-1 predicts token t+1; the last position has no target (-100).
         targets = torch.full_like(token_ids, -100)
         targets[:, :-1] = token_ids[:, 1:]
-        lp = ops.lmhead_logprob(hidden, self.model.lm_head.weight, targets)
+        # Rows whose target is an attended token are the ones a loss can weight (the response
+        # tokens among them); they are the candidates for the logit cache of the backward.
+        cache_rows = torch.zeros_like(token_ids, dtype=torch.bool)
+        cache_rows[:, :-1] = attention_mask[:, 1:].bool()
+        lp = ops.lmhead_logprob(hidden, self.model.lm_head.weight, targets, cache_rows=cache_rows)
         pad = torch.zeros(token_ids.shape[0], 1, device=lp.device, dtype=lp.dtype)
         return torch.cat([pad, lp[:, :-1]], dim=1)
 

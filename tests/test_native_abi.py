@@ -185,3 +185,22 @@ def test_lmhead_launch_plan_rejects_bad_arguments(lib):
         _plan(4, 100, 64)
     with pytest.raises(N.IkrlError, match="bad arguments"):
         _plan(0, 0, 64)
+
+
+def test_logit_cache_layout_and_argument_checks(lib):
+    from invokerl_b200 import _native as N
+
+    q, m = N.c_int64(0), N.c_int64(0)
+    N.call("ikrl_lmhead_cache_row_elems", N.i32(151936), N.byref(q), N.byref(m))
+    assert (q.value, m.value) == (151936, 4748)
+    N.call("ikrl_lmhead_cache_row_elems", N.i32(5000), N.byref(q), N.byref(m))
+    assert (q.value, m.value) == (5056, 157)
+    assert lib.ikrl_lmhead_cache_fwd_workspace_bytes(524288, 4096, 151936) > lib.ikrl_lmhead_fwd_workspace_bytes(
+        524288, 4096, 151936)
+    p = N.c_void_p(256)
+    with pytest.raises(N.IkrlError, match="multiple of 8"):
+        N.call("ikrl_lmhead_logprob_fwd_cached", p, p, p, N.i64(4), N.i32(64), N.i32(1001), p, p, None, N.i64(4),
+               p, p, p, p, N.sz(1 << 20), None)
+    with pytest.raises(N.IkrlError, match="null cache"):
+        N.call("ikrl_lmhead_logprob_bwd_cached", p, p, p, p, p, N.i64(4), N.i32(64), N.i32(1000), N.i64(0), p, p,
+               N.i32(N.IKRL_DTYPE_F32), N.i32(0), None, None, None, p, N.sz(1 << 20), None)
