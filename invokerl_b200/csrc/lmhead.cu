@@ -138,8 +138,12 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
     if (row_ok) tgt = p.ids[grow];
   }
   int cslot = -1;  // logit-cache slot of this row (LSE)
+  bool cache_run = false;  // the warp's 32 rows have consecutive slots: one TMA store per block
+  int cslot0 = 0;
   if constexpr (EPI == EPI_LSE) {
     if (row_ok && p.slot != nullptr) cslot = p.slot[grow];
+    cslot0 = __shfl_sync(0xffffffffu, cslot, 0);
+    cache_run = stage_smem != 0 && __all_sync(0xffffffffu, cslot >= 0 && cslot == cslot0 + lane);
   }
   if constexpr (EPI == EPI_DLOGITS) {
     if (row_ok) {
@@ -189,14 +193,31 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       } else {
         run_s = fmaf(cs, fast_exp2(cm - run_m), run_s);
       }
-      if (cslot >= 0) {
+      if (cache_run) {
+        // Consecutive slots: the 32 x 32 block goes out with one TMA store, as the dS blocks do.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        const uint32_t row_addr = stage_smem + (uint32_t)lane * 64u;
+        const uint32_t sw = ((uint32_t)lane >> 1) & 3u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          st_shared_v4(row_addr + ((((uint32_t)k) ^ sw) << 4), pack_bf16x2(v[8 * k], v[8 * k + 1]),
+                       pack_bf16x2(v[8 * k + 2], v[8 * k + 3]), pack_bf16x2(v[8 * k + 4], v[8 * k + 5]),
+                       pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tm_store, stage_smem, col0, cslot0);
+          bulk_commit();
+        }
+      } else if (cslot >= 0) {
         uint16_t* dst = p.cache_q + (int64_t)cslot * p.ld_cache + col0;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           st_global_v4(dst + 8 * k, pack_bf16x2(v[8 * k], v[8 * k + 1]), pack_bf16x2(v[8 * k + 2], v[8 * k + 3]),
                        pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
-        p.cache_m[(int64_t)cslot * p.n_mchunks + (col0 >> 5)] = cm;
       }
+      if (cslot >= 0) p.cache_m[(int64_t)cslot * p.n_mchunks + (col0 >> 5)] = cm;
     } else if constexpr (EPI == EPI_DLOGITS) {
       uint32_t w[16];
 #pragma unroll
@@ -320,7 +341,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       }
     }
   }
-  if constexpr (EPI == EPI_DLOGITS) {
+  if constexpr (EPI == EPI_DLOGITS || EPI == EPI_LSE) {
     // Every TMA store of this warp has completed before the CTA can exit.
     if (stage_smem != 0 && lane == 0) bulk_wait_all();
     __syncwarp();
@@ -938,7 +959,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     // ---------------- epilogue (both CTAs, own 128 rows x 512 columns) ----------------
     const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
     const uint32_t ae[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0), mapa_shared(smem_u32(&acc_empty[1]), 0)};
-    const uint32_t stage = (EPI == EPI_DLOGITS && p.ds_tma)
+    const uint32_t stage = ((EPI == EPI_DLOGITS || EPI == EPI_LSE) && p.ds_tma)
                                ? smem_base + kWideStages * kWideStageBytes + (uint32_t)(warp - 2) * kDsStageBytes
                                : 0u;
     int jb = 0;
@@ -1139,7 +1160,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
                      int m_tiles, cudaStream_t s) {
   GemmParams p = p_in;
   auto kern = WIDE ? lmhead_gemm_wide_kernel<EPI, A_MN, B_MN> : lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
-  p.ds_tma = (WIDE && EPI == EPI_DLOGITS && c != nullptr) ? 1 : 0;
+  p.ds_tma = (WIDE && c != nullptr && (EPI == EPI_DLOGITS || (EPI == EPI_LSE && p.slot != nullptr))) ? 1 : 0;
   const uint32_t smem_bytes = WIDE ? (p.ds_tma ? kWideDsSmemBytes : kWideSmemBytes) : kPairSmemBytes;
   IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
   IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
@@ -1748,8 +1769,13 @@ static int lmhead_fwd_impl(const char* what, const void* hidden, const void* wei
     p.ld_cache = cdiv64(V, 64) * 64;
     p.n_mchunks = (int)cdiv64(V, 32);
   }
+  CUtensorMap tq;
+  if (cache.slot != nullptr && cache.cap > 0)
+    if ((rc = make_store_tmap(&tq, cache.q, V, cache.cap, cdiv64(V, 64) * 64, "logit cache store"))) return rc;
   const int m_tiles = (int)cdiv64(N, BM);
-  if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s))) return rc;
+  if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s,
+                                             (cache.slot != nullptr && cache.cap > 0) ? &tq : nullptr)))
+    return rc;
   if (shard) {
     lse_shard_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N,
                                                                       vocab_start, V, p.part_sets, logp, lse, err);
