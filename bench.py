@@ -1354,6 +1354,9 @@ def apply_tuning(args) -> dict:
     if args.ds_chunk_bytes:
         ops.set_ds_chunk_bytes(args.ds_chunk_bytes)
         applied["ds_chunk_bytes"] = args.ds_chunk_bytes
+    if args.logit_cache != "auto":
+        ops.set_logit_cache(args.logit_cache)
+        applied["logit_cache"] = args.logit_cache
     return applied
 
 
@@ -1378,6 +1381,8 @@ def main() -> int:
     ap.add_argument("--tune", action="append", default=[], metavar="KNOB=VALUE",
                     help="set a library launch knob (ikrl_set_tuning) for an A/B run")
     ap.add_argument("--ds-chunk-bytes", type=int, default=0, help="bytes of the K1 backward's dlogits chunk")
+    ap.add_argument("--logit-cache", choices=["auto", "off"], default="auto",
+                    help="the K1 logit cache policy (off: the backward recomputes every active row's logits)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

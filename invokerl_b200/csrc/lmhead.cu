@@ -49,7 +49,10 @@ constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment sl
 constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint32_t kMnAtomBytes = 64 * BK * 2;  // one 64-wide MN slab of an MN-major tile: 8 KB
 
-enum Epi : int { EPI_LSE = 0, EPI_DLOGITS = 1, EPI_STORE_BF16 = 2, EPI_F32 = 3 };
+// EPI_LSE_CACHED: the forward's epilogue that also fills the logit cache (its own instantiation,
+// so the plain forward carries none of the cache's code).
+enum Epi : int { EPI_LSE = 0, EPI_DLOGITS = 1, EPI_STORE_BF16 = 2, EPI_F32 = 3, EPI_LSE_CACHED = 4 };
+constexpr bool is_lse(int epi) { return epi == EPI_LSE || epi == EPI_LSE_CACHED; }
 enum F32Mode : int { F32_STORE = 0, F32_ADD = 1, F32_ADD_TO_BF16 = 2 };
 
 struct GemmParams {
@@ -134,13 +137,13 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   const bool row_ok = grow < p.M;
   int64_t tgt = -1;
   float lse2 = 0.f, gval = 0.f;
-  if constexpr (EPI == EPI_LSE || EPI == EPI_DLOGITS) {
+  if constexpr (is_lse(EPI) || EPI == EPI_DLOGITS) {
     if (row_ok) tgt = p.ids[grow];
   }
   int cslot = -1;  // logit-cache slot of this row (LSE)
   bool cache_run = false;  // the warp's 32 rows have consecutive slots: one TMA store per block
   int cslot0 = 0;
-  if constexpr (EPI == EPI_LSE) {
+  if constexpr (EPI == EPI_LSE_CACHED) {
     if (row_ok && p.slot != nullptr) cslot = p.slot[grow];
     cslot0 = __shfl_sync(0xffffffffu, cslot, 0);
     cache_run = stage_smem != 0 && __all_sync(0xffffffffu, cslot >= 0 && cslot == cslot0 + lane);
@@ -162,7 +165,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
   // output (col0 < N; the chunk may end past N).  Warp-uniform control flow.
   auto chunk = [&](float* v, int col0) {
     const int nvalid = min(32, p.N - col0);
-    if constexpr (EPI == EPI_LSE) {
+    if constexpr (is_lse(EPI)) {
       float cm = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 32; ++i)
@@ -193,6 +196,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       } else {
         run_s = fmaf(cs, fast_exp2(cm - run_m), run_s);
       }
+      if constexpr (EPI == EPI_LSE_CACHED) {
       if (cache_run) {
         // Consecutive slots: the 32 x 32 block goes out with one TMA store, as the dS blocks do.
         if (lane == 0) bulk_wait_read_all();
@@ -218,6 +222,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
                        pack_bf16x2(v[8 * k + 4], v[8 * k + 5]), pack_bf16x2(v[8 * k + 6], v[8 * k + 7]));
       }
       if (cslot >= 0) p.cache_m[(int64_t)cslot * p.n_mchunks + (col0 >> 5)] = cm;
+      }  // EPI_LSE_CACHED
     } else if constexpr (EPI == EPI_DLOGITS) {
       uint32_t w[16];
 #pragma unroll
@@ -341,12 +346,12 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       }
     }
   }
-  if constexpr (EPI == EPI_DLOGITS || EPI == EPI_LSE) {
+  if constexpr (EPI == EPI_DLOGITS || EPI == EPI_LSE_CACHED) {
     // Every TMA store of this warp has completed before the CTA can exit.
     if (stage_smem != 0 && lane == 0) bulk_wait_all();
     __syncwarp();
   }
-  if constexpr (EPI == EPI_LSE) {
+  if constexpr (is_lse(EPI)) {
     if (row_ok && !*abort_v) {
       const int set = split * GROUPS + group;
       p.part_m[(int64_t)set * p.M + grow] = run_m;
@@ -959,7 +964,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
     // ---------------- epilogue (both CTAs, own 128 rows x 512 columns) ----------------
     const uint32_t af[2] = {smem_u32(&acc_full[0]), smem_u32(&acc_full[1])};
     const uint32_t ae[2] = {mapa_shared(smem_u32(&acc_empty[0]), 0), mapa_shared(smem_u32(&acc_empty[1]), 0)};
-    const uint32_t stage = ((EPI == EPI_DLOGITS || EPI == EPI_LSE) && p.ds_tma)
+    const uint32_t stage = ((EPI == EPI_DLOGITS || EPI == EPI_LSE_CACHED) && p.ds_tma)
                                ? smem_base + kWideStages * kWideStageBytes + (uint32_t)(warp - 2) * kDsStageBytes
                                : 0u;
     int jb = 0;
@@ -1152,7 +1157,7 @@ int pace_array(unsigned** out) {
 
 // Pacing of the wide kernel's pairs: IKRL_TUNE_PACE is a mask over the epilogues, bit EPI set =
 // launches with that epilogue are paced (all by default).
-bool pacing_enabled(int epi) { return (tuning(IKRL_TUNE_PACE) >> epi) & 1; }
+bool pacing_enabled(int epi) { return (tuning(IKRL_TUNE_PACE) >> (epi == EPI_LSE_CACHED ? EPI_LSE : epi)) & 1; }
 bool persistent_pairs() { return tuning(IKRL_TUNE_PERSISTENT) != 0; }
 
 template <int EPI, bool A_MN, bool B_MN, bool WIDE>
@@ -1160,7 +1165,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
                      int m_tiles, cudaStream_t s) {
   GemmParams p = p_in;
   auto kern = WIDE ? lmhead_gemm_wide_kernel<EPI, A_MN, B_MN> : lmhead_gemm_pair_kernel<EPI, A_MN, B_MN>;
-  p.ds_tma = (WIDE && c != nullptr && (EPI == EPI_DLOGITS || (EPI == EPI_LSE && p.slot != nullptr))) ? 1 : 0;
+  p.ds_tma = (WIDE && c != nullptr && (EPI == EPI_DLOGITS || EPI == EPI_LSE_CACHED)) ? 1 : 0;
   const uint32_t smem_bytes = WIDE ? (p.ds_tma ? kWideDsSmemBytes : kWideSmemBytes) : kPairSmemBytes;
   IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
   IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
@@ -1630,34 +1635,38 @@ __global__ void __launch_bounds__(kCompactThreads) cache_slot_kernel(const uint8
 
 // dS of cached rows: for chunk row k (compacted row c0 + k, original row idx[c0 + k]) and column
 // j < V, dS = g * ([j == t] - q * 2^(m - lse log2e)), with q the cached bf16 numerator and m its
-// chunk maximum.  Eight columns per thread (16-byte loads and stores); V must be a multiple of 8.
+// chunk maximum.  Block row y handles chunk rows y, y + gridDim.y, ...; eight columns per thread
+// (16-byte loads and stores); V must be a multiple of 8.
 __global__ void __launch_bounds__(256) ds_from_cache_kernel(
     const uint16_t* __restrict__ cache_q, const float* __restrict__ cache_m, int64_t ld_cache, int n_mchunks,
     const int* __restrict__ slot, const int* __restrict__ idx, const int64_t* __restrict__ ids_c,
     const float* __restrict__ lse_c, const float* __restrict__ g_c, int64_t c0, int64_t rows, int V,
     int64_t id_offset, uint16_t* __restrict__ ds, int64_t ld_ds) {
   const int vec = V >> 3;
-  const int64_t total = rows * vec;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t k = i / vec;
-    const int j0 = (int)(i - k * vec) << 3;
+  for (int64_t k = blockIdx.y; k < rows; k += gridDim.y) {
     const int64_t kc = c0 + k;
-    const int sl = slot[idx[kc]];
+    const int64_t sl = slot[idx[kc]];
     const float lse2 = lse_c[kc] * kLog2e;
     const float gv = g_c[kc];
     const int64_t t = ids_c[kc] - id_offset;
-    const uint4 qv = *reinterpret_cast<const uint4*>(cache_q + (int64_t)sl * ld_cache + j0);
-    const float sc = fast_exp2(cache_m[(int64_t)sl * n_mchunks + (j0 >> 5)] - lse2);
-    const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-    uint32_t o[4];
+    const uint16_t* qrow = cache_q + sl * ld_cache;
+    const float* mrow = cache_m + sl * n_mchunks;
+    uint16_t* drow = ds + k * ld_ds;
+    for (int jv = blockIdx.x * blockDim.x + threadIdx.x; jv < vec; jv += gridDim.x * blockDim.x) {
+      const int j0 = jv << 3;
+      const uint4 qv = *reinterpret_cast<const uint4*>(qrow + j0);
+      const float sc = fast_exp2(mrow[j0 >> 5] - lse2);
+      const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+      uint32_t o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float p0 = bf16lo(w[e]) * sc, p1 = bf16hi(w[e]) * sc;
-      const float d0 = gv * (((int64_t)(j0 + 2 * e) == t ? 1.f : 0.f) - p0);
-      const float d1 = gv * (((int64_t)(j0 + 2 * e + 1) == t ? 1.f : 0.f) - p1);
-      o[e] = pack_bf16x2(d0, d1);
+      for (int e = 0; e < 4; ++e) {
+        const float p0 = bf16lo(w[e]) * sc, p1 = bf16hi(w[e]) * sc;
+        const float d0 = gv * (((int64_t)(j0 + 2 * e) == t ? 1.f : 0.f) - p0);
+        const float d1 = gv * (((int64_t)(j0 + 2 * e + 1) == t ? 1.f : 0.f) - p1);
+        o[e] = pack_bf16x2(d0, d1);
+      }
+      *reinterpret_cast<uint4*>(drow + j0) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    *reinterpret_cast<uint4*>(ds + k * ld_ds + j0) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -1773,9 +1782,11 @@ static int lmhead_fwd_impl(const char* what, const void* hidden, const void* wei
   if (cache.slot != nullptr && cache.cap > 0)
     if ((rc = make_store_tmap(&tq, cache.q, V, cache.cap, cdiv64(V, 64) * 64, "logit cache store"))) return rc;
   const int m_tiles = (int)cdiv64(N, BM);
-  if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s,
-                                             (cache.slot != nullptr && cache.cap > 0) ? &tq : nullptr)))
-    return rc;
+  if (cache.slot != nullptr && cache.cap > 0) {
+    if ((rc = launch_k1<EPI_LSE_CACHED, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s, &tq))) return rc;
+  } else {
+    if ((rc = launch_k1<EPI_LSE, false, false>(ta, tb, ta, tb2, p, m_tiles, L.splits, s))) return rc;
+  }
   if (shard) {
     lse_shard_combine_kernel<<<(unsigned)cdiv64(N, 256), 256, 0, s>>>(p.part_m, p.part_s, p.part_t, ids, (int)N,
                                                                       vocab_start, V, p.part_sets, logp, lse, err);
@@ -1907,10 +1918,9 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
     const uint16_t* hc = hsrc + c0 * H;
     // 1) dS = g * (onehot - softmax(h W^T)) for this chunk: from the logit cache, or recomputed
     if (chunks[ci].cached) {
-      const int64_t work = rows * (V / 8);
-      const int gb = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv64(work, 256), 148ll * 16));
-      ds_from_cache_kernel<<<gb, 256, 0, s>>>(cache_q, cache_m, L.lds, (int)cdiv64(V, 32), cache_slot, idx_c,
-                                              idsrc, lsesrc, gsrc, c0, rows, V, vocab_start, dS, L.lds);
+      const dim3 grid((unsigned)std::max<int64_t>(1, cdiv64(V / 8, 256)), (unsigned)std::min<int64_t>(rows, 65535));
+      ds_from_cache_kernel<<<grid, 256, 0, s>>>(cache_q, cache_m, L.lds, (int)cdiv64(V, 32), cache_slot, idx_c,
+                                                idsrc, lsesrc, gsrc, c0, rows, V, vocab_start, dS, L.lds);
       if ((rc = check_launch("ds_from_cache_kernel"))) return rc;
     } else {
       CUtensorMap ta, tds;

@@ -85,7 +85,7 @@ def test_every_row_cached_and_active():
 
 
 def test_autograd_op_uses_the_cache_and_matches_the_uncached_op():
-    N_, H, V = 4096, 1024, 151936
+    N_, H, V = 4096, 2048, 151936
     li = lmhead_inputs(N_, H, V, seed=5, w_std=0.05)
     gen = torch.Generator().manual_seed(6)
     rows = torch.rand(N_, generator=gen) < 0.5
@@ -107,6 +107,12 @@ def test_autograd_op_uses_the_cache_and_matches_the_uncached_op():
     assert st_a["rows"] == int(rows.sum()) and st_o["rows"] == 0
     assert torch.equal(lp_a, lp_o)
     assert rel_fro(dh_a, dh_o) <= 5e-3 and rel_fro(dw_a, dw_o) <= 5e-3
+
+
+def test_policy_skips_narrow_heads():
+    """Below H = 2048 the cache costs more than the recompute it saves; "auto" does not cache."""
+    assert ops.logit_cache_rows(4096, 1024, 151936, torch.device(DEV), 4096) == 0
+    assert ops.logit_cache_rows(4096, 4096, 151936, torch.device(DEV), 4096) == 4096
 
 
 def test_no_gradient_no_cache():
