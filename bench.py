@@ -324,8 +324,9 @@ class LMHeadGRPO:
         }
 
     def _traffic(self, n, n_act):
-        f = TRAFFIC["lmhead_fwd_per_row"].get(self.H)
-        b = TRAFFIC["lmhead_bwd_per_active_row"].get(self.H)
+        cached = ops_stats()["rows"] > 0
+        f = TRAFFIC["lmhead_fwd_per_row_cached" if cached else "lmhead_fwd_per_row"].get(self.H)
+        b = TRAFFIC["lmhead_bwd_per_active_row_cached" if cached else "lmhead_bwd_per_active_row"].get(self.H)
         return None if f is None or b is None else f * n + b * n_act
 
     def config(self, world):
@@ -890,6 +891,11 @@ TRAFFIC = {
     # over 131,072 rows moved 4.66 GB, the one backward chunk of 10,066 active rows 13.0 GB.
     "lmhead_fwd_per_row": {4096: 51.37e9 / 65536, 1024: 4.66e9 / 131072},
     "lmhead_bwd_per_active_row": {4096: 106.1e9 / 28160, 1024: 13.0e9 / 10066},
+    # With the logit cache (H = 4096, the same step, 36,992 of 65,536 rows cached): the caching
+    # forward moved 75.97 GB (12.1 GB of it the cache), one full backward chunk 110.3 GB (dS from
+    # the cache 17.6 GB, dW 47.8 GB, dH 44.9 GB).
+    "lmhead_fwd_per_row_cached": {4096: 75.97e9 / 65536},
+    "lmhead_bwd_per_active_row_cached": {4096: 110.3e9 / 28160},
     # K2 forward + backward over [4096, 151936] bf16 logits, 51% active rows
     # (profiles/logits_logprob_fwd_bwd_4096x151936.md): 3.069 GB.
     "logits_per_row": 3.069e9 / 4096,
