@@ -68,6 +68,29 @@ def test_cached_backward_matches_recompute_and_oracle(N_, H, V, chunk, cap_frac)
     assert rel_fro(dw_c.cpu(), dw_o) <= 1e-2
 
 
+@pytest.mark.parametrize("knobs", [{"cta_pairs": 0}, {"wide": 1}, {"wide": 0}, {"skip_zero_rows": 0}])
+def test_cache_under_each_kernel_choice(knobs):
+    """The caching forward in the single-CTA, wide-pair and 256 x 256 pair kernels, and a backward
+    that does not compact rows (the cache then goes unused): gradients as without the cache."""
+    N_, H, V = 900, 512, 20000
+    li = lmhead_inputs(N_, H, V, seed=21, w_std=0.1)
+    gen = torch.Generator().manual_seed(3)
+    g = torch.randn(N_, generator=gen) * (torch.rand(N_, generator=gen) < 0.5)
+    h, w, td, gd = li.hidden.to(DEV), li.weight.to(DEV), li.targets.to(DEV), g.to(DEV)
+    with N.tuning(**knobs):
+        cache = ops.LogitCache(N_, V, N_, DEV)
+        lp_c, lse_c = ops.lmhead_forward_raw(h, w, td, cache, None)
+        lp_p, lse_p = ops.lmhead_forward_raw(h, w, td)
+        dh_c, dw_c = ops.lmhead_backward_raw(h, w, td, lse_c, gd, dw_dtype=torch.float32, chunk_rows=256,
+                                             cache=cache)
+        dh_p, dw_p = ops.lmhead_backward_raw(h, w, td, lse_p, gd, dw_dtype=torch.float32, chunk_rows=256)
+        torch.cuda.synchronize()
+    assert torch.equal(lp_c, lp_p)
+    assert rel_fro(dh_c, dh_p) <= 5e-3 and rel_fro(dw_c, dw_p) <= 5e-3
+    _, dh_o, dw_o = oracle.lmhead_logprob_grads(li.hidden, li.weight, li.targets, g)
+    assert rel_fro(dh_c.cpu(), dh_o) <= 1e-2 and rel_fro(dw_c.cpu(), dw_o) <= 1e-2
+
+
 def test_every_row_cached_and_active():
     """All rows active and all cached: the backward still reorders (cached class first) and
     scatters dH back to the original rows."""
