@@ -104,7 +104,8 @@ enum {
                                    rows; 0 auto (default: 40 when H >= 2048, else 24) */
   IKRL_TUNE_LOSS_KERNEL = 10,   /* GRPO/DAPO loss: 1 register loads (default); 2 bulk-copy staged;
                                    0 the general clipped-ratio kernel */
-  IKRL_TUNE_COUNT = 11
+  IKRL_TUNE_PACE_KB_LONG = 11,  /* pacing checkpoint spacing of the dW and dH launches (default 128) */
+  IKRL_TUNE_COUNT = 12
 };
 /* Passed as `value`, restores the knob's default. */
 #define IKRL_TUNE_DEFAULT (-0x7fffffffffffffffLL - 1)

@@ -38,6 +38,7 @@ TUNE = {
     "l2_policy": 8,
     "l2_budget_mb": 9,
     "loss_kernel": 10,
+    "pace_kb_long": 11,
 }
 TUNE_DEFAULT = -(1 << 63)
 LOSS_NSUMS = 16

@@ -36,6 +36,7 @@ constexpr KnobSpec kKnobs[IKRL_TUNE_COUNT] = {
     {-1, -1, 22},       // IKRL_TUNE_L2_POLICY
     {0, 0, 1024},       // IKRL_TUNE_L2_BUDGET_MB
     {1, 0, 2},          // IKRL_TUNE_LOSS_KERNEL
+    {128, 1, 1 << 20},  // IKRL_TUNE_PACE_KB_LONG
 };
 
 struct Knobs {

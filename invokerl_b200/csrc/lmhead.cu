@@ -1184,7 +1184,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
     IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));
-    p.pace_kb = (int)tuning(IKRL_TUNE_PACE_KB);
+    p.pace_kb = (int)tuning((EPI == EPI_F32 || EPI == EPI_STORE_BF16) ? IKRL_TUNE_PACE_KB_LONG : IKRL_TUNE_PACE_KB);
     p.pace_lag = (int)tuning(IKRL_TUNE_PACE_LAG);
   }
   cudaLaunchConfig_t cfg = {};

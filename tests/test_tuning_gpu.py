@@ -17,6 +17,7 @@ VARIANTS = (
     + [{"cta_pairs": 0}, {"skip_zero_rows": 0}, {"persistent": 0}, {"pace": 0}, {"pace": 3}, {"balance_splits": 0}]
     + [{"wide": v} for v in (0, 1, 2)]
     + [{"pace_kb": v} for v in (1, 7, 256)]
+    + [{"pace_kb_long": v} for v in (16, 512)]
     + [{"pace_lag": v} for v in (0, 2, 5)]
     + [{"l2_policy": 10 * a + b} for a in range(3) for b in range(3)]
     + [{"l2_budget_mb": v} for v in (1, 8, 200)]
