@@ -39,6 +39,7 @@ TUNE = {
     "l2_budget_mb": 9,
     "loss_kernel": 10,
     "pace_kb_long": 11,
+    "split_tail": 12,
 }
 TUNE_DEFAULT = -(1 << 63)
 LOSS_NSUMS = 16

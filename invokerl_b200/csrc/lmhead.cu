@@ -78,6 +78,7 @@ struct GemmParams {
   unsigned* lockstep;     // [npairs] tiles started per pair (zeroed per launch), or null: no pacing
   int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
   int pace_kb, pace_lag;  // pacing: K blocks between checkpoints, checkpoints a pair may lead by
+  int split_tail;         // wide kernel: the last K blocks of a tile run first-half-first
   int ds_tma;             // DLOGITS in the wide kernel: 1 = stage dS in shared memory, TMA-store it
   // Logit cache (LSE, optional): rows with slot[r] >= 0 store, per 32-column chunk, the bf16
   // numerators 2^(S log2e - m) relative to the chunk maximum m and m itself (log2 units), so the
@@ -110,9 +111,11 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 // tile_base: number of tiles this CTA consumed before this unit (accumulator ring position).
 // Returns false when a wait gave up (abort).
 // GROUPS: column groups; warp w drains TMEM lane quadrant w % 4 and column group (w - 2) / 4.
-// SPLIT (wide tile, one accumulator): every warp loads its columns of the first 256-column half
-// into registers and releases that half (acc_empty[0]) at once, so the next tile's first-half
-// MMAs start while it computes; then it does the same for the second half (acc_empty[1]).
+// SPLIT (wide tile, one accumulator): the halves complete separately (acc_full[0] when the first
+// 256-column half of a tile is final, acc_full[1] for the second).  Every warp loads its columns
+// of the first half into registers and releases that half (acc_empty[0]) at once, so the next
+// tile's first-half MMAs start while it computes; then it does the same for the second half
+// (acc_empty[1]).
 // stage_smem (DLOGITS only, 0 = unused): this warp's 2 KB staging tile; the dS values of each
 // 32 x 32 block are written there in the 64-byte swizzled layout of tm_store and sent to global
 // memory with one TMA store per block, instead of 32 scattered row stores.
@@ -305,17 +308,27 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
         }
       }
     }
-    if (!mbar_wait(acc_full[acc], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) {
-      ok = false;
-      break;
+    if constexpr (!SPLIT) {
+      if (!mbar_wait(acc_full[acc], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
     }
-    tc_fence_after();
     const int n0 = (t_begin + j) * TILE_N;
     const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
     if constexpr (SPLIT) {
-      // Load a half's columns, release the half, then compute from registers.
+      // Each half has its own full barrier (the MMA issuer finishes the first half of a tile
+      // before the second): wait for the half, load its columns, release it, then compute from
+      // registers.
+      bool waited = true;
 #pragma unroll
       for (int sg = 0; sg < 2; ++sg) {
+        if (!mbar_wait(acc_full[sg], acc_phase, abort_v, p.err, kErrTimeoutEpilogue)) {
+          waited = false;
+          break;
+        }
+        tc_fence_after();
         const int cs = sg * (TILE_N / 2) + group * kSegCols;
         float v[kSegCols];
 #pragma unroll
@@ -327,6 +340,10 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
 #pragma unroll
         for (int cc = 0; cc < kSegCols; cc += 32)
           if (n0 + cs + cc < p.N) chunk(v + cc, n0 + cs + cc);
+      }
+      if (!waited) {
+        ok = false;
+        break;
       }
     } else {
 #pragma unroll 1
@@ -930,6 +947,12 @@ __global__ void __launch_bounds__(kWideThreads, 1)
             }
           }
           if (!ok) break;
+          auto commit_full = [&](int h) {
+            const uint32_t fb = smem_u32(&acc_full[h]);
+            mma_commit_pair(mapa_shared(fb, 0));
+            mma_commit_pair(mapa_shared(fb, 1));
+          };
+          if (look == nk) commit_full(0);  // the whole first half is issued
           if (!mbar_wait(smem_u32(&acc_empty[1]), epar, abort_v, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -940,7 +963,11 @@ __global__ void __launch_bounds__(kWideThreads, 1)
             release_stage(stage);
             if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
           }
-          for (int kb = look; kb < nk; ++kb) {
+          // The last `tail` K blocks run first-half-first: the first half is final while the
+          // second half's last MMAs still run, so the epilogue drains it and releases it for the
+          // next tile without idling the tensor pipe.
+          const int tail = p.split_tail ? min(kWideStages, nk - look) : 0;
+          for (int kb = look; kb < nk - tail; ++kb) {
             if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
             tc_fence_after();
             issue_half(stage, kb, 0);
@@ -948,11 +975,27 @@ __global__ void __launch_bounds__(kWideThreads, 1)
             release_stage(stage);
             if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
           }
-          if (ok) {
-            const uint32_t fb = smem_u32(&acc_full[0]);
-            mma_commit_pair(mapa_shared(fb, 0));
-            mma_commit_pair(mapa_shared(fb, 1));
+          if (!ok) break;
+          if (tail > 0) {
+            int st = stage;
+            uint32_t ph = phase;
+            for (int kb = nk - tail; kb < nk; ++kb) {
+              if (!mbar_wait(smem_u32(&full_bar[st]), ph, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
+              tc_fence_after();
+              issue_half(st, kb, 0);
+              if (++st == kWideStages) { st = 0; ph ^= 1u; }
+            }
+            if (!ok) break;
+            commit_full(0);
+            for (int kb = nk - tail; kb < nk; ++kb) {
+              issue_half(stage, kb, 1);
+              release_stage(stage);
+              if (++stage == kWideStages) { stage = 0; phase ^= 1u; }
+            }
+          } else if (look < nk) {
+            commit_full(0);
           }
+          commit_full(1);
         }
       }
       if (!ok) {
@@ -1178,6 +1221,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
   const bool persistent = persistent_pairs();
   const int64_t npairs = std::max<int64_t>(1, persistent ? std::min<int64_t>(nunits, nsm / 2) : nunits);
   p.lockstep = nullptr;
+  p.split_tail = (int)tuning(IKRL_TUNE_SPLIT_TAIL);
   // Pacing helps the wide kernel (long tiles, W re-read across pairs); on the 256 x 256 pair
   // kernel at K = 1024 it measured 7% slower (checkpoints every 4 short tiles stall the producer).
   if (WIDE && persistent && npairs <= kMaxPacedPairs && pacing_enabled(EPI)) {
