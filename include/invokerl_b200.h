@@ -93,7 +93,8 @@ enum {
                                    0 one pair per work unit */
   IKRL_TUNE_PACE = 4,           /* 256x512 kernel: which launches pace their persistent pairs, a
                                    mask: 1 forward, 2 dS recompute, 4 dH (and a one-chunk bf16
-                                   dW), 8 fp32 dW; default 15 (all); 0 none */
+                                   dW), 8 fp32 dW; 15 all; 0 none; -1 auto (default): all but a
+                                   forward with K < 2048 */
   IKRL_TUNE_PACE_KB = 5,        /* K blocks between pacing checkpoints (default 128) */
   IKRL_TUNE_PACE_LAG = 6,       /* checkpoints a pair may lead the slowest by (default 1) */
   IKRL_TUNE_BALANCE_SPLITS = 7, /* K1 dS launches: 1 pick the vocab split count for balance of

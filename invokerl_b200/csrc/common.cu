@@ -29,7 +29,7 @@ constexpr KnobSpec kKnobs[IKRL_TUNE_COUNT] = {
     {1, 0, 1},          // IKRL_TUNE_SKIP_ZERO_ROWS
     {-1, -1, 2},        // IKRL_TUNE_WIDE
     {1, 0, 1},          // IKRL_TUNE_PERSISTENT
-    {15, 0, 15},        // IKRL_TUNE_PACE
+    {-1, -1, 15},       // IKRL_TUNE_PACE
     {128, 1, 1 << 20},  // IKRL_TUNE_PACE_KB
     {1, 0, 64},         // IKRL_TUNE_PACE_LAG
     {1, 0, 1},          // IKRL_TUNE_BALANCE_SPLITS

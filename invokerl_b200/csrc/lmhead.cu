@@ -1199,8 +1199,14 @@ int pace_array(unsigned** out) {
 }
 
 // Pacing of the wide kernel's pairs: IKRL_TUNE_PACE is a mask over the epilogues, bit EPI set =
-// launches with that epilogue are paced (all by default).
-bool pacing_enabled(int epi) { return (tuning(IKRL_TUNE_PACE) >> (epi == EPI_LSE_CACHED ? EPI_LSE : epi)) & 1; }
+// launches with that epilogue are paced.  The default (-1) paces every launch except a forward
+// with K < 2048: there W is a quarter of the 8B head's bytes, the forward reads little DRAM
+// unpaced, and its 16-K-block tiles make the checkpoint waits a larger share.
+bool pacing_enabled(int epi, int K) {
+  int64_t mask = tuning(IKRL_TUNE_PACE);
+  if (mask < 0) mask = K >= 2048 ? 15 : 14;
+  return (mask >> (epi == EPI_LSE_CACHED ? EPI_LSE : epi)) & 1;
+}
 bool persistent_pairs() { return tuning(IKRL_TUNE_PERSISTENT) != 0; }
 
 template <int EPI, bool A_MN, bool B_MN, bool WIDE>
@@ -1224,7 +1230,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
   p.split_tail = (int)tuning(IKRL_TUNE_SPLIT_TAIL);
   // Pacing helps the wide kernel (long tiles, W re-read across pairs); on the 256 x 256 pair
   // kernel at K = 1024 it measured 7% slower (checkpoints every 4 short tiles stall the producer).
-  if (WIDE && persistent && npairs <= kMaxPacedPairs && pacing_enabled(EPI)) {
+  if (WIDE && persistent && npairs <= kMaxPacedPairs && pacing_enabled(EPI, p.K)) {
     int rc = pace_array(&p.lockstep);
     if (rc) return rc;
     IKRL_CUDA(cudaMemsetAsync(p.lockstep, 0, sizeof(unsigned) * (size_t)npairs, s));

@@ -153,7 +153,7 @@ def test_tuning_knobs_range_checks_and_defaults(lib):
     library reads no environment variable."""
     from invokerl_b200 import _native as N
 
-    defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": 15, "pace_kb": 128,
+    defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": -1, "pace_kb": 128,
                 "pace_lag": 1, "balance_splits": 1, "l2_policy": -1, "l2_budget_mb": 0, "loss_kernel": 1,
                 "pace_kb_long": 128, "split_tail": 1}
     assert {k: N.get_tuning(k) for k in N.TUNE} == defaults

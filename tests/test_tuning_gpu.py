@@ -14,7 +14,7 @@ DEV = "cuda"
 
 VARIANTS = (
     [{}]
-    + [{"cta_pairs": 0}, {"skip_zero_rows": 0}, {"persistent": 0}, {"pace": 0}, {"pace": 3}, {"balance_splits": 0}]
+    + [{"cta_pairs": 0}, {"skip_zero_rows": 0}, {"persistent": 0}, {"pace": 0}, {"pace": 3}, {"pace": 15}, {"pace": 14}, {"balance_splits": 0}]
     + [{"wide": v} for v in (0, 1, 2)]
     + [{"pace_kb": v} for v in (1, 7, 256)]
     + [{"pace_kb_long": v} for v in (16, 512)]
