@@ -106,9 +106,10 @@ enum {
   IKRL_TUNE_LOSS_KERNEL = 10,   /* GRPO/DAPO loss: 1 register loads (default); 2 bulk-copy staged;
                                    0 the general clipped-ratio kernel */
   IKRL_TUNE_PACE_KB_LONG = 11,  /* pacing checkpoint spacing of the dW and dH launches (default 128) */
-  IKRL_TUNE_SPLIT_TAIL = 12,    /* 256x512 kernel: 1 the last K blocks of each tile complete the first
-                                   accumulator half before the second, so the epilogue drains it
-                                   under the second half's MMAs (default); 0 halves interleaved */
+  IKRL_TUNE_SPLIT_TAIL = 12,    /* 256x512 kernel: how many of each tile's last K blocks (0-4) run
+                                   first-half-first, so the epilogue drains the first accumulator
+                                   half under the second half's last MMAs; default 4; 0 halves
+                                   interleaved to the end */
   IKRL_TUNE_COUNT = 13
 };
 /* Passed as `value`, restores the knob's default. */

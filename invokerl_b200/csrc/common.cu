@@ -37,7 +37,7 @@ constexpr KnobSpec kKnobs[IKRL_TUNE_COUNT] = {
     {0, 0, 1024},       // IKRL_TUNE_L2_BUDGET_MB
     {1, 0, 2},          // IKRL_TUNE_LOSS_KERNEL
     {128, 1, 1 << 20},  // IKRL_TUNE_PACE_KB_LONG
-    {1, 0, 1},          // IKRL_TUNE_SPLIT_TAIL
+    {4, 0, 4},          // IKRL_TUNE_SPLIT_TAIL
 };
 
 struct Knobs {

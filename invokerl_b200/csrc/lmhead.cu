@@ -78,7 +78,7 @@ struct GemmParams {
   unsigned* lockstep;     // [npairs] tiles started per pair (zeroed per launch), or null: no pacing
   int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
   int pace_kb, pace_lag;  // pacing: K blocks between checkpoints, checkpoints a pair may lead by
-  int split_tail;         // wide kernel: the last K blocks of a tile run first-half-first
+  int split_tail;         // wide kernel: how many of a tile's last K blocks run first-half-first
   int ds_tma;             // DLOGITS in the wide kernel: 1 = stage dS in shared memory, TMA-store it
   // Logit cache (LSE, optional): rows with slot[r] >= 0 store, per 32-column chunk, the bf16
   // numerators 2^(S log2e - m) relative to the chunk maximum m and m itself (log2 units), so the
@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(kWideThreads, 1)
           // The last `tail` K blocks run first-half-first: the first half is final while the
           // second half's last MMAs still run, so the epilogue drains it and releases it for the
           // next tile without idling the tensor pipe.
-          const int tail = p.split_tail ? min(kWideStages, nk - look) : 0;
+          const int tail = min(min(p.split_tail, kWideStages), nk - look);
           for (int kb = look; kb < nk - tail; ++kb) {
             if (!mbar_wait(smem_u32(&full_bar[stage]), phase, abort_v, p.err, kErrTimeoutMma)) { ok = false; break; }
             tc_fence_after();

@@ -155,7 +155,7 @@ def test_tuning_knobs_range_checks_and_defaults(lib):
 
     defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": -1, "pace_kb": 128,
                 "pace_lag": 1, "balance_splits": 1, "l2_policy": -1, "l2_budget_mb": 0, "loss_kernel": 1,
-                "pace_kb_long": 128, "split_tail": 1}
+                "pace_kb_long": 128, "split_tail": 4}
     assert {k: N.get_tuning(k) for k in N.TUNE} == defaults
     prev = N.set_tuning("pace_kb", 7)
     assert prev == 128 and N.get_tuning("pace_kb") == 7
