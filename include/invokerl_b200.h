@@ -110,7 +110,11 @@ enum {
                                    first-half-first, so the epilogue drains the first accumulator
                                    half under the second half's last MMAs; default 4; 0 halves
                                    interleaved to the end */
-  IKRL_TUNE_COUNT = 13
+  IKRL_TUNE_DH_SPLIT_K = 13,    /* K1 backward dH with few row tiles: -1 auto (default: split the
+                                   vocabulary reduction into K ranges summed in a fixed order when
+                                   the 256x512 tiles alone leave pairs idle); 0 or 1 never; n > 1
+                                   n ranges wherever the partial buffer holds them */
+  IKRL_TUNE_COUNT = 14
 };
 /* Passed as `value`, restores the knob's default. */
 #define IKRL_TUNE_DEFAULT (-0x7fffffffffffffffLL - 1)
@@ -348,10 +352,12 @@ IKRL_API int ikrl_lmhead_set_cta_pairs(int32_t enable);
 
 /* The launch plan the K1 calls would use, for inspection and tests; makes no CUDA call.  gemm:
  * 0 the forward over `rows` rows, 1 the dS recompute of a backward chunk of `rows` rows, 2 its
- * dW (fp32 accumulator), 3 its dH.  num_sms: SMs of the GPU (148 on B200; one persistent CTA
- * pair per two).  plan_out[4] = kernel (0 single CTAs 128 x 256, 1 CTA pairs 256 x 256, 2 wide
- * CTA pairs 256 x 512), column tiles, tiles per work unit, work units per row pair.  It follows
- * the same tuning knobs as the launches.  No counterpart in the reference. */
+ * dW (fp32 accumulator), 3 its dH undivided, 4 the K ranges of that dH.  num_sms: SMs of the GPU
+ * (148 on B200; one persistent CTA pair per two).  plan_out[4] = kernel (0 single CTAs 128 x 256,
+ * 1 CTA pairs 256 x 256, 2 wide CTA pairs 256 x 512), column tiles, tiles per work unit, work
+ * units per row pair; for gemm 4, plan_out[0] = the K ranges (1: undivided; more: the 256 x 512
+ * kernel stores fp32 partials that a second kernel sums) and the rest 0.  It follows the same
+ * tuning knobs as the launches.  No counterpart in the reference. */
 IKRL_API int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t num_sms,
                               int32_t* plan_out);
 

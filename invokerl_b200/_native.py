@@ -40,6 +40,7 @@ TUNE = {
     "loss_kernel": 10,
     "pace_kb_long": 11,
     "split_tail": 12,
+    "dh_split_k": 13,
 }
 TUNE_DEFAULT = -(1 << 63)
 LOSS_NSUMS = 16

@@ -38,6 +38,7 @@ constexpr KnobSpec kKnobs[IKRL_TUNE_COUNT] = {
     {1, 0, 2},          // IKRL_TUNE_LOSS_KERNEL
     {128, 1, 1 << 20},  // IKRL_TUNE_PACE_KB_LONG
     {4, 0, 4},          // IKRL_TUNE_SPLIT_TAIL
+    {-1, -1, 16},       // IKRL_TUNE_DH_SPLIT_K
 };
 
 struct Knobs {

@@ -79,6 +79,8 @@ struct GemmParams {
   int64_t id_offset;      // first vocabulary id of W's rows (a vocab shard); 0 for the whole vocabulary
   int pace_kb, pace_lag;  // pacing: K blocks between checkpoints, checkpoints a pair may lead by
   int split_tail;         // wide kernel: how many of a tile's last K blocks run first-half-first
+  int ksplits;            // wide kernel: K ranges per output tile (<= 1: one), each to its own
+  int64_t ks_stride;      //   fp32 partial output, ks_stride elements apart (EPI_F32 only)
   int ds_tma;             // DLOGITS in the wide kernel: 1 = stage dS in shared memory, TMA-store it
   // Logit cache (LSE, optional): rows with slot[r] >= 0 store, per 32-column chunk, the bf16
   // numerators 2^(S log2e - m) relative to the chunk maximum m and m itself (log2 units), so the
@@ -124,7 +126,8 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
                                               int t_end, int warp, int lane, const uint32_t (&acc_full)[2],
                                               const uint32_t (&acc_empty)[2], bool cluster_arrive,
                                               volatile int* abort_v, int tile_base = 0,
-                                              const CUtensorMap* tm_store = nullptr, uint32_t stage_smem = 0) {
+                                              const CUtensorMap* tm_store = nullptr, uint32_t stage_smem = 0,
+                                              int64_t out_off = 0) {
   const int ntiles = t_end - t_begin;
   bool ok = true;
   const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -270,7 +273,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
       }
     } else {  // EPI_F32
       if (row_ok) {
-        float* dst = p.out_f32 + (int64_t)grow * p.ld_f32 + col0;
+        float* dst = p.out_f32 + out_off + (int64_t)grow * p.ld_f32 + col0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           if (4 * k >= nvalid) break;
@@ -302,7 +305,7 @@ __device__ __forceinline__ bool epilogue_role(const GemmParams& p, uint32_t tmem
           const int n0p = (t_begin + j) * TILE_N + (SPLIT ? sg * (TILE_N / 2) + group * kSegCols : c_lo);
           const int ncols = min(kSegCols, p.N - n0p);
           if (ncols > 0)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + (int64_t)grow * p.ld_f32 + n0p),
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.out_f32 + out_off + (int64_t)grow * p.ld_f32 + n0p),
                          "r"((uint32_t)ncols * 4u)
                          : "memory");
         }
@@ -801,8 +804,20 @@ __global__ void __launch_bounds__(kWideThreads, 1)
   const int pair_id = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
   const int m_pairs = (((p.M + BM - 1) / BM) + 1) >> 1;
-  const int nunits = m_pairs * p.splits;
-  const int nk = (p.K + BK - 1) / BK;
+  const int kspl = p.ksplits > 1 ? p.ksplits : 1;
+  const int nunits = m_pairs * p.splits * kspl;
+  const int nk_all = (p.K + BK - 1) / BK;
+  // Work unit u: K range ks (slowest, so the units in flight share it), then the row pair, then
+  // the vocab split (fastest), as without K ranges.
+  auto unit_of = [&](int u, int& mp, int& split, int& ks, int& kb0, int& kb1) {
+    const int per = m_pairs * p.splits;
+    ks = u / per;
+    const int r = u - ks * per;
+    split = r % p.splits;
+    mp = r / p.splits;
+    kb0 = (int)((int64_t)ks * nk_all / kspl);
+    kb1 = (int)((int64_t)(ks + 1) * nk_all / kspl);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWideStages; ++s) {
@@ -841,16 +856,16 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       bool pacing = p.lockstep != nullptr && rank == 0;
-      int jt = 0;
+      int gkb = 0;  // K blocks this pair has loaded
       for (int u = pair_id; u < nunits && ok; u += npairs) {
-        const int split = u % p.splits;
-        const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
+        int mp, split, ks, kb0, kb1;
+        unit_of(u, mp, split, ks, kb0, kb1);
+        const int m0 = (2 * mp + (int)rank) * BM;
         const int t_begin = split * p.tiles_per_split;
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
-        for (int t = t_begin; t < t_end && ok; ++t, ++jt) {
-          for (int kb = 0; kb < nk; ++kb) {
+        for (int t = t_begin; t < t_end && ok; ++t) {
+          for (int kb = kb0; kb < kb1; ++kb, ++gkb) {
             // pacing checkpoint every pace_kb K blocks of this pair's work
-            const int gkb = jt * nk + kb;
             if (p.lockstep != nullptr && rank == 0 && gkb % p.pace_kb == 0)
               pace_checkpoint(p.lockstep, pair_id, npairs, gkb / p.pace_kb, p.pace_lag, pacing);
             if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, abort_v, p.err, kErrTimeoutProducer)) {
@@ -906,7 +921,9 @@ __global__ void __launch_bounds__(kWideThreads, 1)
       bool ok = true;
       int j = 0;
       for (int u = pair_id; u < nunits && ok; u += npairs) {
-        const int split = u % p.splits;
+        int mp, split, ks, kb0, kb1;
+        unit_of(u, mp, split, ks, kb0, kb1);
+        const int nk = kb1 - kb0;  // K blocks of this unit; kb below counts from its first
         const int t_begin = split * p.tiles_per_split;
         const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
         // MMAs of one K block into accumulator half h (TMEM columns [256h, 256h + 256)).
@@ -1012,12 +1029,13 @@ __global__ void __launch_bounds__(kWideThreads, 1)
                                : 0u;
     int jb = 0;
     for (int u = pair_id; u < nunits; u += npairs) {
-      const int split = u % p.splits;
-      const int m0 = (2 * (u / p.splits) + (int)rank) * BM;
+      int mp, split, ks, kb0, kb1;
+      unit_of(u, mp, split, ks, kb0, kb1);
+      const int m0 = (2 * mp + (int)rank) * BM;
       const int t_begin = split * p.tiles_per_split;
       const int t_end = min(t_begin + p.tiles_per_split, p.n_tiles);
       if (!epilogue_role<EPI, WN, 1, kWideGroups, true>(p, tmem_base, m0, split, t_begin, t_end, warp, lane, af, ae,
-                                                        true, abort_v, jb, &tmC, stage))
+                                                        true, abort_v, jb, &tmC, stage, (int64_t)ks * p.ks_stride))
         break;
       jb += t_end - t_begin;
     }
@@ -1218,7 +1236,10 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorM
   const uint32_t smem_bytes = WIDE ? (p.ds_tma ? kWideDsSmemBytes : kWideSmemBytes) : kPairSmemBytes;
   IKRL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes));
   IKRL_REQUIRE(p.split_major == 1, IKRL_ERR_UNSUPPORTED, "pair kernel needs a split-major grid");
-  const int64_t nunits = (int64_t)((m_tiles + 1) / 2) * p.splits;
+  IKRL_REQUIRE(WIDE || p.ksplits <= 1, IKRL_ERR_UNSUPPORTED, "K ranges need the 256x512 kernel");
+  IKRL_REQUIRE(p.ksplits <= 1 || (EPI == EPI_F32 && p.f32_mode == F32_STORE), IKRL_ERR_UNSUPPORTED,
+               "K ranges need fp32 partial stores");
+  const int64_t nunits = (int64_t)((m_tiles + 1) / 2) * p.splits * std::max(1, p.ksplits);
   IKRL_REQUIRE(nunits <= 0x3fffffffLL, IKRL_ERR_UNSUPPORTED, "too many work units (%lld)", (long long)nunits);
   int dev = 0, nsm = kNumSMs;
   IKRL_CUDA(cudaGetDevice(&dev));
@@ -1361,6 +1382,62 @@ K1Plan plan_k1(int epi, int64_t m_tiles, int N, int K, int splits_hint, int nsm)
   return pl;
 }
 
+// A chunk's dH may be split into at most kMaxDhSplitK K ranges, whose fp32 partials take at most
+// kSplitKPartElems elements (512 MB) of the backward workspace.
+constexpr int kMaxDhSplitK = 16;
+constexpr int64_t kSplitKPartElems = 128ll << 20;
+
+// K ranges for a chunk's dH = dS W.  Every 256 x 512 dH tile reduces over the whole vocabulary, so
+// few row tiles leave few units: the 0.6B head's 10,066 active rows are 40 row pairs x 2 column
+// tiles = 80 units for 74 pairs, two rounds where the mean is 1.08.  With ks K ranges there are
+// ks times the units, each storing an fp32 partial; a second kernel sums the partials in a fixed
+// order.  ks minimises the busiest pair's work plus the partials' HBM write and read (in units of
+// one full-vocabulary 256 x 256 tile), and is taken when that beats the undivided choice of
+// plan_k1 (256 x 512, or 256 x 256 pairs) by 5%.  1 = no split.
+int dh_split_k(int64_t m_tiles, int H, int V, int64_t rows, int64_t part_elems, int nsm) {
+  const int64_t forced = tuning(IKRL_TUNE_DH_SPLIT_K);
+  if (forced == 0 || forced == 1) return 1;
+  if (!use_pairs() || !use_wide(V) || !persistent_pairs()) return 1;
+  const int64_t nk = cdiv64(V, BK);
+  auto fits = [&](int64_t ks) { return ks * rows * H <= part_elems && nk / ks >= 32; };
+  if (forced > 1) {
+    int64_t ks = std::min<int64_t>(forced, kMaxDhSplitK);
+    while (ks > 1 && !fits(ks)) --ks;
+    return (int)ks;
+  }
+  const int64_t P = std::max(1, nsm / 2);
+  const int64_t m_pairs = (m_tiles + 1) / 2;
+  const int64_t U = m_pairs * cdiv64(H, WN);
+  if (U >= 2 * P) return 1;
+  const double tile_s = 2.0 * BN * BN * (double)V / (1.4e15 / (double)P);  // one tile on one pair
+  const double elem_s = 8.0 / 6.0e12;                                       // fp32 written and read
+  auto cost = [&](int64_t ks) {
+    return 2.0 * (double)cdiv64(U * ks, P) / (double)ks + (double)(ks * rows * H) * elem_s / tile_s;
+  };
+  const double undivided = std::min(2.0 * (double)cdiv64(U, P),
+                                    1.13 * (double)pair_makespan(m_pairs, (int)cdiv64(H, BN), 1, P));
+  int64_t best_ks = 1;
+  double best = undivided;
+  for (int64_t ks = 2; ks <= kMaxDhSplitK && fits(ks); ++ks) {
+    const double c = cost(ks);
+    if (c < best) { best = c; best_ks = ks; }
+  }
+  return best < 0.95 * undivided ? (int)best_ks : 1;
+}
+
+// dH rows of a split dH: out = bf16(part[0] + part[1] + ... + part[ks-1]), summed in that order.
+// n4: float4 groups of one partial (rows * H / 4); the partials are n4 groups apart.
+__global__ void splitk_sum_kernel(const float4* __restrict__ part, int64_t n4, int ks, uint2* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = part[i];
+    for (int s = 1; s < ks; ++s) {
+      const float4 b = part[(int64_t)s * n4 + i];
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    out[i] = make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w));
+  }
+}
+
 // Launch one K1 GEMM with the kernel plan_k1 selects, filling in the tile ranges; p.splits holds
 // the count actually used.
 // c_store: tensor map of the dS chunk for the wide kernel's TMA stores (DLOGITS), or null.
@@ -1440,7 +1517,8 @@ struct BwdLayout {
   int64_t chunk, lds;
   bool need_dw32;
   // active-row compaction (rows whose upstream gradient is exactly zero are skipped)
-  size_t cnt_off, nact_off, idx_off, pos_off, idc_off, lsec_off, gc_off, hc_off;
+  size_t cnt_off, nact_off, idx_off, pos_off, idc_off, lsec_off, gc_off, hc_off, part_off;
+  int64_t part_elems;
   int cblocks;
 };
 
@@ -1470,6 +1548,9 @@ BwdLayout bwd_layout(int64_t N, int H, int V, int64_t chunk_rows, int dweight_dt
   L.lsec_off = o;  o = al(o + (size_t)N * 4);
   L.gc_off = o;    o = al(o + (size_t)N * 4);
   L.hc_off = o;    o = al(o + (size_t)N * H * 2);
+  // fp32 partials of a dH split into K ranges (few row tiles only; see dh_split_k)
+  L.part_elems = std::min<int64_t>(kSplitKPartElems, (int64_t)kMaxDhSplitK * std::min<int64_t>(N, L.chunk) * H);
+  L.part_off = o;  o = al(o + (size_t)L.part_elems * 4);
   L.total = o;
   return L;
 }
@@ -1886,6 +1967,12 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
   float* dw32 = L.need_dw32 ? reinterpret_cast<float*>(w + L.dw_off) : nullptr;
   IKRL_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
   const int n_vt = (int)cdiv64(V, BN);
+  int nsm = kNumSMs;
+  {
+    int dev = 0;
+    IKRL_CUDA(cudaGetDevice(&dev));
+    IKRL_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+  }
 
   // Rows the GEMMs run on: all N, or the compacted active rows.
   const uint16_t* hsrc = reinterpret_cast<const uint16_t*>(hidden);
@@ -2011,15 +2098,28 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
         if ((rc = launch_k1<EPI_F32, true, true>(ta, tb, ta, tb, p, v_tiles, 0, s))) return rc;
       }
     }
-    // 3) dH[chunk] = dS W
+    // 3) dH[chunk] = dS W, whole or as K-range partials summed afterwards
     if (dhidden) {
       CUtensorMap ta;
       if ((rc = make_tmap(&ta, dS, V, rows, L.lds, BM, "dS"))) return rc;
       GemmParams p{};
       p.M = (int)rows; p.N = H; p.K = V;
-      p.out_bf16 = dh_out + c0 * H; p.ld_bf16 = H;
       p.err = err;
-      if ((rc = launch_k1<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, 0, s))) return rc;
+      const int ks = dh_split_k(m_tiles, H, V, rows, L.part_elems, nsm);
+      if (ks > 1) {
+        float* part = reinterpret_cast<float*>(w + L.part_off);
+        p.out_f32 = part; p.ld_f32 = H; p.f32_mode = F32_STORE;
+        p.ksplits = ks; p.ks_stride = rows * H;
+        if ((rc = launch_k1<EPI_F32, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, 0, s))) return rc;
+        const int64_t n4 = rows * H / 4;
+        const int gb = (int)std::min<int64_t>(cdiv64(n4, 256), 148ll * 8);
+        splitk_sum_kernel<<<gb, 256, 0, s>>>(reinterpret_cast<const float4*>(part), n4, ks,
+                                             reinterpret_cast<uint2*>(dh_out + c0 * H));
+        if ((rc = check_launch("splitk_sum_kernel"))) return rc;
+      } else {
+        p.out_bf16 = dh_out + c0 * H; p.ld_bf16 = H;
+        if ((rc = launch_k1<EPI_STORE_BF16, false, true>(ta, t_w_mn, ta, t_w_mn, p, m_tiles, 0, s))) return rc;
+      }
     }
   }
   if (pos != nullptr) {
@@ -2157,7 +2257,7 @@ int ikrl_lmhead_set_cta_pairs(int32_t enable) {
 
 int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t num_sms, int32_t* plan_out) {
   clear_error();
-  IKRL_REQUIRE(gemm >= 0 && gemm <= 3, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_plan: gemm %d not in 0..3", gemm);
+  IKRL_REQUIRE(gemm >= 0 && gemm <= 4, IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_plan: gemm %d not in 0..4", gemm);
   IKRL_REQUIRE(rows > 0 && rows <= (int64_t)65535 * BM && H > 0 && V > 0 && num_sms >= 2 && plan_out,
                IKRL_ERR_INVALID_ARGUMENT, "ikrl_lmhead_plan: bad arguments");
   const int64_t row_tiles = cdiv64(rows, BM);
@@ -2168,8 +2268,14 @@ int ikrl_lmhead_plan(int32_t gemm, int64_t rows, int32_t H, int32_t V, int32_t n
     pl = plan_k1(EPI_DLOGITS, row_tiles, V, H, choose_splits(row_tiles, (int)cdiv64(V, BN), H), num_sms);
   else if (gemm == 2)  // dW += dS^T h over the chunk, fp32 accumulator
     pl = plan_k1(EPI_F32, cdiv64(V, BM), H, (int)rows, 0, num_sms);
-  else  // dH = dS W of the chunk
+  else if (gemm == 3)  // dH = dS W of the chunk, undivided
     pl = plan_k1(EPI_STORE_BF16, row_tiles, H, V, 0, num_sms);
+  if (gemm == 4) {  // K ranges of that dH (1 = undivided), with the partial buffer of such a chunk
+    const int64_t part = std::min<int64_t>(kSplitKPartElems, (int64_t)kMaxDhSplitK * rows * H);
+    plan_out[0] = dh_split_k(row_tiles, H, V, rows, part, num_sms);
+    plan_out[1] = plan_out[2] = plan_out[3] = 0;
+    return IKRL_OK;
+  }
   plan_out[0] = pl.kind;
   plan_out[1] = pl.n_tiles;
   plan_out[2] = pl.tiles_per_split;

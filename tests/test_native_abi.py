@@ -119,7 +119,11 @@ def _plan(gemm, rows, H, V=151936, nsm=148):
     (3, 28160, 4096, (2, 8, 1, 8)),       # 8B dH stays wide
     (0, 131072, 1024, (2, 297, 149, 2)),  # 0.6B forward: wide from K = 1024
     (1, 10092, 1024, (2, 297, 33, 9)),    # 0.6B dS: 4 splits -> 9
-    (3, 10092, 1024, (1, 4, 1, 4)),       # 0.6B dH: 256 x 256 pairs (80 wide units would run 2 rounds)
+    (3, 10092, 1024, (1, 4, 1, 4)),       # 0.6B dH undivided: 256 x 256 pairs (80 wide units would run 2 rounds)
+    (4, 10092, 1024, (12, 0, 0, 0)),      # ... and split: 12 K ranges, 960 units in 13 rounds
+    (4, 3456, 4096, (7, 0, 0, 0)),        # 14 row pairs x 8: 7 ranges (the partials cap the count at 9)
+    (4, 28160, 4096, (1, 0, 0, 0)),       # 8B full chunk: 880 units, no split
+    (4, 8700, 4096, (1, 0, 0, 0)),        # 8B last chunk: 272 units, no split
     (1, 256, 64, (1, 594, 3, 198)),       # K = 64: 256 x 256 pairs
 ])
 def test_lmhead_launch_plan(lib, gemm, rows, H, want):
@@ -146,6 +150,12 @@ def test_lmhead_launch_plan_follows_the_knobs(lib):
         assert _plan(3, 10092, 1024) == (2, 2, 1, 2)
     with N.tuning(l2_budget_mb=8):  # less L2 for resident rows -> more vocabulary splits
         assert _plan(0, 524288, 4096)[3] > 4
+    with N.tuning(dh_split_k=0):
+        assert _plan(4, 10092, 1024)[0] == 1
+    with N.tuning(dh_split_k=3):  # forced, wherever the partials fit
+        assert _plan(4, 28160, 4096)[0] == 1 and _plan(4, 3456, 4096)[0] == 3
+    with N.tuning(wide=0):
+        assert _plan(4, 10092, 1024)[0] == 1
 
 
 def test_tuning_knobs_range_checks_and_defaults(lib):
@@ -155,7 +165,7 @@ def test_tuning_knobs_range_checks_and_defaults(lib):
 
     defaults = {"cta_pairs": 1, "skip_zero_rows": 1, "wide": -1, "persistent": 1, "pace": -1, "pace_kb": 128,
                 "pace_lag": 1, "balance_splits": 1, "l2_policy": -1, "l2_budget_mb": 0, "loss_kernel": 1,
-                "pace_kb_long": 128, "split_tail": 4}
+                "pace_kb_long": 128, "split_tail": 4, "dh_split_k": -1}
     assert {k: N.get_tuning(k) for k in N.TUNE} == defaults
     prev = N.set_tuning("pace_kb", 7)
     assert prev == 128 and N.get_tuning("pace_kb") == 7
@@ -183,7 +193,7 @@ def test_lmhead_launch_plan_rejects_bad_arguments(lib):
     from invokerl_b200 import _native as N
 
     with pytest.raises(N.IkrlError, match="gemm"):
-        _plan(4, 100, 64)
+        _plan(5, 100, 64)
     with pytest.raises(N.IkrlError, match="bad arguments"):
         _plan(0, 0, 64)
 

@@ -19,6 +19,7 @@ VARIANTS = (
     + [{"pace_kb": v} for v in (1, 7, 256)]
     + [{"pace_kb_long": v} for v in (16, 512)]
     + [{"split_tail": v} for v in (0, 1, 2)]
+    + [{"dh_split_k": v} for v in (0, 2, 3, 16)]
     + [{"pace_lag": v} for v in (0, 2, 5)]
     + [{"l2_policy": 10 * a + b} for a in range(3) for b in range(3)]
     + [{"l2_budget_mb": v} for v in (1, 8, 200)]
