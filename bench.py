@@ -167,6 +167,46 @@ def batch_bytes(b) -> int:
     return sum(v.numel() * v.element_size() for v in vars(b).values() if isinstance(v, torch.Tensor))
 
 
+class Prefetch:
+    """Host-to-device input copies of end-to-end steps, issued one step ahead on a copy stream
+    into two sets of device buffers, as a pinned-memory data loader does.  Every step's copies
+    lie inside the timed region: step 0's are issued after the start event, each step's compute
+    waits for its own copies, and step i+1's are issued before step i computes."""
+
+    serial = False  # --e2e-serial: copy each step's inputs in line with the step instead
+
+    def __init__(self, host: dict, device):
+        self.host, self.device = host, device
+        self.bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()}
+                     for _ in range(2)]
+        self.stream = torch.cuda.Stream(device)
+        self.done = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def _issue(self, i):
+        s = self.stream if not Prefetch.serial else torch.cuda.current_stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))  # after the start event / the buffer's last user
+        with torch.cuda.stream(s):
+            for k, v in self.host.items():
+                self.bufs[i % 2][k].copy_(v, non_blocking=True)
+            self.done[i % 2].record(s)
+
+    def get(self, i: int, n: int) -> dict:
+        """Device inputs of step i of n (steps run in order; the host has finished step i-1)."""
+        if i == 0 or Prefetch.serial:
+            self._issue(i)
+        torch.cuda.current_stream(self.device).wait_event(self.done[i % 2])
+        if i + 1 < n and not Prefetch.serial:
+            self._issue(i + 1)
+        return self.bufs[i % 2]
+
+
+def batch_from(hb, d: dict):
+    """RolloutBatch with the tensor fields of host batch `hb` taken from the device buffers `d`."""
+    from invokerl_b200.algorithms import RolloutBatch
+
+    return RolloutBatch(**{k: d.get(k, v) for k, v in vars(hb).items() if k != "extras"}, extras={})
+
+
 _REF_PKG: list = []
 
 
@@ -350,13 +390,17 @@ class LMHeadGRPO:
         hb = host_batch(self.local)
         h2d = host_hidden.numel() * 2 + batch_bytes(hb)
         d2h = 4 + 4 * 12
+        pf = Prefetch({"hidden": host_hidden, **{k: v for k, v in vars(hb).items() if isinstance(v, torch.Tensor)}},
+                      self.device)
 
-        def one():
-            hid = host_hidden.to(self.device, non_blocking=True).requires_grad_(True)
-            b = to_device_batch(hb, self.device)
+        def one(i=0, n=1):
+            d = pf.get(i, n)
+            hid = d["hidden"].detach().requires_grad_(True)
+            b = batch_from(hb, d)
             self.weight.grad = None
             return self._step(b, hid, b.token_ids.reshape(-1))
 
+        one.pipelined = True
         return one, h2d, d2h
 
     def cpu_sample(self, rows, steps):
@@ -951,16 +995,24 @@ class Timed:
         self.steps = steps
 
 
+def input_copies(one) -> str:
+    if getattr(one, "pipelined", False) and not Prefetch.serial:
+        return "one step ahead on a copy stream (two device buffer sets)"
+    return "in line with each step"
+
+
 def time_e2e(one, n, world, device) -> float:
-    """ms for n end-to-end steps (max over ranks), after one untimed step."""
-    one()
+    """ms for n end-to-end steps (max over ranks), after one untimed step.  A step function marked
+    `pipelined` takes (step index, steps) and copies its inputs through a Prefetch."""
+    pipelined = getattr(one, "pipelined", False)
+    one(0, 1) if pipelined else one()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(n):
-        one()
+    for i in range(n):
+        one(i, n) if pipelined else one()
     e.record()
     torch.cuda.synchronize()
     te = torch.tensor([s.elapsed_time(e)], dtype=torch.float64, device=device)
@@ -1020,10 +1072,10 @@ def run_native(args, key, rank, world, device, steps, warmup, cpu_baseline=True)
         e2e = None
         if not args.no_e2e:
             one, h2d, d2h = wl.e2e()
-            n = max(1, min(steps, 3))
+            n = max(1, min(steps, 5))
             te = time_e2e(one, n, world, device)
             e2e = {"value": wl.tokens_per_step() * n / (te / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-                   "d2h_bytes_per_step": int(d2h), "steps": n}
+                   "d2h_bytes_per_step": int(d2h), "steps": n, "input_copies": input_copies(one)}
     finally:
         for name, fn in saved.items():
             setattr(ops, name, fn)
@@ -1150,11 +1202,16 @@ def ref_gpu_lmhead(key, args, device):
         hidden.grad = None
         return run(hidden, rb)
 
-    def e2e():
-        h = host_hidden.to(device, non_blocking=True).requires_grad_(True)
-        b = ref_batch_of(to_device_batch(hb, device))
+    pf = Prefetch({"hidden": host_hidden, **{k: v for k, v in vars(hb).items() if isinstance(v, torch.Tensor)}},
+                  device)
+
+    def e2e(i=0, n=1):
+        d = pf.get(i, n)
+        h = d["hidden"].detach().requires_grad_(True)
+        b = ref_batch_of(batch_from(hb, d))
         return float(run(h, b).detach())  # the reference reads its metrics with .item() as well
 
+    e2e.pipelined = True
     return dict(step=step, e2e=e2e, tokens=B * T, h2d=host_hidden.numel() * 2 + batch_bytes(hb), d2h=4,
                 workload=LMHeadGRPO.PRESETS[key]["name"] + ", invokerl's own chunked F.linear + cross_entropy "
                 "path and GRPO on the same GPU")
@@ -1251,12 +1308,12 @@ def reference_gpu_line(key, args, device, steps, warmup) -> dict:
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = s.elapsed_time(e) / steps
-    ne = max(1, min(steps, 3))
+    ne = max(1, min(steps, 5))
     te = time_e2e(leg["e2e"], ne, 1, device)
     out = {"impl": "reference-gpu", "metric": METRIC, "value": leg["tokens"] / (ms / 1e3), "unit": UNIT,
            "ms_per_step": ms, "steps": steps, "warmup": warmup, "same_config": True,
            "e2e": {"value": leg["tokens"] * ne / (te / 1e3), "unit": UNIT, "h2d_bytes_per_step": int(leg["h2d"]),
-                   "d2h_bytes_per_step": int(leg["d2h"]), "steps": ne},
+                   "d2h_bytes_per_step": int(leg["d2h"]), "steps": ne, "input_copies": input_copies(leg["e2e"])},
            "clocks": clocks, "config": {"workload": leg["workload"]},
            "peak_mem_gb": torch.cuda.max_memory_allocated(device) / 1e9}
     del leg
@@ -1377,6 +1434,8 @@ def main() -> int:
     ap.add_argument("--rows", type=int, default=0, help="override the rows of the logits workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-serial", action="store_true",
+                    help="copy each e2e step's inputs in line with the step instead of one step ahead")
     ap.add_argument("--no-secondary", action="store_true",
                     help="only the headline line: no reference_gpu leg and no secondary workloads")
     ap.add_argument("--fsdp", action="store_true",
@@ -1390,6 +1449,7 @@ def main() -> int:
     ap.add_argument("--logit-cache", choices=["auto", "off"], default="auto",
                     help="the K1 logit cache policy (off: the backward recomputes every active row's logits)")
     args = ap.parse_args()
+    Prefetch.serial = args.e2e_serial
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
