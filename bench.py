@@ -129,6 +129,7 @@ class EventTimer:
 
     def __init__(self):
         self.pairs: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+        self.names: list[str] = []
         self.active = False
 
     def wrap(self, fn):
@@ -140,12 +141,19 @@ class EventTimer:
             out = fn(*a, **k)
             e.record()
             self.pairs.append((s, e))
+            self.names.append(fn.__name__)
             return out
 
         return inner
 
     def total_ms(self) -> float:
         return sum(s.elapsed_time(e) for s, e in self.pairs)
+
+    def by_name_ms(self) -> dict:
+        out: dict = {}
+        for n, (s, e) in zip(self.names, self.pairs):
+            out[n] = out.get(n, 0.0) + s.elapsed_time(e)
+        return out
 
 
 def to_device_batch(b, device):
@@ -991,6 +999,8 @@ class Timed:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         self.ms, self.kms = float(t[0]), float(t[1])
         self.has_kernel_time = timer is not None and bool(timer.pairs)
+        # this rank's CUDA-event time of each timed function, per step
+        self.kms_by_fn = {k: v / steps for k, v in timer.by_name_ms().items()} if self.has_kernel_time else {}
         self.out = out
         self.steps = steps
 
@@ -1103,6 +1113,7 @@ def run_native(args, key, rank, world, device, steps, warmup, cpu_baseline=True)
                      if isinstance(wl, E2EGRPO) else wl.roofline(kms / steps, peaks, peak_src)),
         "e2e": e2e,
         "gpu_launches": tm.launches,
+        "kernel_ms_per_step": {k: round(v, 3) for k, v in tm.kms_by_fn.items()} or None,
         "clocks": tm.clocks,
         "loss": loss,
     }
