@@ -279,7 +279,10 @@ IKRL_API int ikrl_lmhead_logprob_fwd(const void* hidden, const void* weight, con
  * [V, H] (nullable; IKRL_DTYPE_BF16 or IKRL_DTYPE_F32, the latter optionally accumulated into).
  * Rows are processed in chunks of `chunk_rows` (<= 0: all rows at once); the workspace holds one
  * chunk of bf16 dlogits [chunk, round_up(V, 64)] plus, for a bf16 dweight over several chunks,
- * an fp32 [V, H] accumulator, plus the row-compaction buffers below.
+ * an fp32 [V, H] accumulator, plus the row-compaction buffers below, plus fp32 partials for a
+ * dhidden split into K ranges (min(128M, 16 * min(N, chunk) * H) elements; see
+ * IKRL_TUNE_DH_SPLIT_K).  A chunk's dhidden is then the fixed-order sum of its partials, so its
+ * rounding depends on the number of ranges, which depends on the chunk's active rows.
  * Rows whose dlogp is exactly zero (tokens outside the loss mask) and ignore_index rows add
  * exact zeros to both gradients; they are left out of the GEMMs: the other rows are gathered
  * in order into a dense block (a copy of their hidden rows, [N, H] bf16 at most), and dhidden
