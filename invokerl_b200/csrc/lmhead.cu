@@ -1766,8 +1766,10 @@ __global__ void __launch_bounds__(kCompactThreads) cache_slot_kernel(const uint8
 
 // dS of cached rows: for chunk row k (compacted row c0 + k, original row idx[c0 + k]) and column
 // j < V, dS = g * ([j == t] - q * 2^(m - lse log2e)), with q the cached bf16 numerator and m its
-// chunk maximum.  Block row y handles chunk rows y, y + gridDim.y, ...; eight columns per thread
-// (16-byte loads and stores); V must be a multiple of 8.
+// chunk maximum.  Block row y handles chunk rows y, y + gridDim.y, ...; a thread takes
+// kDsUnroll groups of eight columns, 256 groups apart, and issues their 16-byte loads before any
+// store; V must be a multiple of 8.
+constexpr int kDsUnroll = 4;
 __global__ void __launch_bounds__(256) ds_from_cache_kernel(
     const uint16_t* __restrict__ cache_q, const float* __restrict__ cache_m, int64_t ld_cache, int n_mchunks,
     const int* __restrict__ slot, const int* __restrict__ idx, const int64_t* __restrict__ ids_c,
@@ -1783,20 +1785,35 @@ __global__ void __launch_bounds__(256) ds_from_cache_kernel(
     const uint16_t* qrow = cache_q + sl * ld_cache;
     const float* mrow = cache_m + sl * n_mchunks;
     uint16_t* drow = ds + k * ld_ds;
-    for (int jv = blockIdx.x * blockDim.x + threadIdx.x; jv < vec; jv += gridDim.x * blockDim.x) {
-      const int j0 = jv << 3;
-      const uint4 qv = *reinterpret_cast<const uint4*>(qrow + j0);
-      const float sc = fast_exp2(mrow[j0 >> 5] - lse2);
-      const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-      uint32_t o[4];
+    for (int jb = blockIdx.x * blockDim.x * kDsUnroll + threadIdx.x; jb < vec;
+         jb += gridDim.x * blockDim.x * kDsUnroll) {
+      uint4 qv[kDsUnroll];
+      float mv[kDsUnroll];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p0 = bf16lo(w[e]) * sc, p1 = bf16hi(w[e]) * sc;
-        const float d0 = gv * (((int64_t)(j0 + 2 * e) == t ? 1.f : 0.f) - p0);
-        const float d1 = gv * (((int64_t)(j0 + 2 * e + 1) == t ? 1.f : 0.f) - p1);
-        o[e] = pack_bf16x2(d0, d1);
+      for (int u = 0; u < kDsUnroll; ++u) {
+        const int jv = jb + u * (int)blockDim.x;
+        if (jv < vec) {
+          qv[u] = *reinterpret_cast<const uint4*>(qrow + (jv << 3));
+          mv[u] = mrow[jv >> 2];
+        }
       }
-      *reinterpret_cast<uint4*>(drow + j0) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+      for (int u = 0; u < kDsUnroll; ++u) {
+        const int jv = jb + u * (int)blockDim.x;
+        if (jv >= vec) break;
+        const int j0 = jv << 3;
+        const float sc = fast_exp2(mv[u] - lse2);
+        const uint32_t w[4] = {qv[u].x, qv[u].y, qv[u].z, qv[u].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = bf16lo(w[e]) * sc, p1 = bf16hi(w[e]) * sc;
+          const float d0 = gv * (((int64_t)(j0 + 2 * e) == t ? 1.f : 0.f) - p0);
+          const float d1 = gv * (((int64_t)(j0 + 2 * e + 1) == t ? 1.f : 0.f) - p1);
+          o[e] = pack_bf16x2(d0, d1);
+        }
+        *reinterpret_cast<uint4*>(drow + j0) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
   }
 }
@@ -2055,7 +2072,8 @@ static int lmhead_bwd_impl(const char* what, const void* hidden, const void* wei
     const uint16_t* hc = hsrc + c0 * H;
     // 1) dS = g * (onehot - softmax(h W^T)) for this chunk: from the logit cache, or recomputed
     if (chunks[ci].cached) {
-      const dim3 grid((unsigned)std::max<int64_t>(1, cdiv64(V / 8, 256)), (unsigned)std::min<int64_t>(rows, 65535));
+      const dim3 grid((unsigned)std::max<int64_t>(1, cdiv64(V / 8, 256 * kDsUnroll)),
+                      (unsigned)std::min<int64_t>(rows, 65535));
       ds_from_cache_kernel<<<grid, 256, 0, s>>>(cache_q, cache_m, L.lds, (int)cdiv64(V, 32), cache_slot, idx_c,
                                                 idsrc, lsesrc, gsrc, c0, rows, V, vocab_start, dS, L.lds);
       if ((rc = check_launch("ds_from_cache_kernel"))) return rc;
